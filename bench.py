@@ -1,0 +1,403 @@
+"""Benchmark of the PPO learner step (boonta PPO.update) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl native|reference]
+
+Metric: learner env-steps/s = world * T * N / t_update (the reference's `update/SPS`,
+hangar/scripts/benchmark_boonta.py:154-177, 214), weak scaling (N envs per GPU fixed).
+One "step" = one full learner update: bootstrap value, GAE, E x M minibatch
+forward/loss/backward/(all-reduce)/clip+Adam. Inputs are seeded synthetic rollouts of the
+workload's shapes, resident in HBM when the timed region starts (`value`); `e2e` repeats
+the measurement through the public API with the rollout copied from pinned host memory
+and the statistics read back every step. Every timed rollout and its permutations are
+larger than L2 (126 MB), and each step uses a different permutation.
+
+`--impl reference` times the reference's algorithm on the host cores. boonta's own JAX
+path cannot run here (no jax/flax/optax in the image), so it times the NumPy port of it
+(oracle/, the CPU restatement the parity tests check against) on a bounded sample of the
+same workload and scales it to one full update.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from boonta_b200 import configs  # noqa: E402
+from boonta_b200.spec import Conv3x3, Dense, init_params, param_layout  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ---- algorithmic work per minibatch ------------------------------------------------------
+def gemm_flops(w) -> dict:
+    """FLOPs of one minibatch's GEMMs by class (forward, dX, dW), dense count, incl. heads."""
+    net = w.network
+    rows = w.minibatch_size
+    f = {"gemm_fwd": 0.0, "gemm_dx": 0.0, "gemm_dw": 0.0}
+    for tower in net.towers():
+        dim = net.obs_dim
+        for i, layer in enumerate(tower):
+            if isinstance(layer, Conv3x3):
+                m = rows * layer.height * layer.width
+                k, n = 9 * layer.in_channels + 1, layer.features
+                out = layer.height * layer.width * layer.features
+            else:
+                m, k, n = rows, dim + 1, layer.features
+                out = layer.features
+            f["gemm_fwd"] += 2.0 * m * k * n
+            f["gemm_dw"] += 2.0 * m * k * n
+            if i > 0:
+                f["gemm_dx"] += 2.0 * m * (k - 1) * n
+            dim = out
+    # head weight gradients ([F+1, A] and [F+1, 1]) run as dW GEMMs
+    lay = param_layout(net)
+    fpi = lay["actor_head/kernel"].shape[0]
+    fv = lay["critic_head/kernel"].shape[0]
+    f["gemm_dw"] += 2.0 * rows * ((fpi + 1) * net.action_dim + (fv + 1))
+    return f
+
+
+def gae_bytes(w) -> float:
+    return 18.0 * w.batch_size + 4.0 * w.num_envs
+
+
+# ---- synthetic inputs on the device ----------------------------------------------------------
+def device_rollout(w, seed: int, device):
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    t, n, d, a = w.num_steps, w.num_envs, w.network.obs_dim, w.network.action_dim
+
+    def obs(shape):
+        if w.obs_kind == "bernoulli":
+            return (torch.rand(shape, generator=g, device=device) < 1 - w.obs_sparsity).float()
+        if w.obs_kind == "sparse_uniform":
+            x = torch.rand(shape, generator=g, device=device)
+            keep = torch.rand(shape, generator=g, device=device) >= w.obs_sparsity
+            return torch.where(keep, x, torch.zeros((), device=device))
+        return torch.randn(shape, generator=g, device=device)
+
+    r = {"obs": obs((t, n, d)), "bootstrap_obs": obs((n, d))}
+    if w.network.head == "gaussian":
+        r["action"] = torch.randn((t, n, a), generator=g, device=device)
+        r["log_prob"] = (-0.5 * r["action"] ** 2 - 0.9189385).sum(-1) + 0.05 * torch.randn(
+            (t, n), generator=g, device=device)
+    else:
+        r["action"] = torch.randint(0, a, (t, n), generator=g, device=device, dtype=torch.int32)
+        r["log_prob"] = float(np.log(1.0 / a)) + 0.05 * torch.randn((t, n), generator=g, device=device)
+    if w.reward == "ones":
+        r["reward"] = torch.ones((t, n), device=device)
+    elif w.reward == "bernoulli":
+        r["reward"] = (torch.rand((t, n), generator=g, device=device) < w.reward_p).float()
+    else:
+        r["reward"] = w.reward_scale * torch.randn((t, n), generator=g, device=device)
+    r["terminated"] = (torch.rand((t, n), generator=g, device=device) < w.done_p).to(torch.uint8)
+    r["truncated"] = torch.zeros((t, n), dtype=torch.uint8, device=device)
+    r["value"] = torch.randn((t, n), generator=g, device=device)
+    return {k: v.contiguous() for k, v in r.items()}
+
+
+def device_perms(w, world: int, count: int, seed: int, device):
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    size = w.batch_size * world
+    return [torch.stack([torch.randperm(size, generator=g, device=device, dtype=torch.int32)
+                         for _ in range(w.ppo.update_epochs)]) for _ in range(count)]
+
+
+# ---- clocks ---------------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [line for line in out.splitlines() if line.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- CPU baseline (the reference's algorithm on the host) -----------------------------------
+def cpu_baseline(w, budget_s: float = 15.0) -> dict:
+    from oracle import optim
+    from oracle import ppo as oppo
+
+    threads = len(os.sched_getaffinity(0))
+    rng_w = w
+    roll = configs.rollout(rng_w) if w.batch_size * w.network.obs_dim < 6e8 else None
+    if roll is None:  # C5: a full-size host rollout is 8.7 GB; sample 1/16 of the envs
+        rng_w = w.scaled(num_envs=max(w.num_envs // 16, w.ppo.num_minibatches))
+        roll = configs.rollout(rng_w)
+    params = init_params(w.network, seed=0, init=w.init)
+    perms = configs.permutations(rng_w)
+    # GAE + bootstrap alone
+    t0 = time.perf_counter()
+    oppo.update(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
+                max_minibatches=0)
+    t_gae = time.perf_counter() - t0
+    # minibatch steps until the budget is used (at least one)
+    mb_ratio = w.minibatch_size / rng_w.minibatch_size
+    done, t_mb = 0, 0.0
+    while done < w.ppo.update_epochs * w.ppo.num_minibatches:
+        t0 = time.perf_counter()
+        oppo.update(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
+                    max_minibatches=done + 1)
+        t_mb = time.perf_counter() - t0 - t_gae
+        done += 1
+        if t_mb * 1 > budget_s / 4 or t_mb > budget_s / (done + 1):
+            break
+    per_mb = max(t_mb, 1e-9) / done * mb_ratio
+    t_update = t_gae * (w.batch_size / rng_w.batch_size) + per_mb * w.ppo.update_epochs * w.ppo.num_minibatches
+    value = w.batch_size / t_update
+    return {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "sample": (f"NumPy oracle (float32, BLAS threads={threads}) on the {rng_w.name} "
+                       f"rollout T={rng_w.num_steps} N={rng_w.num_envs}: bootstrap+GAE plus {done} "
+                       f"of {w.ppo.update_epochs * w.ppo.num_minibatches} minibatch steps "
+                       f"(rows scaled x{mb_ratio:g}), extrapolated to one full update")}
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = []
+    cb = None
+    for _ in range(args.warmup + args.steps):
+        cb = cpu_baseline(w, budget_s=8.0)
+        steps.append(cb["value"])
+    value = statistics.median(steps[args.warmup:]) if args.steps else steps[-1]
+    cb["value"] = value
+    line = {
+        "impl": "reference", "metric": "ppo_learner_env_steps_per_sec", "value": value,
+        "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * w.batch_size / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "T": w.num_steps, "N_per_gpu": w.num_envs,
+                   "epochs": w.ppo.update_epochs, "minibatches": w.ppo.num_minibatches,
+                   "description": w.description},
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--precision", default=None)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    kw = {"precision": args.precision} if args.precision else {}
+    w = configs.make(args.config, **kw)
+    if args.impl == "reference":
+        return run_reference(args, w)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from boonta_b200.learner import Learner
+
+    lrn = Learner.from_workload(w, world_size=world, rank=rank)
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device=device)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(Learner.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        lrn.comm_init(bytes(uid.cpu().numpy()))
+    lrn.set_state(init_params(w.network, seed=0, init=w.init))
+
+    roll = device_rollout(w, seed=100 + rank, device=device)
+    n_perm = args.warmup + args.steps
+    perms = device_perms(w, world, n_perm, seed=7, device=device)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        lrn.update(roll, perms[i], stats=True)
+    barrier()
+    launches0 = lrn.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            lrn.update(roll, perms[args.warmup + i], stats=True)
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / max(args.steps, 1)
+    launches = (lrn.launch_count() - launches0) // max(args.steps, 1)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = world * w.batch_size / (ms / 1000.0)
+
+    # per-kernel-class device time of one more update (events around every launch)
+    lrn.profile(True)
+    lrn.update(roll, perms[0], stats=True)
+    torch.cuda.synchronize()
+    prof = lrn.profile_read()
+    lrn.profile(False)
+
+    # end to end: rollout from pinned host memory, statistics back to the host, every step
+    e2e = None
+    if not args.no_e2e:
+        host = {k: v.cpu().pin_memory() for k, v in roll.items()}
+        dev = {k: torch.empty_like(v) for k, v in roll.items()}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        st_host = torch.empty((w.ppo.update_epochs, w.ppo.num_minibatches, 8)).pin_memory()
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for i in range(args.steps):
+            for k in host:
+                dev[k].copy_(host[k], non_blocking=True)
+            st = lrn.update(dev, perms[args.warmup + i], stats=True)
+            st_host.copy_(st, non_blocking=True)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms2 = s2.elapsed_time(e2) / max(args.steps, 1)
+        t2 = torch.tensor([ms2], device=device)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        ms2 = float(t2.item())
+        e2e = {"value": world * w.batch_size / (ms2 / 1000.0), "unit": "env-steps/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(st_host.numel() * 4)}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    pk, pk_kind = peaks()
+    flops = gemm_flops(w)
+    updates_mb = w.ppo.update_epochs * w.ppo.num_minibatches
+    top = max(prof.items(), key=lambda kv: kv[1][0]) if prof else ("none", (0.0, 1))
+    cls, (tot_ms, n_launch) = top
+    avg_s = tot_ms / 1000.0 / max(n_launch, 1)
+    if cls.startswith("gemm"):
+        per_launch = flops[cls] * updates_mb / max(n_launch, 1)
+        achieved = per_launch / avg_s / 1e12
+        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": None, "kernel": cls,
+                "note": f"peak = bf16 sustained ({pk_kind}); fp32 CUDA-core GEMM in this build"}
+    else:
+        roof = {"bound": "hbm", "achieved": None, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": None, "traffic": None, "kernel": cls}
+    if "gae" in prof:
+        g_ms, g_n = prof["gae"]
+        gae_gbs = gae_bytes(w) / (g_ms / 1000.0 / g_n) / 1e9
+    else:
+        gae_gbs = None
+
+    line = {
+        "metric": "ppo_learner_env_steps_per_sec", "value": value, "unit": "env-steps/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {"fp32": "f32", "bf16": "bf16", "bf16x3": "bf16x3"}[w.precision],
+        "data": "synthetic",
+        "config": {"workload": w.name, "T": w.num_steps, "N_per_gpu": w.num_envs,
+                   "epochs": w.ppo.update_epochs, "minibatches": w.ppo.num_minibatches,
+                   "minibatch_rows": w.minibatch_size, "precision": w.precision,
+                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (obs rollout "
+                   f"{w.batch_size * w.network.obs_dim * 4 / 1e6:.0f} MB per GPU)",
+                   "description": w.description},
+        "roofline": roof,
+        "gae_hbm_gbs": gae_gbs,
+        "kernel_ms_per_step": {k: v[0] for k, v in sorted(prof.items())},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+// Shared helpers of the boonta_b200 CUDA library: status reporting, launch checks and
+// small device utilities. Every C-ABI entry point returns an int status and leaves a
+// message in a thread-local buffer (bt_last_error), mirroring the ffi::Error(code, msg)
+// convention of the reference's XLA FFI handlers (boonta/environments/ale/ffi/ffi.cc).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "boonta_b200.h"
+
+namespace bt {
+
+void set_error(const char* fmt, ...);
+const char* last_error();
+
+struct Status {
+  int code = BT_OK;
+  bool ok() const { return code == BT_OK; }
+};
+
+}  // namespace bt
+
+#define BT_CHECK_ARG(cond, ...)            \
+  do {                                     \
+    if (!(cond)) {                         \
+      ::bt::set_error(__VA_ARGS__);        \
+      return BT_ERR_INVALID;               \
+    }                                      \
+  } while (0)
+
+#define BT_CUDA(call)                                                                 \
+  do {                                                                                \
+    cudaError_t err_ = (call);                                                        \
+    if (err_ != cudaSuccess) {                                                        \
+      ::bt::set_error("%s:%d: %s failed: %s", __FILE__, __LINE__, #call,              \
+                      cudaGetErrorString(err_));                                      \
+      return BT_ERR_CUDA;                                                             \
+    }                                                                                 \
+  } while (0)
+
+// After a kernel launch: catch configuration errors without synchronising.
+#define BT_LAUNCH_CHECK(name)                                                         \
+  do {                                                                                \
+    cudaError_t err_ = cudaGetLastError();                                            \
+    if (err_ != cudaSuccess) {                                                        \
+      ::bt::set_error("%s:%d: launch of %s failed: %s", __FILE__, __LINE__, name,     \
+                      cudaGetErrorString(err_));                                      \
+      return BT_ERR_CUDA;                                                             \
+    }                                                                                 \
+  } while (0)
+
+#define BT_TRY(expr)          \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != BT_OK) return rc_; \
+  } while (0)
+
+namespace bt {
+
+constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
+
+__host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+__host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Activation and its derivative. The derivative is evaluated from the pre-activation
+// `z` and the output `h` (tanh uses h, relu and silu use z).
+__device__ __forceinline__ float act_forward(float z, int act) {
+  switch (act) {
+    case BT_ACT_TANH: return tanhf(z);
+    case BT_ACT_RELU: return z > 0.f ? z : 0.f;
+    case BT_ACT_SILU: return z / (1.f + expf(-z));
+    default: return z;
+  }
+}
+
+__device__ __forceinline__ float act_grad(float z, float h, int act) {
+  switch (act) {
+    case BT_ACT_TANH: return 1.f - h * h;
+    case BT_ACT_RELU: return z > 0.f ? 1.f : 0.f;
+    case BT_ACT_SILU: {
+      float s = 1.f / (1.f + expf(-z));
+      return s * (1.f + z * (1.f - s));
+    }
+    default: return 1.f;
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Effective row count: rows of a padded minibatch that carry data (a device-side count
+// when the rank's share of a global minibatch varies, else the static size).
+__device__ __forceinline__ int live_rows(const int* count, int rows) {
+  if (count == nullptr) return rows;
+  int c = *count;
+  return c < rows ? c : rows;
+}
+
+}  // namespace bt

@@ -1,0 +1,404 @@
+// Memory-bound kernels of the learner step:
+//   K4  LayerNorm forward/backward fused with the following activation
+//   K10 gradient reduction (split-K partials -> gradients, with the global-norm partial
+//       sums), clip_by_global_norm + Adam + apply_updates (optax semantics)
+//   K12 advantage normalisation;  K13 statistics reductions
+//   the multi-GPU minibatch split (global permutation -> this rank's rows)
+// Every reduction sums in a fixed order (per-block partials written to scratch, then
+// summed in index order), so a fixed input gives bitwise identical results.
+#include "kernels.cuh"
+
+namespace bt {
+
+constexpr float kLnEps = 1e-6f;
+
+// ---- LayerNorm -------------------------------------------------------------------------
+// flax.linen.LayerNorm(epsilon=1e-6, use_fast_variance=True):
+//   mean = E[z], var = max(E[z^2] - mean^2, 0), y = (z - mean) * (rsqrt(var + eps) * scale) + bias
+// One warp per row.
+__global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int n, int act,
+                                  float* y, float* h, float* mean_out, float* rstd_out,
+                                  const int* count) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= live_rows(count, rows)) return;
+  const float* zr = z + (size_t)row * n;
+  float s = 0.f, s2 = 0.f;
+  for (int k = lane; k < n; k += 32) {
+    const float v = zr[k];
+    s += v;
+    s2 += v * v;
+  }
+  s = warp_sum(s);
+  s2 = warp_sum(s2);
+  const float mean = s / n;
+  const float var = fmaxf(s2 / n - mean * mean, 0.f);
+  const float r = rsqrtf(var + kLnEps);
+  for (int k = lane; k < n; k += 32) {
+    const float yv = (zr[k] - mean) * (r * sb[k]) + sb[n + k];
+    y[(size_t)row * n + k] = yv;
+    h[(size_t)row * n + k] = act_forward(yv, act);
+  }
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = r;
+  }
+}
+
+int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act, float* y,
+                      float* h, float* mean, float* rstd, const int* count, cudaStream_t stream) {
+  if (rows <= 0) return BT_OK;
+  ln_forward_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(z, scale_bias, rows, n, act, y,
+                                                                  h, mean, rstd, count);
+  BT_LAUNCH_CHECK("ln_forward_kernel");
+  return BT_OK;
+}
+
+// d_z = r * (dxhat - mean(dxhat) - xhat * mean(dxhat * xhat)), dxhat = d_y * scale.
+// Grid-stride over rows, one warp per row; lanes keep the (d scale, d bias) partial sums
+// of the columns they own; the block sums its warps in order into partials[block].
+constexpr int kLnMaxCols = 1024;
+__global__ void __launch_bounds__(256) ln_backward_kernel(const float* d_y, const float* z,
+                                                          const float* mean, const float* rstd,
+                                                          const float* scale, int rows, int n,
+                                                          float* d_z, float* partials,
+                                                          const int* count) {
+  __shared__ float red[8][2 * 64];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int warps_total = gridDim.x * 8;
+  const int live = live_rows(count, rows);
+  constexpr int kPer = kLnMaxCols / 32;
+  float ds[kPer], db[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) ds[i] = db[i] = 0.f;
+  for (int row = blockIdx.x * 8 + warp; row < live; row += warps_total) {
+    const float* dyr = d_y + (size_t)row * n;
+    const float* zr = z + (size_t)row * n;
+    const float mu = mean[row], r = rstd[row];
+    float m1 = 0.f, m2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int k = lane + 32 * i;
+      if (k < n) {
+        const float xhat = (zr[k] - mu) * r;
+        const float dy = dyr[k];
+        const float dx = dy * scale[k];
+        m1 += dx;
+        m2 += dx * xhat;
+        ds[i] += dy * xhat;
+        db[i] += dy;
+      }
+    }
+    m1 = warp_sum(m1) / n;
+    m2 = warp_sum(m2) / n;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int k = lane + 32 * i;
+      if (k < n) {
+        const float xhat = (zr[k] - mu) * r;
+        const float dx = dyr[k] * scale[k];
+        d_z[(size_t)row * n + k] = r * (dx - m1 - xhat * m2);
+      }
+    }
+  }
+  // Block reduction of the column partial sums, 64 columns at a time.
+  for (int c0 = 0; c0 < n; c0 += 64) {
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int k = lane + 32 * i;
+      if (k >= c0 && k < c0 + 64 && k < n) {
+        red[warp][k - c0] = ds[i];
+        red[warp][64 + k - c0] = db[i];
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < 128) {
+      const int c = threadIdx.x & 63, which = threadIdx.x >> 6;
+      if (c0 + c < n) {
+        float s = 0.f;
+        for (int w = 0; w < 8; ++w) s += red[w][which * 64 + c];
+        partials[(size_t)blockIdx.x * 2 * n + which * n + c0 + c] = s;
+      }
+    }
+  }
+}
+
+int launch_ln_backward(const float* d_y, const float* z, const float* mean, const float* rstd,
+                       const float* scale, int rows, int n, float* d_z, float* partials,
+                       int blocks, const int* count, cudaStream_t stream) {
+  BT_CHECK_ARG(n <= kLnMaxCols, "layernorm width %d > %d", n, kLnMaxCols);
+  ln_backward_kernel<<<blocks, 256, 0, stream>>>(d_y, z, mean, rstd, scale, rows, n, d_z,
+                                                 partials, count);
+  BT_LAUNCH_CHECK("ln_backward_kernel");
+  return BT_OK;
+}
+
+// ---- gradient reduction + global norm ---------------------------------------------------
+__device__ __forceinline__ double block_sum_d(double v, double* sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  double s = 0.0;
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += sh[w];
+  }
+  __syncthreads();
+  return s;  // valid in thread 0
+}
+
+__global__ void __launch_bounds__(256) reduce_segments_kernel(const Segment* segs, float* grads,
+                                                              double* norm_partials) {
+  __shared__ double sh[8];
+  const Segment sg = segs[blockIdx.y];
+  double sq = 0.0;
+  const int per = ceil_div(sg.len, kReduceBlocksPerSegment);
+  const int b = blockIdx.x * per, e = min(sg.len, b + per);
+  for (int i = b + threadIdx.x; i < e; i += blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < sg.nsplit; ++k) s += sg.src[(size_t)k * sg.stride + i];
+    grads[sg.dst + i] = s;
+    sq += (double)s * (double)s;
+  }
+  if (norm_partials) {
+    const double t = block_sum_d(sq, sh);
+    if (threadIdx.x == 0)
+      norm_partials[(size_t)blockIdx.y * kReduceBlocksPerSegment + blockIdx.x] = t;
+  }
+}
+
+int launch_reduce_segments(const Segment* segs, int num_segments, float* grads,
+                           double* norm_partials, cudaStream_t stream) {
+  if (num_segments <= 0) return BT_OK;
+  dim3 grid(kReduceBlocksPerSegment, num_segments);
+  reduce_segments_kernel<<<grid, 256, 0, stream>>>(segs, grads, norm_partials);
+  BT_LAUNCH_CHECK("reduce_segments_kernel");
+  return BT_OK;
+}
+
+__global__ void __launch_bounds__(256) sumsq_kernel(const float* g, int64_t n, double* out) {
+  __shared__ double sh[8];
+  const int64_t per = ceil_div64(n, kNormBlocks);
+  const int64_t b = blockIdx.x * per, e = min(n, b + per);
+  double sq = 0.0;
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) sq += (double)g[i] * (double)g[i];
+  const double t = block_sum_d(sq, sh);
+  if (threadIdx.x == 0) out[blockIdx.x] = t;
+}
+
+int launch_sumsq(const float* g, int64_t n, double* norm_partials, cudaStream_t stream) {
+  sumsq_kernel<<<kNormBlocks, 256, 0, stream>>>(g, n, norm_partials);
+  BT_LAUNCH_CHECK("sumsq_kernel");
+  return BT_OK;
+}
+
+// ---- clip_by_global_norm + adam + apply_updates ------------------------------------------
+// optax: g_norm = ||g||; g <- g if g_norm < max_norm else (g / g_norm) * max_norm;
+// mu = (1-b1) g + b1 mu; nu = (1-b2) g^2 + b2 nu; count += 1;
+// p += -lr * (mu / (1 - b1^count)) / (sqrt(nu / (1 - b2^count) + eps_root) + eps).
+// Every block sums the norm partials itself, in index order (no grid-wide sync needed).
+__global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
+  __shared__ double sh[8];
+  __shared__ float s_norm;
+  double part = 0.0;
+  for (int i = threadIdx.x; i < p.num_norm_partials; i += blockDim.x) part += p.norm_partials[i];
+  // fixed-order block sum: thread-strided partial sums, then warps in order
+  const double total = block_sum_d(part, sh);
+  if (threadIdx.x == 0) s_norm = (float)sqrt(total);
+  __syncthreads();
+  const float g_norm = s_norm;
+  const bool clip = !(g_norm < p.max_norm);
+  const int count = *p.count + p.step + 1;
+  const float bc1 = __fsub_rn(1.f, powf(p.b1, (float)count));
+  const float bc2 = __fsub_rn(1.f, powf(p.b2, (float)count));
+  const float omb1 = __fsub_rn(1.f, p.b1), omb2 = __fsub_rn(1.f, p.b2);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += stride) {
+    float g = p.grads[i];
+    if (clip) g = __fmul_rn(__fdiv_rn(g, g_norm), p.max_norm);
+    const float m = __fadd_rn(__fmul_rn(omb1, g), __fmul_rn(p.b1, p.mu[i]));
+    const float v = __fadd_rn(__fmul_rn(omb2, __fmul_rn(g, g)), __fmul_rn(p.b2, p.nu[i]));
+    const float mh = __fdiv_rn(m, bc1);
+    const float vh = __fdiv_rn(v, bc2);
+    const float den = __fadd_rn(__fsqrt_rn(__fadd_rn(vh, p.eps_root)), p.eps);
+    const float u = __fmul_rn(-p.lr, __fdiv_rn(mh, den));
+    const float np_ = __fadd_rn(p.params[i], u);
+    p.params[i] = np_;
+    p.mu[i] = m;
+    p.nu[i] = v;
+    if (p.shadow) p.shadow[i] = __float2bfloat16_rn(np_);
+  }
+}
+
+int launch_adam(const AdamParams& p, cudaStream_t stream) {
+  adam_kernel<<<2 * kNumSMs, 256, 0, stream>>>(p);
+  BT_LAUNCH_CHECK("adam_kernel");
+  return BT_OK;
+}
+
+__global__ void increment_kernel(int* count, int by) { *count += by; }
+
+int launch_increment(int* count, int by, cudaStream_t stream) {
+  increment_kernel<<<1, 1, 0, stream>>>(count, by);
+  BT_LAUNCH_CHECK("increment_kernel");
+  return BT_OK;
+}
+
+// ---- statistics --------------------------------------------------------------------------
+__global__ void stat_reduce_kernel(const double* partials, int blocks, double* out) {
+  const int s = threadIdx.x;
+  if (s >= kNumStatSums) return;
+  double t = 0.0;
+  for (int b = 0; b < blocks; ++b) t += partials[(size_t)b * kNumStatSums + s];
+  out[s] = t;
+}
+
+int launch_stat_reduce(const double* partials, int blocks, double* out, cudaStream_t stream) {
+  stat_reduce_kernel<<<1, 32, 0, stream>>>(partials, blocks, out);
+  BT_LAUNCH_CHECK("stat_reduce_kernel");
+  return BT_OK;
+}
+
+// stats[i] = the eight logged values of boonta/algorithms/ppo.py:170-179 for minibatch i.
+__global__ void stat_finalize_kernel(const double* sums, int count, float inv_mb, float* stats) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  const double* s = sums + (size_t)i * kNumStatSums;
+  const double inv = (double)inv_mb;
+  float* o = stats + (size_t)i * BT_NUM_STATS;
+  o[0] = (float)(-s[0] * inv);
+  o[1] = (float)(s[1] * inv);
+  o[2] = (float)(s[2] * inv);
+  o[3] = (float)(s[3] * inv);
+  o[4] = (float)(s[4] * inv);
+  o[5] = (float)(s[5] * inv);
+  const double mr = s[6] * inv, var_res = fmax(s[7] * inv - mr * mr, 0.0);
+  const double mR = s[8] * inv, var_R = fmax(s[9] * inv - mR * mR, 0.0);
+  o[6] = (float)(1.0 - var_res / (var_R + 1e-8));
+  o[7] = (float)(s[10] * inv);
+}
+
+int launch_stat_finalize(const double* sums, int count, float inv_mb, float* stats,
+                         cudaStream_t stream) {
+  if (count <= 0) return BT_OK;
+  stat_finalize_kernel<<<ceil_div(count, 128), 128, 0, stream>>>(sums, count, inv_mb, stats);
+  BT_LAUNCH_CHECK("stat_finalize_kernel");
+  return BT_OK;
+}
+
+// ---- advantage normalisation (ppo.py:220-221) ----------------------------------------------
+__global__ void __launch_bounds__(256) adv_moments_kernel(const float* a, int64_t n,
+                                                          double* partials) {
+  __shared__ double sh[8];
+  const int64_t per = ceil_div64(n, kNormBlocks);
+  const int64_t b = blockIdx.x * per, e = min(n, b + per);
+  double s = 0.0, s2 = 0.0;
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) {
+    s += a[i];
+    s2 += (double)a[i] * a[i];
+  }
+  const double t = block_sum_d(s, sh);
+  const double t2 = block_sum_d(s2, sh);
+  if (threadIdx.x == 0) {
+    partials[2 * blockIdx.x] = t;
+    partials[2 * blockIdx.x + 1] = t2;
+  }
+}
+
+int launch_adv_moments(const float* adv, int64_t n, double* partials, cudaStream_t stream) {
+  adv_moments_kernel<<<kNormBlocks, 256, 0, stream>>>(adv, n, partials);
+  BT_LAUNCH_CHECK("adv_moments_kernel");
+  return BT_OK;
+}
+
+__global__ void adv_normalize_kernel(float* a, int64_t n, const double* partials, int np,
+                                     double total) {
+  __shared__ float s_mean, s_den;
+  if (threadIdx.x == 0) {
+    double s = 0.0, s2 = 0.0;
+    for (int i = 0; i < np; ++i) {
+      s += partials[2 * i];
+      s2 += partials[2 * i + 1];
+    }
+    const double mean = s / total;
+    const double var = fmax(s2 / total - mean * mean, 0.0);
+    s_mean = (float)mean;
+    s_den = (float)sqrt(var) + 1e-8f;
+  }
+  __syncthreads();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    a[i] = (a[i] - s_mean) / s_den;
+}
+
+int launch_adv_normalize(float* adv, int64_t n, const double* partials, int num_partials,
+                         double total, cudaStream_t stream) {
+  adv_normalize_kernel<<<2 * kNumSMs, 256, 0, stream>>>(adv, n, partials, num_partials, total);
+  BT_LAUNCH_CHECK("adv_normalize_kernel");
+  return BT_OK;
+}
+
+// ---- multi-GPU minibatch split ---------------------------------------------------------
+// Global flat index i = t * N_global + n_global (the flatten order of ppo.py:226-228 over
+// the global env axis). Rank r owns n_global in [r*N, (r+1)*N); its local flat index is
+// t * N + (n_global - r*N). For env permutations (recurrent) t is 0. One block per slice,
+// order-preserving compaction with a block-wide scan.
+__global__ void __launch_bounds__(1024) local_indices_kernel(const int* perm, int slice_len,
+                                                             int local_units, int rank,
+                                                             int global_units, int capacity,
+                                                             int* local_idx, int* counts,
+                                                             int* err) {
+  __shared__ int warp_tot[32];
+  __shared__ int base_s;
+  const int slice = blockIdx.x;
+  const int* src = perm + (size_t)slice * slice_len;
+  int* dst = local_idx + (size_t)slice * capacity;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) base_s = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < slice_len; c0 += 1024) {
+    const int i = c0 + threadIdx.x;
+    int local = -1;
+    if (i < slice_len) {
+      const int g = src[i];
+      const int t = g / global_units, ng = g - t * global_units;
+      if (ng / local_units == rank) local = t * local_units + (ng - rank * local_units);
+    }
+    const unsigned ballot = __ballot_sync(0xffffffffu, local >= 0);
+    const int before = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) warp_tot[warp] = __popc(ballot);
+    __syncthreads();
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += warp_tot[w];
+    const int pos = base_s + off + before;
+    if (local >= 0 && pos < capacity) dst[pos] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int tot = 0;
+      for (int w = 0; w < 32; ++w) tot += warp_tot[w];
+      base_s += tot;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const int n = base_s;
+    counts[slice] = n < capacity ? n : capacity;
+    if (n > capacity && err) atomicExch(err, 2);
+  }
+  // Pad the tail with a valid index so gathers of padding rows stay in bounds.
+  const int n = min(base_s, capacity);
+  for (int i = n + threadIdx.x; i < capacity; i += 1024) dst[i] = 0;
+}
+
+int launch_local_indices(const int* perm, int num_slices, int slice_len, int /*units_per_row*/,
+                         int local_units, int rank, int global_units, int capacity,
+                         int* local_idx, int* counts, int* err, cudaStream_t stream) {
+  local_indices_kernel<<<num_slices, 1024, 0, stream>>>(perm, slice_len, local_units, rank,
+                                                        global_units, capacity, local_idx,
+                                                        counts, err);
+  BT_LAUNCH_CHECK("local_indices_kernel");
+  return BT_OK;
+}
+
+}  // namespace bt

@@ -1,0 +1,119 @@
+// Declarations shared by the learner's kernels and its orchestration (learner.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace bt {
+
+// Per-minibatch statistic sums (double), in this order:
+//  0 sum min(surr1, surr2)   1 sum entropy        2 sum (lp_old - lp)   3 sum clipped
+//  4 sum advantage           5 sum critic term    6 sum (R - v)         7 sum (R - v)^2
+//  8 sum R                   9 sum R^2           10 sum v              11 live rows
+constexpr int kNumStatSums = 12;
+
+struct HeadsParams {
+  int rows;          // capacity rows of the minibatch buffers
+  const int* count;  // nullable: live rows
+  const int* idx;    // [rows] flat sample index (into [T*N] arrays); nullable = identity
+  const float* f_pi;
+  int F_pi;
+  const float* f_v;  // == f_pi when the torso is shared
+  int F_v;
+  const float* w_pi;   // [F_pi + 1, A]
+  const float* w_v;    // [F_v + 1, 1]
+  const float* scale;  // gaussian [A]
+  int A;
+  int head;
+  const void* action;
+  const float* lp_old;
+  const float* v_old;
+  const float* adv;
+  const float* ret;
+  float inv_mb;
+  float clip;
+  int clip_value;
+  float ent_coef;
+  float vf_coef;
+  float* d_out;  // [rows, A]
+  float* d_val;  // [rows]
+  float* d_fpi;  // [rows, F_pi]
+  float* d_fv;   // [rows, F_v] (separate towers)
+  const float* pre_pi;
+  const float* post_pi;
+  int act_pi;
+  const float* pre_v;
+  const float* post_v;
+  int act_v;
+  double* stat_partials;   // [gridDim.x][kNumStatSums]
+  float* dscale_partials;  // [gridDim.x][A] (gaussian)
+};
+
+int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream);
+size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared);
+int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
+                         const float* w_v, int A, int rows, float* out, float* value,
+                         cudaStream_t stream);
+
+// LayerNorm (flax, epsilon 1e-6, fast variance) fused with the following activation.
+int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act,
+                      float* y, float* h, float* mean, float* rstd, const int* count,
+                      cudaStream_t stream);
+// d_y already carries the activation derivative; writes d_z and per-block partial sums
+// [blocks][2n] of (d scale, d bias).
+int launch_ln_backward(const float* d_y, const float* z, const float* mean, const float* rstd,
+                       const float* scale, int rows, int n, float* d_z, float* partials,
+                       int blocks, const int* count, cudaStream_t stream);
+
+// One gradient segment: dst[0:len] = sum over s of src[s * stride + 0:len] (fixed order).
+struct Segment {
+  const float* src;
+  int nsplit;
+  int len;
+  int64_t stride;
+  int64_t dst;  // offset in the flat gradient buffer
+};
+constexpr int kReduceBlocksPerSegment = 32;
+// Sums split partials into the gradient buffer; when `norm_partials` is non-null also
+// writes per-block sums of squares [num_segments][kReduceBlocksPerSegment].
+int launch_reduce_segments(const Segment* segs, int num_segments, float* grads,
+                           double* norm_partials, cudaStream_t stream);
+// Sum of squares of a flat buffer into norm_partials[kNormBlocks] (multi-GPU path).
+constexpr int kNormBlocks = 256;
+int launch_sumsq(const float* g, int64_t n, double* norm_partials, cudaStream_t stream);
+
+struct AdamParams {
+  float* params;
+  float* mu;
+  float* nu;
+  const float* grads;
+  int64_t n;
+  const double* norm_partials;
+  int num_norm_partials;
+  const int* count;  // device adam count before this update block
+  int step;          // optimizer steps already taken in this update (count offset)
+  float lr, max_norm, b1, b2, eps, eps_root;
+  __nv_bfloat16* shadow;  // nullable bf16 copy of params
+};
+int launch_adam(const AdamParams& p, cudaStream_t stream);
+
+// Per-minibatch statistics.
+int launch_stat_reduce(const double* partials, int blocks, double* out, cudaStream_t stream);
+int launch_stat_finalize(const double* sums, int count, float inv_mb, float* stats,
+                         cudaStream_t stream);
+
+// Advantage normalisation over the whole rollout: (A - mean) / (std + 1e-8).
+int launch_adv_moments(const float* adv, int64_t n, double* partials, cudaStream_t stream);
+int launch_adv_normalize(float* adv, int64_t n, const double* partials, int num_partials,
+                         double total, cudaStream_t stream);
+
+int launch_increment(int* count, int by, cudaStream_t stream);
+
+// Multi-GPU minibatch split: for every (epoch, minibatch) slice of the global
+// permutation, keep the indices owned by this rank (in order), mapped to local flat
+// indices, and count them. Sets *err = BT_ERR_CAPACITY-style flag when a count exceeds
+// `capacity`.
+int launch_local_indices(const int* perm, int num_slices, int slice_len, int units_per_row,
+                         int local_units, int rank, int global_units, int capacity,
+                         int* local_idx, int* counts, int* err, cudaStream_t stream);
+
+}  // namespace bt

@@ -1,0 +1,747 @@
+// The learner handle: one PPO learner step per call, enqueued on one stream.
+//
+// Restates the control flow of boonta/algorithms/ppo.py:76-233 (PPO.update):
+//   1. bootstrap value V(second.obs[T-1])                        (:208-212)
+//   2. GAE over [T, N] (gae.cu)                                   (:213-219)
+//   3. optional advantage normalisation                           (:220-221)
+//   4. for each epoch e, minibatch m: the rows permutation[e][m*mb:(m+1)*mb] of the
+//      flattened rollout (index t*N + n, :199-203, :226-228):
+//        forward -> fused heads + loss + loss gradient -> backward -> gradient
+//        reduction (+ NCCL all-reduce across ranks) -> clip + Adam  (:148-197)
+// with every buffer allocated once at create. Parameters, gradients and both Adam
+// moments live in one flat fp32 buffer each (layout below), so the optimizer is a
+// single elementwise pass and the cross-GPU gradient mean is one all-reduce.
+//
+// Flat layout (must match boonta_b200/spec.py:param_layout): for every tower (shared
+// torso, or actor then critic), for every layer, a group [kernel [K, N]; bias [N]]
+// (+ [ln_scale [N]; ln_bias [N]]); conv kernels [3, 3, Cin, Cout] + bias; then
+// actor_head [F, A] + bias [A], gaussian scale [A], critic_head [F, 1] + bias [1].
+// Each group starts on a 64-float boundary.
+#include <algorithm>
+#include <cstring>
+
+#include "gemm_simt.cuh"
+#include "learner.h"
+
+namespace bt {
+
+int launch_gae_internal(const float* reward, const uint8_t* term, const uint8_t* trunc,
+                        const float* values, const float* bootstrap, int T, int N, double gamma,
+                        double lam, float* adv, float* ret, int* err, cudaStream_t stream);
+int comm_allreduce_f32(Comm* c, float* buf, size_t n, cudaStream_t stream);
+int comm_allreduce_f64(Comm* c, double* buf, size_t n, cudaStream_t stream);
+void comm_destroy(Comm* c);
+
+namespace {
+
+constexpr int64_t kAlign = 64;
+int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+int layer_out_dim(const bt_layer& l) {
+  if (l.kind == BT_LAYER_CONV3X3) return l.height * l.width * l.features;
+  return l.features;
+}
+
+struct LayoutBuilder {
+  std::vector<ParamEntryC>& out;
+  int64_t off = 0;
+  void part(const std::string& name, std::vector<int64_t> shape) {
+    int64_t n = 1;
+    for (auto s : shape) n *= s;
+    out.push_back({name, off, shape});
+    off += n;
+  }
+  void end() { off = align_up(off); }
+};
+
+int check_layer(const bt_layer& l, int in_dim, bool first) {
+  BT_CHECK_ARG(l.features > 0, "layer with %d features", l.features);
+  BT_CHECK_ARG(l.activation >= BT_ACT_NONE && l.activation <= BT_ACT_SILU, "bad activation %d",
+               l.activation);
+  if (l.kind == BT_LAYER_CONV3X3) {
+    BT_CHECK_ARG(first, "a Conv3x3 layer is only supported as the first layer of a tower");
+    BT_CHECK_ARG(l.height * l.width * l.in_channels == in_dim,
+                 "conv input %dx%dx%d does not match obs_dim %d", l.height, l.width, l.in_channels,
+                 in_dim);
+    BT_CHECK_ARG(!l.layernorm, "LayerNorm after a conv is not supported");
+  } else if (l.kind == BT_LAYER_GRU) {
+    ::bt::set_error("GRU layers are not supported by this learner build yet");
+    return BT_ERR_UNSUPPORTED;
+  } else {
+    BT_CHECK_ARG(l.kind == BT_LAYER_DENSE, "bad layer kind %d", l.kind);
+  }
+  return BT_OK;
+}
+
+}  // namespace
+
+int build_layout(bt_learner* L) {
+  const bt_network& net = L->cfg.network;
+  LayoutBuilder b{L->entries};
+  L->shared = net.num_critic == 0;
+  L->ntowers = L->shared ? 1 : 2;
+  const char* names[2] = {L->shared ? "torso" : "actor", "critic"};
+  for (int t = 0; t < L->ntowers; ++t) {
+    const bt_layer* layers = t == 0 ? net.torso : net.critic;
+    const int n = t == 0 ? net.num_torso : net.num_critic;
+    BT_CHECK_ARG(n >= 1 && n <= BT_MAX_LAYERS, "tower %d has %d layers", t, n);
+    TowerPlan& tp = L->towers[t];
+    tp.layers.clear();
+    tp.in_dim = net.obs_dim;
+    int dim = net.obs_dim;
+    for (int i = 0; i < n; ++i) {
+      const bt_layer& l = layers[i];
+      BT_TRY(check_layer(l, dim, i == 0));
+      LayerPlan lp;
+      lp.kind = l.kind;
+      lp.act = l.activation;
+      lp.ln = l.layernorm ? 1 : 0;
+      std::string p = std::string(names[t]) + "/" + std::to_string(i);
+      if (l.kind == BT_LAYER_CONV3X3) {
+        lp.H = l.height;
+        lp.W = l.width;
+        lp.C = l.in_channels;
+        lp.kin = 9 * l.in_channels;
+        lp.ncol = l.features;
+        lp.kout = layer_out_dim(l);
+        lp.w_off = b.off;
+        b.part(p + "/kernel", {3, 3, l.in_channels, l.features});
+        b.part(p + "/bias", {l.features});
+        b.end();
+      } else {
+        lp.kin = dim;
+        lp.kout = l.features;
+        lp.ncol = l.features;
+        lp.w_off = b.off;
+        b.part(p + "/kernel", {dim, l.features});
+        b.part(p + "/bias", {l.features});
+        b.end();
+        if (lp.ln) {
+          lp.ln_off = b.off;
+          b.part(p + "/ln_scale", {l.features});
+          b.part(p + "/ln_bias", {l.features});
+          b.end();
+        }
+      }
+      dim = lp.kout;
+      tp.layers.push_back(lp);
+    }
+    tp.out_dim = dim;
+  }
+  L->F_pi = L->towers[0].out_dim;
+  L->F_v = L->shared ? L->F_pi : L->towers[1].out_dim;
+  L->A = net.action_dim;
+  BT_CHECK_ARG(L->A >= 1 && L->A <= 64, "action_dim %d outside [1, 64]", L->A);
+  BT_CHECK_ARG(net.head == BT_HEAD_CATEGORICAL || net.head == BT_HEAD_GAUSSIAN, "bad head %d",
+               net.head);
+  L->head_pi_off = b.off;
+  b.part("actor_head/kernel", {L->F_pi, L->A});
+  b.part("actor_head/bias", {L->A});
+  b.end();
+  if (net.head == BT_HEAD_GAUSSIAN) {
+    L->head_scale_off = b.off;
+    b.part("actor_head/scale", {L->A});
+    b.end();
+  }
+  L->head_v_off = b.off;
+  b.part("critic_head/kernel", {L->F_v, 1});
+  b.part("critic_head/bias", {1});
+  b.end();
+  L->num_params = b.off;
+  return BT_OK;
+}
+
+namespace {
+
+template <class T>
+int dalloc(bt_learner* L, T** p, size_t count) {
+  if (count == 0) count = 1;
+  void* q = nullptr;
+  BT_CUDA(cudaMalloc(&q, count * sizeof(T)));
+  L->allocations.push_back(q);
+  *p = static_cast<T*>(q);
+  return BT_OK;
+}
+
+// Split-K factor for a dW GEMM: enough CTAs for ~2 waves on 148 SMs, at least 256
+// reduction rows per split.
+int pick_splits(int M, int N, int K) {
+  const int tiles = ceil_div(M, kBM) * ceil_div(N, kBN);
+  int s = std::max(1, (2 * kNumSMs) / tiles);
+  s = std::min(s, std::max(1, K / 256));
+  return s;
+}
+
+}  // namespace
+
+int allocate(bt_learner* L) {
+  const bt_learner_config& c = L->cfg;
+  const int E = c.ppo.update_epochs, M = c.ppo.num_minibatches;
+  const int world = std::max(1, c.world_size);
+  L->T = c.num_steps;
+  L->N = c.num_envs;
+  L->B = (int64_t)L->T * L->N;
+  const int64_t B_global = L->B * world;
+  BT_CHECK_ARG(M >= 1 && E >= 1, "num_minibatches %d / update_epochs %d", M, E);
+  BT_CHECK_ARG(B_global % M == 0, "batch %lld not divisible by num_minibatches %d",
+               (long long)B_global, M);
+  L->mb = (int)(B_global / M);
+  if (world == 1) {
+    L->rows_cap = L->mb;
+  } else {
+    // Hypergeometric share of a global minibatch: mean mb/world, std < sqrt(mb/world).
+    const double mean = (double)L->mb / world;
+    int cap = (int)std::ceil(mean + 16.0 * std::sqrt(mean) + 64.0);
+    L->rows_cap = std::min<int64_t>(std::min<int64_t>(cap, L->mb), L->B);
+  }
+  L->act_rows = std::max(L->rows_cap, L->N);
+  const int R = L->act_rows;
+
+  const int64_t P = L->num_params;
+  BT_TRY(dalloc(L, &L->params, P));
+  BT_TRY(dalloc(L, &L->grads, P));
+  BT_TRY(dalloc(L, &L->mu, P));
+  BT_TRY(dalloc(L, &L->nu, P));
+  BT_CUDA(cudaMemset(L->params, 0, P * 4));
+  BT_CUDA(cudaMemset(L->grads, 0, P * 4));
+  BT_CUDA(cudaMemset(L->mu, 0, P * 4));
+  BT_CUDA(cudaMemset(L->nu, 0, P * 4));
+  BT_TRY(dalloc(L, &L->count_d, 4));
+  BT_CUDA(cudaMemset(L->count_d, 0, 16));
+  L->err_d = L->count_d + 1;
+  L->mb_count_d = L->count_d + 2;
+
+  L->segs_h.clear();
+  for (int t = 0; t < L->ntowers; ++t) {
+    for (size_t i = 0; i < L->towers[t].layers.size(); ++i) {
+      LayerPlan& lp = L->towers[t].layers[i];
+      const size_t n = (size_t)R * lp.kout;
+      BT_TRY(dalloc(L, &lp.z, n));
+      BT_TRY(dalloc(L, &lp.h, n));
+      BT_TRY(dalloc(L, &lp.d_pre, n));
+      if (lp.ln) {
+        BT_TRY(dalloc(L, &lp.y, n));
+        BT_TRY(dalloc(L, &lp.d_z, n));
+        BT_TRY(dalloc(L, &lp.mean, R));
+        BT_TRY(dalloc(L, &lp.rstd, R));
+        lp.ln_blocks = 2 * kNumSMs;
+        BT_TRY(dalloc(L, &lp.ln_part, (size_t)lp.ln_blocks * 2 * lp.kout));
+      } else {
+        lp.d_z = lp.d_pre;
+      }
+      // dW GEMM: [kin + 1, ncol] over K = rows (dense) or rows * H*W (conv)
+      const int dm = lp.kin + 1, dn = lp.ncol;
+      const int dk = lp.kind == BT_LAYER_CONV3X3 ? L->rows_cap * lp.H * lp.W : L->rows_cap;
+      lp.dw_splits = pick_splits(dm, dn, dk);
+      BT_TRY(dalloc(L, &lp.dw_part, (size_t)lp.dw_splits * dm * dn));
+      L->segs_h.push_back({lp.dw_part, lp.dw_splits, dm * dn, (int64_t)dm * dn, lp.w_off});
+      if (lp.ln) {
+        L->segs_h.push_back(
+            {lp.ln_part, lp.ln_blocks, 2 * lp.kout, (int64_t)2 * lp.kout, lp.ln_off});
+      }
+    }
+  }
+  // heads
+  const int A = L->A;
+  BT_TRY(dalloc(L, &L->d_out, (size_t)R * A));
+  BT_TRY(dalloc(L, &L->d_val, R));
+  L->head_pi_splits = pick_splits(L->F_pi + 1, A, L->rows_cap);
+  L->head_v_splits = pick_splits(L->F_v + 1, 1, L->rows_cap);
+  BT_TRY(dalloc(L, &L->head_pi_part, (size_t)L->head_pi_splits * (L->F_pi + 1) * A));
+  BT_TRY(dalloc(L, &L->head_v_part, (size_t)L->head_v_splits * (L->F_v + 1)));
+  L->segs_h.push_back({L->head_pi_part, L->head_pi_splits, (L->F_pi + 1) * A,
+                       (int64_t)(L->F_pi + 1) * A, L->head_pi_off});
+  L->heads_blocks = kNumSMs;
+  BT_TRY(dalloc(L, &L->stat_part, (size_t)L->heads_blocks * kNumStatSums));
+  if (c.network.head == BT_HEAD_GAUSSIAN) {
+    BT_TRY(dalloc(L, &L->dscale_part, (size_t)L->heads_blocks * A));
+    L->segs_h.push_back({L->dscale_part, L->heads_blocks, A, (int64_t)A, L->head_scale_off});
+  }
+  L->segs_h.push_back(
+      {L->head_v_part, L->head_v_splits, L->F_v + 1, (int64_t)(L->F_v + 1), L->head_v_off});
+  BT_TRY(dalloc(L, &L->segs_d, L->segs_h.size()));
+  BT_CUDA(cudaMemcpy(L->segs_d, L->segs_h.data(), L->segs_h.size() * sizeof(Segment),
+                     cudaMemcpyHostToDevice));
+  BT_TRY(dalloc(L, &L->norm_part,
+                std::max<size_t>(L->segs_h.size() * kReduceBlocksPerSegment, kNormBlocks)));
+  BT_TRY(dalloc(L, &L->stat_sums, (size_t)(E * M + 1) * kNumStatSums));
+  BT_TRY(dalloc(L, &L->adv_part, 2 * kNormBlocks));
+  // targets
+  BT_TRY(dalloc(L, &L->adv, L->B));
+  BT_TRY(dalloc(L, &L->ret, L->B));
+  BT_TRY(dalloc(L, &L->boot, L->N));
+  BT_TRY(dalloc(L, &L->act_out, (size_t)R * A));
+  BT_TRY(dalloc(L, &L->act_val, R));
+  if (world > 1) {
+    BT_TRY(dalloc(L, &L->local_idx, (size_t)E * M * L->rows_cap));
+    BT_TRY(dalloc(L, &L->local_counts, (size_t)E * M));
+  }
+  return BT_OK;
+}
+
+// ---- forward / backward of one tower --------------------------------------------------
+int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
+                  const int* count, cudaStream_t s) {
+  const float* in = obs;
+  const int* gather = idx;
+  int in_ld = tp.in_dim;
+  for (size_t i = 0; i < tp.layers.size(); ++i) {
+    LayerPlan& lp = tp.layers[i];
+    const float* w = L->params + lp.w_off;
+    if (lp.kind == BT_LAYER_CONV3X3) {
+      AIm2col a{in, gather, lp.H, lp.W, lp.C};
+      BRows b{w, lp.ncol, lp.kin + 1};
+      EpiForward ep{lp.z, lp.h, lp.ncol, lp.act};
+      BT_K(L, kProfGemmFwd, s, launch_gemm_simt(a, b, ep, rows * lp.H * lp.W, lp.ncol, lp.kin + 1, 1, s, count,
+                              nullptr, lp.H * lp.W));
+    } else {
+      ARows a{in, gather, in_ld, lp.kin};
+      BRows b{w, lp.ncol, lp.kin + 1};
+      EpiForward ep{lp.z, lp.ln ? nullptr : lp.h, lp.ncol, lp.ln ? BT_ACT_NONE : lp.act};
+      BT_K(L, kProfGemmFwd, s, launch_gemm_simt(a, b, ep, rows, lp.ncol, lp.kin + 1, 1, s, count, nullptr));
+      if (lp.ln) {
+        BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act, lp.y, lp.h,
+                                 lp.mean, lp.rstd, count, s));
+      }
+    }
+    in = lp.h;
+    gather = nullptr;
+    in_ld = lp.kout;
+  }
+  return BT_OK;
+}
+
+int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
+                   const int* count, cudaStream_t s) {
+  for (int i = (int)tp.layers.size() - 1; i >= 0; --i) {
+    LayerPlan& lp = tp.layers[i];
+    const float* w = L->params + lp.w_off;
+    if (lp.ln) {
+      BT_K(L, kProfLnBwd, s, launch_ln_backward(lp.d_pre, lp.z, lp.mean, lp.rstd, L->params + lp.ln_off, rows,
+                                lp.kout, lp.d_z, lp.ln_part, lp.ln_blocks, count, s));
+    }
+    const int dm = lp.kin + 1, dn = lp.ncol;
+    EpiPartial ep{lp.dw_part, dn, (size_t)dm * dn};
+    if (lp.kind == BT_LAYER_CONV3X3) {
+      AIm2colT a{AIm2col{obs, idx, lp.H, lp.W, lp.C}};
+      const int K = rows * lp.H * lp.W;
+      BRows b{lp.d_z, lp.ncol, K};
+      BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, dm, dn, K, lp.dw_splits, s, nullptr, count,
+                              lp.H * lp.W));
+    } else {
+      const float* in = i == 0 ? obs : tp.layers[i - 1].h;
+      const int* gather = i == 0 ? idx : nullptr;
+      ACols a{in, gather, lp.kin, lp.kin};
+      BRows b{lp.d_z, lp.ncol, rows};
+      BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, dm, dn, rows, lp.dw_splits, s, nullptr, count));
+    }
+    if (i > 0) {
+      LayerPlan& prev = tp.layers[i - 1];
+      ARows a{lp.d_z, nullptr, lp.ncol, lp.ncol};
+      BCols b{w, lp.ncol, lp.ncol};
+      EpiActGrad ep2{prev.d_pre, prev.pre(), prev.h, prev.kout, prev.act};
+      BT_K(L, kProfGemmDx, s, launch_gemm_simt(a, b, ep2, rows, lp.kin, lp.ncol, 1, s, count, nullptr));
+    }
+  }
+  return BT_OK;
+}
+
+struct MinibatchInputs {
+  const float* obs;
+  const void* action;
+  const float* lp_old;
+  const float* v_old;
+  const float* adv;
+  const float* ret;
+  const int* idx;
+  const int* count;  // nullable
+  float inv_mb;
+};
+
+// Forward + loss + backward + gradient reduction for one minibatch. Leaves the
+// (unreduced across ranks) gradients in L->grads and the statistic sums in stat_slot.
+int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool with_norm,
+               cudaStream_t s) {
+  const int rows = L->rows_cap;
+  const bt_learner_config& c = L->cfg;
+  for (int t = 0; t < L->ntowers; ++t)
+    BT_TRY(forward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
+  TowerPlan& t0 = L->towers[0];
+  TowerPlan& tv = L->towers[L->ntowers - 1];
+  LayerPlan& last_pi = t0.layers.back();
+  LayerPlan& last_v = tv.layers.back();
+  HeadsParams hp{};
+  hp.rows = rows;
+  hp.count = in.count;
+  hp.idx = in.idx;
+  hp.f_pi = last_pi.h;
+  hp.F_pi = L->F_pi;
+  hp.f_v = last_v.h;
+  hp.F_v = L->F_v;
+  hp.w_pi = L->params + L->head_pi_off;
+  hp.w_v = L->params + L->head_v_off;
+  hp.scale = L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr;
+  hp.A = L->A;
+  hp.head = c.network.head;
+  hp.action = in.action;
+  hp.lp_old = in.lp_old;
+  hp.v_old = in.v_old;
+  hp.adv = in.adv;
+  hp.ret = in.ret;
+  hp.inv_mb = in.inv_mb;
+  hp.clip = c.ppo.clip_coefficient;
+  hp.clip_value = c.ppo.clip_value_loss;
+  hp.ent_coef = c.ppo.entropy_coefficient;
+  hp.vf_coef = c.ppo.value_coefficient;
+  hp.d_out = L->d_out;
+  hp.d_val = L->d_val;
+  hp.d_fpi = last_pi.d_pre;
+  hp.d_fv = L->shared ? nullptr : last_v.d_pre;
+  hp.pre_pi = last_pi.pre();
+  hp.post_pi = last_pi.h;
+  hp.act_pi = last_pi.act;
+  hp.pre_v = last_v.pre();
+  hp.post_v = last_v.h;
+  hp.act_v = last_v.act;
+  hp.stat_partials = L->stat_part;
+  hp.dscale_partials = L->dscale_part;
+  BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
+  BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
+  // head weight gradients: [F + 1, A] = [f, 1]^T d_out
+  {
+    ACols a{last_pi.h, nullptr, L->F_pi, L->F_pi};
+    BRows b{L->d_out, L->A, rows};
+    EpiPartial ep{L->head_pi_part, L->A, (size_t)(L->F_pi + 1) * L->A};
+    BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, L->F_pi + 1, L->A, rows, L->head_pi_splits, s, nullptr,
+                            in.count));
+  }
+  {
+    ACols a{last_v.h, nullptr, L->F_v, L->F_v};
+    BRows b{L->d_val, 1, rows};
+    EpiPartial ep{L->head_v_part, 1, (size_t)(L->F_v + 1)};
+    BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, L->F_v + 1, 1, rows, L->head_v_splits, s, nullptr,
+                            in.count));
+  }
+  for (int t = 0; t < L->ntowers; ++t)
+    BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
+  BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, (int)L->segs_h.size(), L->grads,
+                                with_norm ? L->norm_part : nullptr, s));
+  return BT_OK;
+}
+
+int check_batch(bt_learner* L, const bt_batch* b) {
+  BT_CHECK_ARG(b != nullptr, "null batch");
+  BT_CHECK_ARG(b->obs && b->bootstrap_obs && b->action && b->reward && b->terminated &&
+                   b->truncated && b->log_prob && b->value,
+               "batch has a null field");
+  return BT_OK;
+}
+
+int bootstrap_and_gae(bt_learner* L, const bt_batch* b, cudaStream_t s) {
+  // V(second.obs[T-1]) through the critic's tower (or the shared torso).
+  TowerPlan& tv = L->towers[L->ntowers - 1];
+  BT_TRY(forward_tower(L, tv, b->bootstrap_obs, nullptr, L->N, nullptr, s));
+  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(tv.layers.back().h, L->F_v, tv.layers.back().h, L->F_v,
+                              L->params + L->head_pi_off, L->params + L->head_v_off, L->A, L->N,
+                              nullptr, L->boot, s));
+  BT_K(L, kProfGae, s, launch_gae_internal(b->reward, b->terminated, b->truncated, b->value, L->boot, L->T,
+                             L->N, L->cfg.ppo.gamma, L->cfg.ppo.gae_lambda, L->adv, L->ret,
+                             L->err_d, s));
+  if (L->cfg.ppo.normalize_advantage) {
+    BT_K(L, kProfMisc, s, launch_adv_moments(L->adv, L->B, L->adv_part, s));
+    if (L->comm) BT_TRY(comm_allreduce_f64(L->comm, L->adv_part, 2 * kNormBlocks, s));
+    BT_K(L, kProfMisc, s, launch_adv_normalize(L->adv, L->B, L->adv_part, kNormBlocks,
+                                (double)L->B * std::max(1, L->cfg.world_size), s));
+  }
+  return BT_OK;
+}
+
+int optimizer_step(bt_learner* L, int step, cudaStream_t s) {
+  const bt_optimizer& o = L->cfg.optimizer;
+  AdamParams ap{};
+  ap.params = L->params;
+  ap.mu = L->mu;
+  ap.nu = L->nu;
+  ap.grads = L->grads;
+  ap.n = L->num_params;
+  if (L->comm) {
+    BT_C(L, kProfAllreduce, s, comm_allreduce_f32(L->comm, L->grads, (size_t)L->num_params, s));
+    BT_K(L, kProfReduce, s, launch_sumsq(L->grads, L->num_params, L->norm_part, s));
+    ap.num_norm_partials = kNormBlocks;
+  } else {
+    ap.num_norm_partials = (int)L->segs_h.size() * kReduceBlocksPerSegment;
+  }
+  ap.norm_partials = L->norm_part;
+  ap.count = L->count_d;
+  ap.step = step;
+  ap.lr = o.lr;
+  ap.max_norm = o.max_grad_norm;
+  ap.b1 = o.b1;
+  ap.b2 = o.b2;
+  ap.eps = o.eps;
+  ap.eps_root = o.eps_root;
+  ap.shadow = nullptr;
+  BT_K(L, kProfAdam, s, launch_adam(ap, s));
+  return BT_OK;
+}
+
+}  // namespace bt
+
+using namespace bt;
+
+// ---- C ABI -------------------------------------------------------------------------------
+extern "C" int bt_learner_create(const bt_learner_config* cfg, bt_learner** out) {
+  BT_CHECK_ARG(cfg && out, "bt_learner_create: null argument");
+  *out = nullptr;
+  BT_CHECK_ARG(cfg->num_steps > 0 && cfg->num_envs > 0, "num_steps %d / num_envs %d",
+               cfg->num_steps, cfg->num_envs);
+  BT_CHECK_ARG(cfg->network.obs_dim > 0, "obs_dim %d", cfg->network.obs_dim);
+  BT_CHECK_ARG(cfg->precision == BT_PREC_FP32, "precision %d is not available in this build",
+               cfg->precision);
+  BT_CHECK_ARG(cfg->world_size >= 1 && cfg->rank >= 0 && cfg->rank < cfg->world_size,
+               "rank %d / world_size %d", cfg->rank, cfg->world_size);
+  bt_learner* L = new bt_learner();
+  L->cfg = *cfg;
+  int rc = cudaGetDevice(&L->device) == cudaSuccess ? BT_OK : BT_ERR_CUDA;
+  if (rc == BT_OK) rc = build_layout(L);
+  if (rc == BT_OK) rc = allocate(L);
+  if (rc != BT_OK) {
+    bt_learner_destroy(L);
+    return rc;
+  }
+  *out = L;
+  return BT_OK;
+}
+
+extern "C" void bt_learner_destroy(bt_learner* L) {
+  if (!L) return;
+  if (L->comm) comm_destroy(L->comm);
+  for (cudaEvent_t e : L->prof.pool) cudaEventDestroy(e);
+  for (void* p : L->allocations) cudaFree(p);
+  delete L;
+}
+
+extern "C" int64_t bt_learner_num_params(const bt_learner* L) { return L ? L->num_params : -1; }
+
+extern "C" int32_t bt_learner_param_count(const bt_learner* L) {
+  return L ? (int32_t)L->entries.size() : -1;
+}
+
+extern "C" int bt_learner_param_info(const bt_learner* L, int32_t index, char* name,
+                                     int32_t name_len, int64_t* offset, int32_t* ndim,
+                                     int64_t* shape) {
+  BT_CHECK_ARG(L, "null learner");
+  BT_CHECK_ARG(index >= 0 && index < (int32_t)L->entries.size(), "param index %d", index);
+  const ParamEntryC& e = L->entries[index];
+  if (name && name_len > 0) {
+    std::strncpy(name, e.name.c_str(), name_len - 1);
+    name[name_len - 1] = 0;
+  }
+  if (offset) *offset = e.offset;
+  if (ndim) *ndim = (int32_t)e.shape.size();
+  if (shape)
+    for (size_t i = 0; i < e.shape.size() && i < 4; ++i) shape[i] = e.shape[i];
+  return BT_OK;
+}
+
+extern "C" int bt_learner_set_state(bt_learner* L, const float* params, const float* mu,
+                                    const float* nu, int32_t count, void* stream) {
+  BT_CHECK_ARG(L && params, "bt_learner_set_state: null argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t bytes = (size_t)L->num_params * 4;
+  BT_CUDA(cudaMemcpyAsync(L->params, params, bytes, cudaMemcpyDefault, s));
+  if (mu) {
+    BT_CUDA(cudaMemcpyAsync(L->mu, mu, bytes, cudaMemcpyDefault, s));
+  } else {
+    BT_CUDA(cudaMemsetAsync(L->mu, 0, bytes, s));
+  }
+  if (nu) {
+    BT_CUDA(cudaMemcpyAsync(L->nu, nu, bytes, cudaMemcpyDefault, s));
+  } else {
+    BT_CUDA(cudaMemsetAsync(L->nu, 0, bytes, s));
+  }
+  static thread_local int host_count;
+  host_count = count;
+  BT_CUDA(cudaMemcpyAsync(L->count_d, &host_count, 4, cudaMemcpyHostToDevice, s));
+  BT_CUDA(cudaStreamSynchronize(s));  // host_count must outlive the copy
+  return BT_OK;
+}
+
+extern "C" int bt_learner_get_state(bt_learner* L, float* params, float* mu, float* nu,
+                                    int32_t* count, void* stream) {
+  BT_CHECK_ARG(L, "null learner");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t bytes = (size_t)L->num_params * 4;
+  if (params) BT_CUDA(cudaMemcpyAsync(params, L->params, bytes, cudaMemcpyDefault, s));
+  if (mu) BT_CUDA(cudaMemcpyAsync(mu, L->mu, bytes, cudaMemcpyDefault, s));
+  if (nu) BT_CUDA(cudaMemcpyAsync(nu, L->nu, bytes, cudaMemcpyDefault, s));
+  if (count) {
+    BT_CUDA(cudaMemcpyAsync(count, L->count_d, 4, cudaMemcpyDefault, s));
+    BT_CUDA(cudaStreamSynchronize(s));
+  }
+  return BT_OK;
+}
+
+extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int32_t* perm,
+                                 float* stats, void* stream) {
+  BT_CHECK_ARG(L && perm, "bt_learner_update: null argument");
+  BT_TRY(check_batch(L, batch));
+  const int world = std::max(1, L->cfg.world_size);
+  BT_CHECK_ARG(world == 1 || L->comm, "world_size %d needs bt_learner_comm_init", world);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
+  const int64_t Bg = L->B * world;
+  BT_TRY(bootstrap_and_gae(L, batch, s));
+  if (world > 1) {
+    BT_K(L, kProfMisc, s, launch_local_indices(perm, E * M, L->mb, 0, L->N, L->cfg.rank, L->N * world,
+                                L->rows_cap, L->local_idx, L->local_counts, L->err_d, s));
+  }
+  MinibatchInputs in{};
+  in.obs = batch->obs;
+  in.action = batch->action;
+  in.lp_old = batch->log_prob;
+  in.v_old = batch->value;
+  in.adv = L->adv;
+  in.ret = L->ret;
+  in.inv_mb = 1.0f / (float)L->mb;
+  for (int e = 0; e < E; ++e) {
+    for (int m = 0; m < M; ++m) {
+      const int i = e * M + m;
+      if (world > 1) {
+        in.idx = L->local_idx + (size_t)i * L->rows_cap;
+        in.count = L->local_counts + i;
+      } else {
+        in.idx = perm + (size_t)e * Bg + (size_t)m * L->mb;
+        in.count = nullptr;
+      }
+      BT_TRY(loss_grads(L, in, L->stat_sums + (size_t)i * kNumStatSums, world == 1, s));
+      BT_TRY(optimizer_step(L, i, s));
+    }
+  }
+  BT_K(L, kProfMisc, s, launch_increment(L->count_d, E * M, s));
+  if (L->comm) BT_TRY(comm_allreduce_f64(L->comm, L->stat_sums, (size_t)E * M * kNumStatSums, s));
+  if (stats) BT_K(L, kProfStats, s, launch_stat_finalize(L->stat_sums, E * M, 1.0f / (float)L->mb, stats, s));
+  return BT_OK;
+}
+
+extern "C" int bt_learner_targets(bt_learner* L, float* advantages, float* returns,
+                                  float* bootstrap, void* stream) {
+  BT_CHECK_ARG(L, "null learner");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (advantages)
+    BT_CUDA(cudaMemcpyAsync(advantages, L->adv, L->B * 4, cudaMemcpyDeviceToDevice, s));
+  if (returns) BT_CUDA(cudaMemcpyAsync(returns, L->ret, L->B * 4, cudaMemcpyDeviceToDevice, s));
+  if (bootstrap)
+    BT_CUDA(cudaMemcpyAsync(bootstrap, L->boot, L->N * 4, cudaMemcpyDeviceToDevice, s));
+  return BT_OK;
+}
+
+extern "C" int bt_learner_loss_grads(bt_learner* L, const bt_batch* batch, const float* adv,
+                                     const float* ret, const int32_t* indices, int32_t count,
+                                     float* grads, float* stats, void* stream) {
+  BT_CHECK_ARG(L && indices && adv && ret, "bt_learner_loss_grads: null argument");
+  BT_TRY(check_batch(L, batch));
+  BT_CHECK_ARG(count >= 1 && count <= L->rows_cap, "count %d outside [1, %d]", count,
+               L->rows_cap);
+  cudaStream_t s = (cudaStream_t)stream;
+  static thread_local int host_count;
+  host_count = count;
+  BT_CUDA(cudaMemcpyAsync(L->mb_count_d, &host_count, 4, cudaMemcpyHostToDevice, s));
+  BT_CUDA(cudaStreamSynchronize(s));
+  MinibatchInputs in{};
+  in.obs = batch->obs;
+  in.action = batch->action;
+  in.lp_old = batch->log_prob;
+  in.v_old = batch->value;
+  in.adv = adv;
+  in.ret = ret;
+  in.idx = indices;
+  in.count = L->mb_count_d;
+  in.inv_mb = 1.0f / (float)count;
+  const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
+  double* slot = L->stat_sums + (size_t)E * M * kNumStatSums;
+  BT_TRY(loss_grads(L, in, slot, true, s));
+  if (grads)
+    BT_CUDA(cudaMemcpyAsync(grads, L->grads, (size_t)L->num_params * 4, cudaMemcpyDeviceToDevice,
+                            s));
+  if (stats) BT_K(L, kProfStats, s, launch_stat_finalize(slot, 1, 1.0f / (float)count, stats, s));
+  return BT_OK;
+}
+
+namespace bt {
+int launch_sample(const float* out, const float* scale, int head, int A, int rows,
+                  const float* noise, float temperature, void* action, float* log_prob,
+                  cudaStream_t stream);
+}
+
+extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, const float* noise,
+                              float temperature, void* action, float* log_prob, float* value,
+                              void* stream) {
+  BT_CHECK_ARG(L && obs && action && log_prob, "bt_learner_act: null argument");
+  BT_CHECK_ARG(num >= 0 && num <= L->act_rows, "bt_learner_act: %d rows > capacity %d", num,
+               L->act_rows);
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int t = 0; t < L->ntowers; ++t)
+    BT_TRY(forward_tower(L, L->towers[t], obs, nullptr, num, nullptr, s));
+  TowerPlan& t0 = L->towers[0];
+  TowerPlan& tv = L->towers[L->ntowers - 1];
+  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(t0.layers.back().h, L->F_pi, tv.layers.back().h, L->F_v,
+                              L->params + L->head_pi_off, L->params + L->head_v_off, L->A, num,
+                              L->act_out, value ? value : L->act_val, s));
+  BT_K(L, kProfMisc, s, launch_sample(L->act_out,
+                       L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr,
+                       L->cfg.network.head, L->A, num, noise, temperature, action, log_prob, s));
+  return BT_OK;
+}
+
+// ---- profiling ---------------------------------------------------------------------------
+const char* const kProfNames[kProfNumClasses] = {
+    "gae", "gemm_fwd", "gemm_dx", "gemm_dw", "heads_loss", "heads_fwd", "ln_fwd",
+    "ln_bwd", "grad_reduce", "clip_adam", "stats", "allreduce", "misc"};
+
+cudaEvent_t prof_event(bt_learner* L) {
+  Profiler& p = L->prof;
+  if (p.used == p.pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    p.pool.push_back(e);
+  }
+  return p.pool[p.used++];
+}
+
+extern "C" int bt_learner_profile(bt_learner* L, int32_t enable) {
+  BT_CHECK_ARG(L, "null learner");
+  L->prof.on = enable != 0;
+  if (enable) {
+    L->prof.recs.clear();
+    L->prof.used = 0;
+  }
+  return BT_OK;
+}
+
+extern "C" int bt_learner_profile_read(bt_learner* L, int32_t cls, char* name, int32_t name_len,
+                                       double* total_ms, int64_t* launches) {
+  BT_CHECK_ARG(L, "null learner");
+  BT_CHECK_ARG(cls >= 0 && cls < kProfNumClasses, "profile class %d", cls);
+  double ms = 0.0;
+  int64_t n = 0;
+  for (const ProfRecord& r : L->prof.recs) {
+    if (r.cls != cls) continue;
+    BT_CUDA(cudaEventSynchronize(r.b));
+    float t = 0.f;
+    BT_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+    ms += t;
+    ++n;
+  }
+  if (name && name_len > 0) {
+    std::strncpy(name, kProfNames[cls], name_len - 1);
+    name[name_len - 1] = 0;
+  }
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = n;
+  return BT_OK;
+}
+
+extern "C" int64_t bt_learner_launch_count(const bt_learner* L) {
+  return L ? L->prof.launches : -1;
+}

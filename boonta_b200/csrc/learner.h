@@ -1,0 +1,145 @@
+// Internal state of a learner handle (one per GPU and stream).
+#pragma once
+
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+
+struct ParamEntryC {
+  std::string name;
+  int64_t offset;
+  std::vector<int64_t> shape;
+};
+
+struct LayerPlan {
+  int kind = BT_LAYER_DENSE;
+  int act = BT_ACT_NONE;
+  int ln = 0;
+  int kin = 0;    // input width (dense), 9*C (conv patch)
+  int kout = 0;   // output width per row (conv: H*W*Cout)
+  int ncol = 0;   // GEMM N: dense kout, conv Cout
+  int H = 0, W = 0, C = 0;
+  int64_t w_off = 0, ln_off = 0;
+  float* z = nullptr;     // pre-activation (pre-LayerNorm)
+  float* y = nullptr;     // LayerNorm output (LN layers)
+  float* h = nullptr;     // layer output
+  float* mean = nullptr;  // LN row statistics
+  float* rstd = nullptr;
+  float* d_pre = nullptr;  // dL/d(pre-activation): d y for LN layers, d z otherwise
+  float* d_z = nullptr;    // dL/dz (== d_pre without LayerNorm)
+  float* dw_part = nullptr;
+  int dw_splits = 1;
+  float* ln_part = nullptr;
+  int ln_blocks = 0;
+  // GRU (recurrent torso)
+  int hidden = 0;
+  int64_t wi_off = 0, wh_off = 0, bhn_off = 0;
+  const float* pre() const { return ln ? y : z; }
+};
+
+struct TowerPlan {
+  std::vector<LayerPlan> layers;
+  int in_dim = 0;
+  int out_dim = 0;
+};
+
+struct Comm;  // NCCL communicator (comm.cu)
+
+// Kernel classes of the per-class device-time profile (bt_learner_profile_read).
+enum ProfClass {
+  kProfGae = 0, kProfGemmFwd, kProfGemmDx, kProfGemmDw, kProfHeads, kProfHeadsFwd, kProfLnFwd,
+  kProfLnBwd, kProfReduce, kProfAdam, kProfStats, kProfAllreduce, kProfMisc, kProfNumClasses
+};
+extern const char* const kProfNames[kProfNumClasses];
+
+struct ProfRecord {
+  int cls;
+  cudaEvent_t a, b;
+};
+
+// CUDA-event timing of every launch of the learner, by kernel class (off by default).
+struct Profiler {
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  size_t used = 0;
+  std::vector<ProfRecord> recs;
+  int64_t launches = 0;  // kernels (and collectives) enqueued since creation
+};
+
+struct bt_learner {
+  bt_learner_config cfg{};
+  int device = 0;
+  std::vector<ParamEntryC> entries;
+  int64_t num_params = 0;
+  // state (flat layout)
+  float* params = nullptr;
+  float* grads = nullptr;
+  float* mu = nullptr;
+  float* nu = nullptr;
+  int* count_d = nullptr;   // adam count
+  int* err_d = nullptr;     // device error word
+  int* mb_count_d = nullptr;  // live rows for bt_learner_loss_grads
+  // network
+  TowerPlan towers[2];
+  int ntowers = 1;
+  bool shared = true;
+  int A = 0;
+  int F_pi = 0, F_v = 0;
+  int64_t head_pi_off = 0, head_scale_off = -1, head_v_off = 0;
+  // sizes
+  int T = 0, N = 0;
+  int64_t B = 0;     // T*N on this rank
+  int mb = 0;        // global minibatch size (rows, or envs for recurrent)
+  int rows_cap = 0;  // local minibatch capacity (rows)
+  int act_rows = 0;  // rows of the activation buffers
+  // heads
+  float* d_out = nullptr;
+  float* d_val = nullptr;
+  float* head_pi_part = nullptr;
+  int head_pi_splits = 1;
+  float* head_v_part = nullptr;
+  int head_v_splits = 1;
+  float* dscale_part = nullptr;
+  double* stat_part = nullptr;
+  int heads_blocks = 0;
+  // targets
+  float* adv = nullptr;
+  float* ret = nullptr;
+  float* boot = nullptr;
+  float* act_out = nullptr;  // act: [rows, A] head outputs
+  float* act_val = nullptr;
+  // reductions
+  std::vector<bt::Segment> segs_h;
+  bt::Segment* segs_d = nullptr;
+  double* norm_part = nullptr;
+  double* stat_sums = nullptr;  // [E*M + 1][kNumStatSums]
+  double* adv_part = nullptr;
+  // multi-GPU
+  int* local_idx = nullptr;
+  int* local_counts = nullptr;
+  Comm* comm = nullptr;
+  std::vector<void*> allocations;
+  Profiler prof;
+};
+
+cudaEvent_t prof_event(bt_learner* L);
+
+// Enqueue one kernel (or collective) launch `call`, counting it and, when profiling is
+// on, bracketing it with CUDA events on stream `s`.
+#define BT_K(L, cls, s, call)                                   \
+  do {                                                          \
+    cudaEvent_t a_ = nullptr;                                   \
+    if ((L)->prof.on) {                                         \
+      a_ = prof_event(L);                                       \
+      cudaEventRecord(a_, s);                                   \
+    }                                                           \
+    BT_TRY(call);                                               \
+    (L)->prof.launches++;                                       \
+    if ((L)->prof.on) {                                         \
+      cudaEvent_t b_ = prof_event(L);                           \
+      cudaEventRecord(b_, s);                                   \
+      (L)->prof.recs.push_back({cls, a_, b_});                  \
+    }                                                           \
+  } while (0)
+#define BT_C(L, cls, s, call) BT_K(L, cls, s, call)

@@ -1,0 +1,226 @@
+/*
+ * boonta_b200 — C-ABI of the B200-native PPO learner step.
+ *
+ * This header is the drop-in boundary for boonta's Anakin PPO learner path. Every entry
+ * point takes plain pointers and sizes (device pointers unless stated), an opaque
+ * `void* stream` (a cudaStream_t; NULL = the legacy default stream) and returns an int
+ * status (0 = ok, negative = error, with a message in `bt_last_error()`). Calls only
+ * enqueue work on the given stream and never synchronise the device, which is the stream
+ * contract of an XLA FFI custom call.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   bt_gae                  boonta/algorithms/advantage_estimators.py:8-56
+ *                           (generalized_advantage_estimator, incl. rho/c V-trace weights)
+ *   bt_learner_create       boonta/algorithms/ppo.py:37-55 (PPO(cfg, network, optimizer),
+ *                           PPO.init) and recurrent_ppo.py:37-69 for GRU networks; the
+ *                           network and optimizer are described by value, not as flax /
+ *                           optax objects
+ *   bt_learner_update       boonta/algorithms/ppo.py:76-233 (PPO.update) and
+ *                           recurrent_ppo.py:98-281 (RecurrentPPO.update), including the
+ *                           implicit gradient mean across devices inserted for
+ *                           boonta/podracers/anakin.py:165-186
+ *   bt_learner_act          boonta/algorithms/ppo.py:57-74 (PPO.step) with
+ *                           boonta/networks/distributions.py:21-23 (Gumbel-argmax sample)
+ *   bt_learner_set_state /
+ *   bt_learner_get_state    the PPOState pytree (ppo.py:30-34): params and the optax
+ *                           chain state (clip: empty; adam: count, mu, nu)
+ *   bt_learner_comm_init    the NCCL communicator behind jax.distributed / XLA's
+ *                           all-reduce (hangar/train.py:17-18, anakin.py:165-186)
+ *
+ * The XLA FFI handlers a JAX host would register (jax.ffi.register_ffi_target, the
+ * mechanism of boonta/environments/__init__.py:10-15,38-43) wrap these functions one to
+ * one; INTEGRATION.md shows that binding.
+ */
+#ifndef BOONTA_B200_H_
+#define BOONTA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BT_API __attribute__((visibility("default")))
+#else
+#define BT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------ */
+#define BT_OK 0
+#define BT_ERR_INVALID (-1)     /* bad argument: null pointer, shape, alignment, config */
+#define BT_ERR_CUDA (-2)        /* a CUDA runtime call failed                            */
+#define BT_ERR_NCCL (-3)        /* an NCCL call failed or the communicator is missing     */
+#define BT_ERR_TIMEOUT (-4)     /* a bounded wait gave up                                 */
+#define BT_ERR_CAPACITY (-5)    /* a rank's share of a global minibatch exceeded capacity */
+#define BT_ERR_UNSUPPORTED (-6) /* a network or option this build does not implement      */
+
+/* ---- enums --------------------------------------------------------------------------- */
+#define BT_LAYER_DENSE 0
+#define BT_LAYER_CONV3X3 1 /* flax Conv(features, (3,3), padding="SAME"), NHWC, then flatten */
+#define BT_LAYER_GRU 2     /* flax GRUCell scanned over time, reset to zero on first.done   */
+
+#define BT_ACT_NONE 0
+#define BT_ACT_TANH 1
+#define BT_ACT_RELU 2
+#define BT_ACT_SILU 3
+
+#define BT_HEAD_CATEGORICAL 0 /* distrax Categorical over the logits (distributions.py:8-38) */
+#define BT_HEAD_GAUSSIAN 1    /* MultivariateNormalDiag(mean, softplus(scale) + 1e-3) with a
+                                 learned state-independent scale (distributions.py:49-57)    */
+
+#define BT_PREC_FP32 0   /* fp32 operands, fp32 accumulation (CUDA cores)                 */
+#define BT_PREC_BF16 1   /* bf16 operands, fp32 accumulation (tcgen05 tensor cores)       */
+#define BT_PREC_BF16X3 2 /* fp32 split into bf16 hi + lo, three tcgen05 products          */
+
+#define BT_MAX_LAYERS 8
+#define BT_NUM_STATS 8 /* actor/loss, actor/entropy, actor/approximate_kl,
+                          actor/clip_fraction, actor/advantage, critic/loss,
+                          critic/explained_variance, critic/value (ppo.py:170-179) */
+
+/* ---- configuration -------------------------------------------------------------------- */
+typedef struct bt_layer {
+  int32_t kind;       /* BT_LAYER_*                                          */
+  int32_t features;   /* Dense/GRU output width; Conv3x3 output channels      */
+  int32_t activation; /* BT_ACT_* (Dense, Conv3x3)                           */
+  int32_t layernorm;  /* Dense: 1 = LayerNorm(eps 1e-6) before the activation */
+  int32_t height, width, in_channels; /* Conv3x3 input image (NHWC)          */
+} bt_layer;
+
+typedef struct bt_network {
+  int32_t obs_dim;    /* features per observation row (flattened)               */
+  int32_t num_torso;  /* layers of the shared torso, or of the actor's tower       */
+  bt_layer torso[BT_MAX_LAYERS];
+  int32_t num_critic; /* 0: the torso is shared; else the critic's own tower        */
+  bt_layer critic[BT_MAX_LAYERS];
+  int32_t head;       /* BT_HEAD_*                                               */
+  int32_t action_dim; /* logits (categorical) or mean dimensions (gaussian)       */
+} bt_network;
+
+typedef struct bt_ppo_config { /* boonta/algorithms/ppo.py:17-27 */
+  int32_t num_minibatches;
+  int32_t update_epochs;
+  float clip_coefficient;
+  int32_t clip_value_loss;
+  float entropy_coefficient;
+  float value_coefficient;
+  double gamma;      /* python floats in the reference: gamma*gae_lambda is formed in */
+  double gae_lambda; /* double and rounded once to float32                           */
+  int32_t normalize_advantage;
+} bt_ppo_config;
+
+typedef struct bt_optimizer { /* optax.chain(clip_by_global_norm, adam) */
+  float lr, max_grad_norm, b1, b2, eps, eps_root;
+} bt_optimizer;
+
+typedef struct bt_learner_config {
+  bt_network network;
+  bt_ppo_config ppo;
+  bt_optimizer optimizer;
+  int32_t num_steps; /* T                                  */
+  int32_t num_envs;  /* N envs on this rank                 */
+  int32_t precision; /* BT_PREC_* for the torso GEMMs       */
+  int32_t world_size;/* ranks the env batch is sharded over */
+  int32_t rank;
+} bt_learner_config;
+
+/* One rollout in boonta's Transition layout, leaves [T, N, ...] (utils/transition.py). */
+typedef struct bt_batch {
+  const float* obs;           /* first.obs        [T, N, obs_dim]                     */
+  const float* bootstrap_obs; /* second.obs[T-1]  [N, obs_dim]                        */
+  const void* action;         /* second.action    int32 [T, N] | float [T, N, A]       */
+  const float* reward;        /* second.reward    [T, N]                              */
+  const uint8_t* terminated;  /* second.terminated [T, N] (0/1)                        */
+  const uint8_t* truncated;   /* second.truncated  [T, N] (0/1)                        */
+  const float* log_prob;      /* aux.log_prob     [T, N]                              */
+  const float* value;         /* aux.value        [T, N]                              */
+  const uint8_t* first_done;  /* recurrent: first.done [T, N]                          */
+  const float* carry;         /* recurrent: carry entering step 0   [N, H]             */
+  const float* last_carry;    /* recurrent: carry entering step T-1 [N, H]             */
+} bt_batch;
+
+typedef struct bt_learner bt_learner;
+
+/* ---- error reporting -------------------------------------------------------------------- */
+BT_API const char* bt_last_error(void); /* thread-local message of the last failing call */
+BT_API const char* bt_version(void);
+
+/* ---- GAE (boonta/algorithms/advantage_estimators.py:8-56) ----------------------------------
+ * advantages/returns [T, N] float32; rho and c may be NULL (= 1.0). Device pointers. */
+BT_API int bt_gae(const float* reward, const uint8_t* terminated, const uint8_t* truncated,
+           const float* values, const float* bootstrap, const float* rho, const float* c,
+           int32_t num_steps, int32_t num_envs, double gamma, double gae_lambda,
+           float* advantages, float* returns, void* stream);
+
+/* ---- learner ---------------------------------------------------------------------------- */
+BT_API int bt_learner_create(const bt_learner_config* cfg, bt_learner** out);
+BT_API void bt_learner_destroy(bt_learner* learner);
+
+/* Flat parameter layout (floats). Entries are (name, offset, shape). */
+BT_API int64_t bt_learner_num_params(const bt_learner* learner); /* length of the flat buffer */
+BT_API int32_t bt_learner_param_count(const bt_learner* learner);
+BT_API int bt_learner_param_info(const bt_learner* learner, int32_t index, char* name,
+                          int32_t name_len, int64_t* offset, int32_t* ndim, int64_t* shape);
+
+/* Copy state in/out (device pointers, flat layout; mu/nu/count = optax adam state). */
+BT_API int bt_learner_set_state(bt_learner* learner, const float* params, const float* mu,
+                         const float* nu, int32_t count, void* stream);
+BT_API int bt_learner_get_state(bt_learner* learner, float* params, float* mu, float* nu,
+                         int32_t* count, void* stream);
+
+/* One full learner step. permutations: device int32 [E, T*N*world_size] (or
+ * [E, N*world_size] env permutations for recurrent networks); stats: device float
+ * [E, M, BT_NUM_STATS] or NULL. */
+BT_API int bt_learner_update(bt_learner* learner, const bt_batch* batch, const int32_t* permutations,
+                      float* stats, void* stream);
+
+/* Targets of the last update: advantages/returns [T, N], bootstrap values [N]. */
+BT_API int bt_learner_targets(bt_learner* learner, float* advantages, float* returns,
+                       float* bootstrap, void* stream);
+
+/* Loss gradients of one minibatch without an optimizer step (parity testing):
+ * indices [count] into the flattened rollout; advantages/returns as in the rollout
+ * layout; grads: flat [num_params]; stats: [BT_NUM_STATS]. */
+BT_API int bt_learner_loss_grads(bt_learner* learner, const bt_batch* batch,
+                          const float* advantages, const float* returns,
+                          const int32_t* indices, int32_t count, float* grads, float* stats,
+                          void* stream);
+
+/* Act (PPO.step): obs [num, obs_dim]. Categorical: noise = uniform draws u in (0, 1)
+ * [num, A] (the Gumbel noise is -log(-log(u))), NULL = no noise; temperature 0 = greedy
+ * argmax; action int32 [num]. Gaussian: noise = standard normal draws [num, A],
+ * action float [num, A] = mean + temperature * scale * noise. log_prob [num],
+ * value [num] (nullable). */
+BT_API int bt_learner_act(bt_learner* learner, const float* obs, int32_t num, const float* noise,
+                   float temperature, void* action, float* log_prob, float* value,
+                   void* stream);
+
+/* Categorical sampling alone (boonta/networks/distributions.py:8-23): action =
+ * argmax(log_softmax(logits / temperature) + (-log(-log(u)))), first index on ties; the
+ * noise and log_softmax are evaluated in double and rounded once to float32, so the index
+ * is a deterministic function of (logits, u). logits, uniforms [rows, num_actions]. */
+BT_API int bt_sample_categorical(const float* logits, const float* uniforms, int32_t rows,
+                                 int32_t num_actions, float temperature, int32_t* action,
+                                 float* log_prob, void* stream);
+
+/* ---- tracing ----------------------------------------------------------------------------
+ * The reference profiles with jax.profiler traces (hangar/scripts/profile_boonta.py:25-65);
+ * here every kernel the learner enqueues can be bracketed with CUDA events on its stream.
+ * bt_learner_profile(1) clears and starts recording, (0) stops. profile_read returns, for
+ * kernel class `cls` (0 .. until it returns BT_ERR_INVALID), its name, the summed device
+ * time in ms and the number of launches recorded (it synchronises on the events).
+ * bt_learner_launch_count: kernels and collectives enqueued since creation. */
+BT_API int bt_learner_profile(bt_learner* learner, int32_t enable);
+BT_API int bt_learner_profile_read(bt_learner* learner, int32_t cls, char* name,
+                                   int32_t name_len, double* total_ms, int64_t* launches);
+BT_API int64_t bt_learner_launch_count(const bt_learner* learner);
+
+/* ---- multi-GPU (NCCL over NVLink) -------------------------------------------------------- */
+BT_API int bt_nccl_unique_id(void* out, int32_t size); /* size >= 128 bytes */
+BT_API int bt_learner_comm_init(bt_learner* learner, const void* unique_id, int32_t size);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BOONTA_B200_H_ */
