@@ -35,7 +35,7 @@ EXPORTS = (
     "bt_learner_set_state", "bt_learner_get_state", "bt_learner_update", "bt_learner_targets",
     "bt_learner_loss_grads", "bt_learner_act", "bt_sample_categorical", "bt_nccl_unique_id",
     "bt_learner_comm_init", "bt_learner_profile", "bt_learner_profile_read",
-    "bt_learner_launch_count",
+    "bt_learner_launch_count", "bt_gemm_bf16",
 )
 
 
@@ -128,6 +128,7 @@ def lib() -> C.CDLL:
         "bt_learner_profile_read": (C.c_int, [vp, i32, C.c_char_p, i32, C.POINTER(f64),
                                               C.POINTER(i64)]),
         "bt_learner_launch_count": (i64, [vp]),
+        "bt_gemm_bf16": (C.c_int, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -30,7 +30,7 @@ struct ARows {  // k contiguous
   const int* idx;  // nullable row gather
   int ld;
   int kin;  // k == kin -> 1.0 (bias column); k > kin -> 0
-  __device__ __forceinline__ float load(int m, int k, int M) const {
+  __device__ __forceinline__ float load(int m, int k, int M, int /*K*/) const {
     if (m >= M) return 0.f;
     if (k < kin) {
       const int r = idx ? idx[m] : m;
@@ -46,7 +46,7 @@ struct ACols {  // m contiguous: A(m, k) = src[row(k) * ld + m]
   const int* idx;
   int ld;
   int kin;  // m == kin -> 1.0 (bias row); m > kin -> 0
-  __device__ __forceinline__ float load(int m, int k, int K) const {
+  __device__ __forceinline__ float load(int m, int k, int /*M*/, int K) const {
     if (k >= K) return 0.f;
     if (m < kin) {
       const int r = idx ? idx[k] : k;
@@ -63,7 +63,7 @@ struct AIm2col {
   const float* src;
   const int* idx;
   int H, W, C;
-  __device__ __forceinline__ float load(int m, int k, int M) const {
+  __device__ __forceinline__ float load(int m, int k, int M, int /*K*/) const {
     if (m >= M) return 0.f;
     const int kin = 9 * C;
     if (k >= kin) return k == kin ? 1.f : 0.f;
@@ -81,9 +81,9 @@ struct AIm2col {
 struct AIm2colT {  // A(m, k) = patch value with m the (tap, c) index and k the pixel row
   static constexpr bool kMContig = false;
   AIm2col inner;
-  __device__ __forceinline__ float load(int m, int k, int K) const {
-    if (k >= K) return 0.f;
-    return inner.load(k, m, K);
+  __device__ __forceinline__ float load(int m, int k, int M, int K) const {
+    if (k >= K || m >= M) return 0.f;
+    return inner.load(k, m, K, M);
   }
 };
 
@@ -178,10 +178,10 @@ __global__ void __launch_bounds__(kGemmThreads)
     for (int j = 0; j < 4; ++j) {
       if (AL::kMContig) {
         const int kk = tid >> 5, mm = ((tid & 31) << 2) + j;
-        ra[j] = (k0 + kk < ke) ? a.load(m0 + mm, k0 + kk, ke) : 0.f;
+        ra[j] = (k0 + kk < ke) ? a.load(m0 + mm, k0 + kk, M, ke) : 0.f;
       } else {
         const int mm = tid >> 1, kk = ((tid & 1) << 2) + j;
-        ra[j] = (k0 + kk < ke) ? a.load(m0 + mm, k0 + kk, M) : 0.f;
+        ra[j] = (k0 + kk < ke) ? a.load(m0 + mm, k0 + kk, M, ke) : 0.f;
       }
       if (BL::kNContig) {
         const int kk = tid >> 5, nn = ((tid & 31) << 2) + j;

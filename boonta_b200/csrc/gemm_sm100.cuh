@@ -1,0 +1,386 @@
+// K2 (tensor-core path): tcgen05 GEMM for sm_100a with TMA-staged bf16 operands and the
+// fp32 accumulator in tensor memory, with the learner's epilogues fused.
+//
+//   D[M, N] (fp32, TMEM) = sum_k A[m, k] * B[n, k]       A, B bf16 in shared memory
+//
+// One CTA computes one 128 x BN output tile over a range of K (split-K over gridDim.z):
+//   warp 0      TMA producer: one elected lane loads 64-wide K blocks of A and B into a
+//               ring of shared-memory stages (128-byte swizzle), arming "full" mbarriers;
+//   warp 1      allocates BN TMEM columns; one elected lane issues tcgen05.mma
+//               (kind::f16, M = 128, N = BN, K = 16; four per K block) and frees a stage
+//               with tcgen05.commit on its "empty" mbarrier;
+//   warps 2-5   epilogue: after the final commit, each warp reads its 32-lane quarter of
+//               the accumulator with tcgen05.ld (32 columns at a time) and applies the
+//               fused epilogue (bias + activation + bf16/fp32 stores, activation
+//               derivative, or transposed split-K partial stores).
+// Operands may be K-major (rows of K contiguous) or MN-major (the M/N index contiguous),
+// selected per operand by template flags, so the forward (A K-major, B MN-major), dX
+// (both K-major) and dW^T (both MN-major) contractions all read the row-major activation
+// and weight buffers directly, with no transposed copies.
+//
+// Every mbarrier wait is bounded (ptx.cuh): a wait that gives up records an error code in
+// `err`, the CTA skips the rest of its work, waits (bounded) for its own copies in flight,
+// frees its TMEM and returns.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace bt {
+namespace umma {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle span of bf16
+constexpr int kThreads = 192;
+constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// ---- PTX wrappers ------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), descriptor version 1.
+// K-major: 8-row x 128-byte atoms stacked along M/N, SBO = 1024 B between atoms.
+// MN-major: 8 K-rows x 128 bytes (64 M/N elements) per atom; SBO = 1024 B between K
+// groups; LBO = 8192 B between 64-wide M/N blocks (each block holds the 64 K rows of the
+// stage).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+template <bool kMN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kstep) {
+  if (kMN) return smem_desc(base + kstep * 2048, 8192, 1024);
+  return smem_desc(base + kstep * 32, 16, 1024);
+}
+
+// Instruction descriptor: D fp32, A/B bf16, majors, N >> 3 at bit 17, M >> 4 at bit 24.
+template <int BN, bool A_MN, bool B_MN>
+__device__ __forceinline__ constexpr uint32_t instr_desc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
+         ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+struct GemmShape {
+  int M, N, K;
+  int kblocks_per_split;
+  const int* m_count;  // nullable: live rows bound M (forward / dX)
+  const int* k_count;  // nullable: live rows bound K (dW)
+  int* err;
+};
+
+template <int BN, bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, GemmShape sh, Epi epi) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  __shared__ int s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int M = sh.M, K = sh.K;
+  if (sh.m_count) M = min(M, *sh.m_count);
+  if (sh.k_count) K = min(K, *sh.k_count);
+  const int m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  if (m0 >= M) return;  // whole CTA leaves before any barrier or TMEM use
+  const int kb0 = blockIdx.z * sh.kblocks_per_split;
+  const int kb1 = min(ceil_div(K, BK), kb0 + sh.kblocks_per_split);
+  const int nk = max(0, kb1 - kb0);
+
+  if (threadIdx.x == 0) {
+    s_fail = 0;
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::kStages;
+        if (i >= C::kStages) {
+          if (!mbar_wait_bounded(&empty[s], ((i / C::kStages) - 1) & 1)) {
+            atomicExch(&s_fail, kErrTimeoutEmpty);
+            break;
+          }
+        }
+        if (*(volatile int*)&s_fail) break;
+        uint8_t* sa = smem + s * C::kStageBytes;
+        uint8_t* sb = sa + C::kABytes;
+        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+        const int k0 = (kb0 + i) * BK;
+        if (A_MN) {
+          tma_load_2d(sa, &tma_a, m0, k0, &full[s]);
+          tma_load_2d(sa + 8192, &tma_a, m0 + 64, k0, &full[s]);
+        } else {
+          tma_load_2d(sa, &tma_a, k0, m0, &full[s]);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tma_b, n0 + 64 * j, k0, &full[s]);
+        } else {
+          tma_load_2d(sb, &tma_b, k0, n0, &full[s]);
+        }
+        issued = i + 1;
+      }
+      // Let every copy this CTA issued land before the CTA may leave.
+      for (int i = max(0, issued - C::kStages); i < issued; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) atomicExch(&s_fail, kErrTimeoutFull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc<BN, A_MN, B_MN>();
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) {
+          atomicExch(&s_fail, kErrTimeoutFull);
+          break;
+        }
+        fence_after_sync();
+        const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
+        const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          mma_bf16(tmem, operand_desc<A_MN>(sa, k), operand_desc<B_MN>(sb, k), idesc,
+                   (i > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+      }
+      mma_commit(acc_full);
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    const int q = warp & 3;
+    const bool ok = mbar_wait_bounded(acc_full, 0);
+    if (!ok && lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
+    fence_after_sync();
+    const int row = m0 + q * 32 + lane;
+    const bool have = ok && nk > 0;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      if (n0 + c >= sh.N) break;
+      float v[32];
+      if (have) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+      if (row < M) epi.apply(row, n0 + c, v, blockIdx.z);
+    }
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after_sync();
+    tmem_dealloc(tmem, BN);
+  }
+  if (threadIdx.x == 0 && s_fail && sh.err) atomicExch(sh.err, s_fail);
+}
+
+// ---- epilogues -----------------------------------------------------------------------------
+// Forward: z = acc + bias; writes z (fp32, nullable), h = act(z) as bf16 (nullable) and as
+// fp32 (nullable).
+struct EpiFwd {
+  const float* bias;
+  float* z;
+  int ldz;
+  __nv_bfloat16* hb;
+  int ldhb;
+  float* hf;
+  int ldhf;
+  int act;
+  int N;
+  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int) const {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = col0 + j;
+      if (n >= N) break;
+      const float zz = v[j] + bias[n];
+      if (z) z[(size_t)row * ldz + n] = zz;
+      const float h = act_forward(zz, act);
+      if (hb) hb[(size_t)row * ldhb + n] = __float2bfloat16_rn(h);
+      if (hf) hf[(size_t)row * ldhf + n] = h;
+    }
+  }
+};
+
+// dX of a layer: g = acc * act'(pre) of the previous layer (from its pre-activation alone);
+// writes g as fp32 (LayerNorm previous layer) or bf16 (otherwise).
+struct EpiDx {
+  const float* pre;
+  int ldpre;
+  float* gf;
+  __nv_bfloat16* gb;
+  int ldg;
+  int act;
+  int N;
+  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int) const {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = col0 + j;
+      if (n >= N) break;
+      float g = v[j];
+      if (act != BT_ACT_NONE) {
+        const float z = pre[(size_t)row * ldpre + n];
+        g *= act_grad(z, act == BT_ACT_TANH ? tanhf(z) : 0.f, act);
+      }
+      if (gf) gf[(size_t)row * ldg + n] = g;
+      if (gb) gb[(size_t)row * ldg + n] = __float2bfloat16_rn(g);
+    }
+  }
+};
+
+// dW^T tile: acc[m = output feature][n = input feature (bias row last)] stored transposed
+// into out[split][n][m] (the [K_in + 1, N_out] kernel+bias layout); coalesced across the
+// warp's rows.
+struct EpiDwT {
+  float* out;
+  int ld;  // N_out
+  size_t split_stride;
+  int N;  // K_in + 1
+  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int split) const {
+    float* o = out + (size_t)split * split_stride;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = col0 + j;
+      if (n >= N) break;
+      o[(size_t)n * ld + row] = v[j];
+    }
+  }
+};
+
+// Plain fp32 store of the tile (diagnostics and tests).
+struct EpiStore {
+  float* out;
+  int ld;
+  int N;
+  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int) const {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = col0 + j;
+      if (n >= N) break;
+      out[(size_t)row * ld + n] = v[j];
+    }
+  }
+};
+
+// 2-D bf16 tensor map with 128-byte swizzle: `inner` elements contiguous (row stride
+// `row_bytes`), `outer` rows; box {box_inner, box_outer}.
+int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+
+template <int BN, bool A_MN, bool B_MN, class Epi>
+int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmShape& sh, const Epi& epi,
+                int splits, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  if (sh.M <= 0 || sh.N <= 0) return BT_OK;
+  static bool configured = false;  // per template instance (attribute is per function)
+  if (!configured) {
+    BT_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, A_MN, B_MN, Epi>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    configured = true;
+  }
+  dim3 grid(ceil_div(sh.M, BM), ceil_div(sh.N, BN), max(1, splits));
+  umma_gemm_kernel<BN, A_MN, B_MN, Epi><<<grid, kThreads, C::kSmem, stream>>>(a, b, sh, epi);
+  BT_LAUNCH_CHECK("umma_gemm_kernel");
+  return BT_OK;
+}
+
+}  // namespace umma
+}  // namespace bt

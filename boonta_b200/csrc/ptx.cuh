@@ -51,14 +51,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase. Returns false if the phase did not complete within
-// `max_polls` polls (each try_wait itself suspends for a hardware-defined interval).
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase: gives up (returns false) once `limit_ns` of wall time
+// has passed (default 2 s) — far beyond any legitimate wait in these kernels.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint32_t max_polls = (1u << 22)) {
-  for (uint32_t i = 0; i < max_polls; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+                                                  uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
-  return false;
 }
 
 // 1-D bulk copy global -> shared through the TMA engine, completing on `bar`.

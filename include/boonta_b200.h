@@ -204,6 +204,15 @@ BT_API int bt_sample_categorical(const float* logits, const float* uniforms, int
                                  int32_t num_actions, float temperature, int32_t* action,
                                  float* log_prob, void* stream);
 
+/* ---- diagnostics ---------------------------------------------------------------------------
+ * One tcgen05 tensor-core GEMM, D[M, N] (fp32, row-major) = sum_k A(m, k) B(n, k), bf16
+ * operands: A is [M, K] row-major (a_mn = 0) or [K, M] row-major (a_mn = 1); B is [N, K]
+ * (b_mn = 0) or [K, N] (b_mn = 1). Contiguous extents must be multiples of 8. The learner
+ * runs the same kernel with fused epilogues; this entry point lets tests check the operand
+ * layouts against a reference product. `splits`/`partial` are reserved (pass 1 / NULL). */
+BT_API int bt_gemm_bf16(const void* A, const void* B, float* D, int32_t M, int32_t N, int32_t K,
+                        int32_t a_mn, int32_t b_mn, int32_t splits, float* partial, void* stream);
+
 /* ---- tracing ----------------------------------------------------------------------------
  * The reference profiles with jax.profiler traces (hangar/scripts/profile_boonta.py:25-65);
  * here every kernel the learner enqueues can be bracketed with CUDA events on its stream.
