@@ -54,33 +54,65 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t oute
 
 using namespace bt;
 
+namespace {
+
+int make_operand_maps(const void* A, const void* B, int M, int N, int K, int a_mn, int b_mn,
+                      CUtensorMap* ta, CUtensorMap* tb) {
+  if (a_mn) {
+    BT_TRY(umma::encode_map(ta, A, M, K, (uint64_t)M * 2, 64, 64));
+  } else {
+    BT_TRY(umma::encode_map(ta, A, K, M, (uint64_t)K * 2, 64, 128));
+  }
+  if (b_mn) {
+    BT_TRY(umma::encode_map(tb, B, N, K, (uint64_t)N * 2, 64, 64));
+  } else {
+    BT_TRY(umma::encode_map(tb, B, K, N, (uint64_t)K * 2, 64, 128));
+  }
+  return BT_OK;
+}
+
+template <bool X3>
+int run_debug_gemm(const umma::Operands& ops, int M, int N, int K, int a_mn, int b_mn, float* D,
+                   cudaStream_t s) {
+  umma::GemmShape sh{M, N, K, ceil_div(K, umma::BK), nullptr, nullptr, nullptr};
+  umma::EpiStore ep{D, N};
+  if (a_mn && b_mn) return umma::launch_gemm<128, true, true, X3>(ops, sh, ep, 1, s);
+  if (a_mn) return umma::launch_gemm<128, true, false, X3>(ops, sh, ep, 1, s);
+  if (b_mn) return umma::launch_gemm<128, false, true, X3>(ops, sh, ep, 1, s);
+  return umma::launch_gemm<128, false, false, X3>(ops, sh, ep, 1, s);
+}
+
+}  // namespace
+
 // D[M, N] = sum_k A(m, k) B(n, k). A is [M, K] row-major (a_mn = 0) or [K, M] row-major
 // (a_mn = 1); B is [N, K] (b_mn = 0) or [K, N] (b_mn = 1). bf16 in, fp32 out.
 extern "C" int bt_gemm_bf16(const void* A, const void* B, float* D, int32_t M, int32_t N,
                             int32_t K, int32_t a_mn, int32_t b_mn, int32_t splits, float* partial,
                             void* stream) {
+  (void)splits;
+  (void)partial;
   BT_CHECK_ARG(A && B && D, "bt_gemm_bf16: null pointer");
   BT_CHECK_ARG(M > 0 && N > 0 && K > 0, "bt_gemm_bf16: bad shape");
   BT_CHECK_ARG(K % 8 == 0 && (a_mn ? M % 8 == 0 : true) && (b_mn ? N % 8 == 0 : true),
                "bt_gemm_bf16: contiguous extents must be multiples of 8");
-  cudaStream_t s = (cudaStream_t)stream;
-  CUtensorMap ta, tb;
-  if (a_mn) {
-    BT_TRY(umma::encode_map(&ta, A, M, K, (uint64_t)M * 2, 64, 64));
-  } else {
-    BT_TRY(umma::encode_map(&ta, A, K, M, (uint64_t)K * 2, 64, 128));
-  }
-  constexpr int BN = 128;
-  if (b_mn) {
-    BT_TRY(umma::encode_map(&tb, B, N, K, (uint64_t)N * 2, 64, 64));
-  } else {
-    BT_TRY(umma::encode_map(&tb, B, K, N, (uint64_t)K * 2, 64, BN));
-  }
-  umma::GemmShape sh{M, N, K, ceil_div(ceil_div(K, umma::BK), max(1, splits)), nullptr, nullptr,
-                     nullptr};
-  umma::EpiStore ep{D, N, N};
-  if (a_mn && b_mn) return umma::launch_gemm<BN, true, true>(ta, tb, sh, ep, 1, s);
-  if (a_mn) return umma::launch_gemm<BN, true, false>(ta, tb, sh, ep, 1, s);
-  if (b_mn) return umma::launch_gemm<BN, false, true>(ta, tb, sh, ep, 1, s);
-  return umma::launch_gemm<BN, false, false>(ta, tb, sh, ep, 1, s);
+  umma::Operands ops;
+  BT_TRY(make_operand_maps(A, B, M, N, K, a_mn, b_mn, &ops.a, &ops.b));
+  ops.a_lo = ops.a;
+  ops.b_lo = ops.b;
+  return run_debug_gemm<false>(ops, M, N, K, a_mn, b_mn, D, (cudaStream_t)stream);
+}
+
+// The split-precision variant: A = A_hi + A_lo, B = B_hi + B_lo (bf16 pairs), D = A_hi B_hi
+// + A_hi B_lo + A_lo B_hi.
+extern "C" int bt_gemm_bf16x3(const void* A_hi, const void* A_lo, const void* B_hi,
+                              const void* B_lo, float* D, int32_t M, int32_t N, int32_t K,
+                              int32_t a_mn, int32_t b_mn, void* stream) {
+  BT_CHECK_ARG(A_hi && A_lo && B_hi && B_lo && D, "bt_gemm_bf16x3: null pointer");
+  BT_CHECK_ARG(M > 0 && N > 0 && K > 0, "bt_gemm_bf16x3: bad shape");
+  BT_CHECK_ARG(K % 8 == 0 && (a_mn ? M % 8 == 0 : true) && (b_mn ? N % 8 == 0 : true),
+               "bt_gemm_bf16x3: contiguous extents must be multiples of 8");
+  umma::Operands ops;
+  BT_TRY(make_operand_maps(A_hi, B_hi, M, N, K, a_mn, b_mn, &ops.a, &ops.b));
+  BT_TRY(make_operand_maps(A_lo, B_lo, M, N, K, a_mn, b_mn, &ops.a_lo, &ops.b_lo));
+  return run_debug_gemm<true>(ops, M, N, K, a_mn, b_mn, D, (cudaStream_t)stream);
 }

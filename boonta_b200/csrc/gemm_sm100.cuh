@@ -9,10 +9,11 @@
 //   warp 1      allocates BN TMEM columns; one elected lane issues tcgen05.mma
 //               (kind::f16, M = 128, N = BN, K = 16; four per K block) and frees a stage
 //               with tcgen05.commit on its "empty" mbarrier;
-//   warps 2-5   epilogue: after the final commit, each warp reads its 32-lane quarter of
-//               the accumulator with tcgen05.ld (32 columns at a time) and applies the
-//               fused epilogue (bias + activation + bf16/fp32 stores, activation
-//               derivative, or transposed split-K partial stores).
+//   warps 2-9   epilogue: after the final commit, each warp reads its 32-lane quarter of
+//               the accumulator (two warps per quarter, each on half of the columns) with
+//               tcgen05.ld (32 columns at a time) and applies the fused epilogue (bias +
+//               activation + bf16/fp32 stores, activation derivative, or transposed
+//               split-K partial stores).
 // Operands may be K-major (rows of K contiguous) or MN-major (the M/N index contiguous),
 // selected per operand by template flags, so the forward (A K-major, B MN-major), dX
 // (both K-major) and dW^T (both MN-major) contractions all read the row-major activation
@@ -33,15 +34,24 @@ namespace umma {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle span of bf16
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each on half the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13;
 
-template <int BN>
+// Shared-memory budget: a ring of stages of A (and, in the split mode, A_lo) and B (B_lo)
+// tiles, each stage 1024-byte aligned. The ring is sized so that two to three CTAs fit on
+// an SM (about 72 KB each): one CTA's epilogue then overlaps the others' main loops, which
+// matters for the learner's short-K GEMMs (K = 87..512); for long K the co-resident CTAs
+// keep enough TMA loads in flight.
+// kDeep: a long-K GEMM (the dW contractions over the minibatch rows, about one CTA per
+// SM) gets a deep ring of up to 200 KB instead, to keep enough TMA loads in flight.
+template <int BN, bool X3, bool kDeep = false>
 struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kStageBytes = (kABytes + kBBytes) * (X3 ? 2 : 1);
+  static constexpr int kFit = ((kDeep ? 200 : 72) * 1024) / kStageBytes;
+  static constexpr int kStages = kFit < 2 ? 2 : (kFit > 6 ? 6 : kFit);
   static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -146,11 +156,16 @@ struct GemmShape {
   int* err;
 };
 
-template <int BN, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
-    umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, GemmShape sh, Epi epi) {
-  using C = Cfg<BN>;
+// Tensor maps of the operands; a_lo / b_lo are the low bf16 halves of split fp32 operands
+// (X3 mode: x = hi + lo, the product taken as hi*hi + hi*lo + lo*hi).
+struct Operands {
+  CUtensorMap a, b, a_lo, b_lo;
+};
+
+template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
+__global__ void __launch_bounds__(kThreads)
+    umma_gemm_kernel(const __grid_constant__ Operands ops, GemmShape sh, Epi epi) {
+  using C = Cfg<BN, X3, Epi::kDeep>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -186,6 +201,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  // stage layout: A | B | (A_lo | B_lo)
+  auto load_a = [&](uint8_t* dst, const CUtensorMap* map, int k0, uint64_t* bar) {
+    if (A_MN) {
+      tma_load_2d(dst, map, m0, k0, bar);
+      tma_load_2d(dst + 8192, map, m0 + 64, k0, bar);
+    } else {
+      tma_load_2d(dst, map, k0, m0, bar);
+    }
+  };
+  auto load_b = [&](uint8_t* dst, const CUtensorMap* map, int k0, uint64_t* bar) {
+    if (B_MN) {
+#pragma unroll
+      for (int j = 0; j < BN / 64; ++j) tma_load_2d(dst + j * 8192, map, n0 + 64 * j, k0, bar);
+    } else {
+      tma_load_2d(dst, map, k0, n0, bar);
+    }
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
@@ -202,17 +235,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sb = sa + C::kABytes;
         mbar_arrive_expect_tx(&full[s], C::kStageBytes);
         const int k0 = (kb0 + i) * BK;
-        if (A_MN) {
-          tma_load_2d(sa, &tma_a, m0, k0, &full[s]);
-          tma_load_2d(sa + 8192, &tma_a, m0 + 64, k0, &full[s]);
-        } else {
-          tma_load_2d(sa, &tma_a, k0, m0, &full[s]);
-        }
-        if (B_MN) {
-#pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tma_b, n0 + 64 * j, k0, &full[s]);
-        } else {
-          tma_load_2d(sb, &tma_b, k0, n0, &full[s]);
+        load_a(sa, &ops.a, k0, &full[s]);
+        load_b(sb, &ops.b, k0, &full[s]);
+        if (X3) {
+          load_a(sb + C::kBBytes, &ops.a_lo, k0, &full[s]);
+          load_b(sb + C::kBBytes + C::kABytes, &ops.b_lo, k0, &full[s]);
         }
         issued = i + 1;
       }
@@ -234,25 +261,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after_sync();
         const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
         const uint32_t sb = sa + C::kABytes;
+        const uint32_t sa_lo = sb + C::kBBytes;
+        const uint32_t sb_lo = sa_lo + C::kABytes;
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
-          mma_bf16(tmem, operand_desc<A_MN>(sa, k), operand_desc<B_MN>(sb, k), idesc,
-                   (i > 0 || k > 0) ? 1u : 0u);
+          const uint64_t ah = operand_desc<A_MN>(sa, k), bh = operand_desc<B_MN>(sb, k);
+          if (X3) {
+            // small cross terms first, then the leading product
+            mma_bf16(tmem, operand_desc<A_MN>(sa_lo, k), bh, idesc, (i > 0 || k > 0) ? 1u : 0u);
+            mma_bf16(tmem, ah, operand_desc<B_MN>(sb_lo, k), idesc, 1u);
+            mma_bf16(tmem, ah, bh, idesc, 1u);
+          } else {
+            mma_bf16(tmem, ah, bh, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          }
         }
         mma_commit(&empty[s]);
       }
       mma_commit(acc_full);
     }
   } else {
-    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    // Epilogue warps 2..9: TMEM lane quarter = warp % 4 (the hardware's access rule), column
+    // half = (warp - 2) / 4. After the final commit the stage ring is idle, so each warp
+    // stages 32 x 32 chunks through its own piece of it to turn the row-per-thread
+    // accumulator layout into row-contiguous (coalesced) stores.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    float* scr = reinterpret_cast<float*>(smem) + (warp - 2) * (32 * 33);
     const bool ok = mbar_wait_bounded(acc_full, 0);
     if (!ok && lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
     fence_after_sync();
     const int row = m0 + q * 32 + lane;
     const bool have = ok && nk > 0;
+    constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = half * kHalf; c < (half + 1) * kHalf && c < BN; c += 32) {
       if (n0 + c >= sh.N) break;
       float v[32];
       if (have) {
@@ -261,7 +303,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = 0.f;
       }
-      if (row < M) epi.apply(row, n0 + c, v, blockIdx.z);
+      if constexpr (Epi::kStaged) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) scr[lane * 33 + j] = v[j];
+        __syncwarp();
+        float col_v[32];
+#pragma unroll
+        for (int r = 0; r < 32; ++r) col_v[r] = scr[r * 33 + lane];
+        __syncwarp();
+        const int col = n0 + c + lane;
+        const int row0 = m0 + q * 32;
+        if (col < sh.N) epi.apply_col(row0, min(32, M - row0), col, col_v);
+      } else {
+        if (row < M) epi.apply(row, n0 + c, v, blockIdx.z);
+      }
     }
   }
   fence_before_sync();
@@ -273,55 +328,89 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && s_fail && sh.err) atomicExch(sh.err, s_fail);
 }
 
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+  hi = __float2bfloat16_rn(x);
+  lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+
 // ---- epilogues -----------------------------------------------------------------------------
-// Forward: z = acc + bias; writes z (fp32, nullable), h = act(z) as bf16 (nullable) and as
-// fp32 (nullable).
+// Staged epilogues (kStaged) see one element at a time with consecutive lanes on
+// consecutive columns; unstaged ones see a thread's 32 consecutive columns of one row.
+
+// Forward: z = acc + bias; writes z (fp32, nullable), h = act(z) as bf16 (split into
+// hi/lo when hb_lo is set) and as fp32 (nullable). apply_col: one column, rows
+// [row0, row0 + nrows), consecutive lanes on consecutive columns (coalesced).
 struct EpiFwd {
+  static constexpr bool kStaged = true;
+  static constexpr bool kDeep = false;
   const float* bias;
   float* z;
   int ldz;
   __nv_bfloat16* hb;
+  __nv_bfloat16* hb_lo;
   int ldhb;
   float* hf;
   int ldhf;
   int act;
-  int N;
-  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int) const {
+  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
+    const float b = bias[col];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = col0 + j;
-      if (n >= N) break;
-      const float zz = v[j] + bias[n];
-      if (z) z[(size_t)row * ldz + n] = zz;
+    for (int r = 0; r < 32; ++r) {
+      if (r >= nrows) break;
+      const size_t row = (size_t)(row0 + r);
+      const float zz = v[r] + b;
+      if (z) z[row * ldz + col] = zz;
       const float h = act_forward(zz, act);
-      if (hb) hb[(size_t)row * ldhb + n] = __float2bfloat16_rn(h);
-      if (hf) hf[(size_t)row * ldhf + n] = h;
+      if (hb) {
+        if (hb_lo) {
+          split_bf16(h, hb[row * ldhb + col], hb_lo[row * ldhb + col]);
+        } else {
+          hb[row * ldhb + col] = __float2bfloat16_rn(h);
+        }
+      }
+      if (hf) hf[row * ldhf + col] = h;
     }
   }
 };
 
 // dX of a layer: g = acc * act'(pre) of the previous layer (from its pre-activation alone);
-// writes g as fp32 (LayerNorm previous layer) or bf16 (otherwise).
+// writes g as fp32 (LayerNorm previous layer) or bf16 (hi/lo when gb_lo is set). All 32
+// pre-activations of the column are loaded before any store, so each lane keeps 32 loads
+// in flight.
 struct EpiDx {
+  static constexpr bool kStaged = true;
+  static constexpr bool kDeep = false;
   const float* pre;
   int ldpre;
   float* gf;
   __nv_bfloat16* gb;
+  __nv_bfloat16* gb_lo;
   int ldg;
   int act;
-  int N;
-  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int) const {
+  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
+    float zr[32];
+    if (act != BT_ACT_NONE) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = col0 + j;
-      if (n >= N) break;
-      float g = v[j];
+      for (int r = 0; r < 32; ++r)
+        zr[r] = r < nrows ? __ldg(pre + (size_t)(row0 + r) * ldpre + col) : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      if (r >= nrows) break;
+      const size_t row = (size_t)(row0 + r);
+      float g = v[r];
       if (act != BT_ACT_NONE) {
-        const float z = pre[(size_t)row * ldpre + n];
+        const float z = zr[r];
         g *= act_grad(z, act == BT_ACT_TANH ? tanhf(z) : 0.f, act);
       }
-      if (gf) gf[(size_t)row * ldg + n] = g;
-      if (gb) gb[(size_t)row * ldg + n] = __float2bfloat16_rn(g);
+      if (gf) gf[row * ldg + col] = g;
+      if (gb) {
+        if (gb_lo) {
+          split_bf16(g, gb[row * ldg + col], gb_lo[row * ldg + col]);
+        } else {
+          gb[row * ldg + col] = __float2bfloat16_rn(g);
+        }
+      }
     }
   }
 };
@@ -330,6 +419,8 @@ struct EpiDx {
 // into out[split][n][m] (the [K_in + 1, N_out] kernel+bias layout); coalesced across the
 // warp's rows.
 struct EpiDwT {
+  static constexpr bool kStaged = false;
+  static constexpr bool kDeep = true;
   float* out;
   int ld;  // N_out
   size_t split_stride;
@@ -347,16 +438,14 @@ struct EpiDwT {
 
 // Plain fp32 store of the tile (diagnostics and tests).
 struct EpiStore {
+  static constexpr bool kStaged = true;
+  static constexpr bool kDeep = false;
   float* out;
   int ld;
-  int N;
-  __device__ __forceinline__ void apply(int row, int col0, const float (&v)[32], int) const {
+  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = col0 + j;
-      if (n >= N) break;
-      out[(size_t)row * ld + n] = v[j];
-    }
+    for (int r = 0; r < 32; ++r)
+      if (r < nrows) out[(size_t)(row0 + r) * ld + col] = v[r];
   }
 };
 
@@ -365,19 +454,19 @@ struct EpiStore {
 int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
 
-template <int BN, bool A_MN, bool B_MN, class Epi>
-int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmShape& sh, const Epi& epi,
-                int splits, cudaStream_t stream) {
-  using C = Cfg<BN>;
+template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
+int launch_gemm(const Operands& ops, const GemmShape& sh, const Epi& epi, int splits,
+                cudaStream_t stream) {
+  using C = Cfg<BN, X3, Epi::kDeep>;
   if (sh.M <= 0 || sh.N <= 0) return BT_OK;
   static bool configured = false;  // per template instance (attribute is per function)
   if (!configured) {
-    BT_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, A_MN, B_MN, Epi>,
+    BT_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, A_MN, B_MN, X3, Epi>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
     configured = true;
   }
   dim3 grid(ceil_div(sh.M, BM), ceil_div(sh.N, BN), max(1, splits));
-  umma_gemm_kernel<BN, A_MN, B_MN, Epi><<<grid, kThreads, C::kSmem, stream>>>(a, b, sh, epi);
+  umma_gemm_kernel<BN, A_MN, B_MN, X3, Epi><<<grid, kThreads, C::kSmem, stream>>>(ops, sh, epi);
   BT_LAUNCH_CHECK("umma_gemm_kernel");
   return BT_OK;
 }

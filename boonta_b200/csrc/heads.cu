@@ -18,276 +18,307 @@
 
 namespace bt {
 
-constexpr int kHeadRows = 32;
 constexpr int kHeadThreads = 256;
+constexpr int kHeadWarps = kHeadThreads / 32;
+constexpr int kMaxChunks = 4;  // float4 chunks per lane: feature widths up to 512
 constexpr float kLog2Pi = 1.8378770664093453f;
 
-__host__ __device__ inline int head_stride(int f) { return ((f + 31) / 32) * 32 + 1; }
-
-size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared) {
-  const int sp = head_stride(F_pi), sv = head_stride(F_v);
-  size_t floats = 0;
-  floats += (size_t)(A + (shared ? 1 : 0)) * sp;  // wT (actor rows + critic row if shared)
-  floats += shared ? 0 : (size_t)sv;              // critic row of a separate tower
-  floats += (size_t)kHeadRows * sp;               // f_pi tile
-  floats += shared ? 0 : (size_t)kHeadRows * sv;  // f_v tile
-  floats += 2 * (size_t)kHeadRows * (A + 1);      // out_s, dout_s
-  floats += 3 * (size_t)A;                        // sigma, 1/sigma, log sigma
-  floats += (size_t)(kHeadThreads / 32) * (A + kNumStatSums * 2);  // per-warp reductions
-  return floats * 4 + 64;
+// Shared memory: transposed head kernels wT[j][k] (actor rows j < A, then the critic row),
+// the biases, per-warp head outputs / output gradients, gaussian constants, reductions.
+size_t heads_smem_bytes(int F_pi, int F_v, int A, bool /*shared*/) {
+  size_t floats = (size_t)A * F_pi + F_v + (A + 1);  // wT, wTv, biases
+  floats += 2 * (size_t)kHeadWarps * (A + 1);         // out / dout per warp
+  floats += 3 * (size_t)A;                            // sigma, 1/sigma, log sigma
+  floats += (size_t)kHeadWarps * A;                   // dscale reduction
+  return floats * 4 + (size_t)kHeadWarps * kNumStatSums * 8 + 64;
 }
 
+__device__ __forceinline__ void load_row(const float* src, int F, int lane, float4 (&v)[kMaxChunks]) {
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int q = lane + 32 * i;
+    v[i] = (4 * q < F) ? __ldg(reinterpret_cast<const float4*>(src) + q) : make_float4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ float dot_row(const float4 (&f)[kMaxChunks], const float* w, int F,
+                                         int lane) {
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int q = lane + 32 * i;
+    if (4 * q < F) {
+      const float4 ww = reinterpret_cast<const float4*>(w)[q];
+      acc = fmaf(f[i].x, ww.x, acc);
+      acc = fmaf(f[i].y, ww.y, acc);
+      acc = fmaf(f[i].z, ww.z, acc);
+      acc = fmaf(f[i].w, ww.w, acc);
+    }
+  }
+  return warp_sum(acc);
+}
+
+// dL/d f for the lane's chunks, times the tower's last activation derivative, stored as
+// fp32 or bf16 (hi/lo) at row `row`.
+__device__ __forceinline__ void store_df(float4 g, const float4& pre, int act, size_t base, int q,
+                                         float* df, __nv_bfloat16* dfb, __nv_bfloat16* dfb_lo) {
+  if (act != BT_ACT_NONE) {
+    g.x *= act_grad(pre.x, act == BT_ACT_TANH ? tanhf(pre.x) : 0.f, act);
+    g.y *= act_grad(pre.y, act == BT_ACT_TANH ? tanhf(pre.y) : 0.f, act);
+    g.z *= act_grad(pre.z, act == BT_ACT_TANH ? tanhf(pre.z) : 0.f, act);
+    g.w *= act_grad(pre.w, act == BT_ACT_TANH ? tanhf(pre.w) : 0.f, act);
+  }
+  const size_t i = base + 4 * (size_t)q;
+  if (dfb) {
+    store_bf16(dfb, dfb_lo, i, g.x);
+    store_bf16(dfb, dfb_lo, i + 1, g.y);
+    store_bf16(dfb, dfb_lo, i + 2, g.z);
+    store_bf16(dfb, dfb_lo, i + 3, g.w);
+  } else {
+    *reinterpret_cast<float4*>(df + i) = g;
+  }
+}
+
+// One warp per row (grid-stride over the minibatch rows). All loads of a row — the
+// features of both towers and the pre-activations behind the activation derivative — are
+// issued together as float4s before any arithmetic.
 __global__ void __launch_bounds__(kHeadThreads) heads_loss_kernel(HeadsParams p) {
   extern __shared__ __align__(16) float sm[];
   const int A = p.A;
   const bool shared = (p.f_v == p.f_pi);
-  const int sp = head_stride(p.F_pi), sv = head_stride(p.F_v);
-  float* wT = sm;                                                    // [A(+1)][sp]
-  float* wTv = shared ? wT + (size_t)A * sp : wT + (size_t)A * sp;   // critic row
-  float* f_s = wT + (size_t)(A + (shared ? 1 : 0)) * sp + (shared ? 0 : sv);
-  float* fv_s = shared ? f_s : f_s + (size_t)kHeadRows * sp;
-  float* out_s = fv_s + (shared ? (size_t)kHeadRows * sp : (size_t)kHeadRows * sv);
-  float* dout_s = out_s + kHeadRows * (A + 1);
-  float* sig_s = dout_s + kHeadRows * (A + 1);
+  const int F = p.F_pi, Fv = p.F_v;
+  float* wT = sm;                          // [A][F]
+  float* wTv = wT + (size_t)A * F;         // [Fv]
+  float* bias = wTv + Fv;                  // [A + 1] (actor biases, critic bias)
+  float* out_s = bias + (A + 1);           // [warps][A + 1]
+  float* dout_s = out_s + kHeadWarps * (A + 1);
+  float* sig_s = dout_s + kHeadWarps * (A + 1);
   float* isig_s = sig_s + A;
   float* lsig_s = isig_s + A;
-  float* red_s = lsig_s + A;  // [8 warps][A] dscale, then doubles for stats
+  float* red_s = lsig_s + A;               // [warps][A]
   double* stat_s = reinterpret_cast<double*>(
-      (reinterpret_cast<uintptr_t>(red_s + (kHeadThreads / 32) * A) + 7) & ~uintptr_t(7));
+      (reinterpret_cast<uintptr_t>(red_s + kHeadWarps * A) + 7) & ~uintptr_t(7));
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int F = p.F_pi, Fv = p.F_v;
   const int live = live_rows(p.count, p.rows);
+  // the critic's pre-activations: the actor's when the torso is shared
+  const float* pre_v = shared ? p.pre_pi : p.pre_v;
 
-  // Stage transposed head kernels (bias in column F).
-  for (int i = tid; i < (F + 1) * A; i += kHeadThreads) {
+  for (int i = tid; i < F * A; i += kHeadThreads) {
     const int k = i / A, j = i - k * A;
-    wT[(size_t)j * sp + k] = p.w_pi[i];
+    wT[(size_t)j * F + k] = p.w_pi[i];
   }
-  for (int k = tid; k < Fv + 1; k += kHeadThreads) wTv[k] = p.w_v[k];
+  for (int k = tid; k < Fv; k += kHeadThreads) wTv[k] = p.w_v[k];
+  for (int j = tid; j < A; j += kHeadThreads) bias[j] = p.w_pi[(size_t)F * A + j];
+  if (tid == 0) bias[A] = p.w_v[Fv];
   if (p.head == BT_HEAD_GAUSSIAN) {
     for (int j = tid; j < A; j += kHeadThreads) {
       const float s = p.scale[j];
-      const float sp_ = fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)));  // softplus
-      const float sig = sp_ + 1e-3f;
+      const float sig = (fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)))) + 1e-3f;  // softplus + 1e-3
       sig_s[j] = sig;
       isig_s[j] = 1.f / sig;
       lsig_s[j] = logf(sig);
     }
   }
+  __syncthreads();
 
   double st[kNumStatSums];
 #pragma unroll
   for (int s = 0; s < kNumStatSums; ++s) st[s] = 0.0;
   float dscale_acc[2] = {0.f, 0.f};  // lanes own j = lane, lane + 32
+  float* o = out_s + warp * (A + 1);
+  float* d = dout_s + warp * (A + 1);
 
-  const int num_tiles = ceil_div(live, kHeadRows);
-  for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-    const int r0 = tile * kHeadRows;
-    __syncthreads();  // previous tile done with f_s / out_s / dout_s (and staging done)
-    for (int i = tid; i < kHeadRows * F; i += kHeadThreads) {
-      const int r = i / F, k = i - r * F;
-      f_s[(size_t)r * sp + k] = (r0 + r < live) ? p.f_pi[(size_t)(r0 + r) * F + k] : 0.f;
+  for (int row = blockIdx.x * kHeadWarps + warp; row < live; row += gridDim.x * kHeadWarps) {
+    const int flat = p.idx ? p.idx[row] : row;
+    float4 f[kMaxChunks], fv[kMaxChunks], zp[kMaxChunks], zv[kMaxChunks];
+    load_row(p.f_pi + (size_t)row * F, F, lane, f);
+    if (!shared) load_row(p.f_v + (size_t)row * Fv, Fv, lane, fv);
+    if (p.act_pi != BT_ACT_NONE) load_row(p.pre_pi + (size_t)row * F, F, lane, zp);
+    if (!shared && p.act_v != BT_ACT_NONE) load_row(pre_v + (size_t)row * Fv, Fv, lane, zv);
+    const float lp_old = p.lp_old[flat];
+    const float adv = p.adv[flat];
+    const float ret = p.ret[flat];
+    const float v_old = p.v_old[flat];
+    int action = 0;
+    if (p.head == BT_HEAD_CATEGORICAL) action = reinterpret_cast<const int*>(p.action)[flat];
+    float act_j[2] = {0.f, 0.f};
+    if (p.head == BT_HEAD_GAUSSIAN) {
+      const float* av = reinterpret_cast<const float*>(p.action) + (size_t)flat * A;
+      if (lane < A) act_j[0] = av[lane];
+      if (lane + 32 < A) act_j[1] = av[lane + 32];
     }
-    if (!shared) {
-      for (int i = tid; i < kHeadRows * Fv; i += kHeadThreads) {
-        const int r = i / Fv, k = i - r * Fv;
-        fv_s[(size_t)r * sv + k] = (r0 + r < live) ? p.f_v[(size_t)(r0 + r) * Fv + k] : 0.f;
-      }
+    // Head outputs.
+    for (int j = 0; j < A; ++j) {
+      const float t = dot_row(f, wT + (size_t)j * F, F, lane);
+      if (lane == 0) o[j] = t + bias[j];
     }
-    __syncthreads();
-    // Head outputs: out_s[r][j], j < A actor, j == A critic value.
-    for (int o = tid; o < kHeadRows * (A + 1); o += kHeadThreads) {
-      const int r = o / (A + 1), j = o - r * (A + 1);
-      float acc;
-      if (j < A) {
-        const float* w = wT + (size_t)j * sp;
-        const float* f = f_s + (size_t)r * sp;
-        acc = w[F];
-        for (int k = 0; k < F; ++k) acc = fmaf(f[k], w[k], acc);
-      } else {
-        const float* f = fv_s + (size_t)r * (shared ? sp : sv);
-        acc = wTv[Fv];
-        for (int k = 0; k < Fv; ++k) acc = fmaf(f[k], wTv[k], acc);
-      }
-      out_s[r * (A + 1) + j] = acc;
+    {
+      const float t = shared ? dot_row(f, wTv, F, lane) : dot_row(fv, wTv, Fv, lane);
+      if (lane == 0) o[A] = t + bias[A];
     }
-    __syncthreads();
-    // Loss and its gradient, one warp per row.
-    for (int r = warp; r < kHeadRows; r += kHeadThreads / 32) {
-      const int row = r0 + r;
-      float* o = out_s + r * (A + 1);
-      float* d = dout_s + r * (A + 1);
-      if (row >= live) {
-        for (int j = lane; j <= A; j += 32) d[j] = 0.f;
-        continue;
-      }
-      const int flat = p.idx ? p.idx[row] : row;
-      const float lp_old = p.lp_old[flat];
-      const float adv = p.adv[flat];
-      const float ret = p.ret[flat];
-      const float v_old = p.v_old[flat];
-      const float value = o[A];
-      float lp, ent;
-      // per-lane pieces for the gradient
-      float pj[2] = {0.f, 0.f}, lpj[2] = {0.f, 0.f}, zj[2] = {0.f, 0.f};
-      int action = 0;
-      if (p.head == BT_HEAD_CATEGORICAL) {
-        action = reinterpret_cast<const int*>(p.action)[flat];
-        float mx = -INFINITY;
-        for (int j = lane; j < A; j += 32) mx = fmaxf(mx, o[j]);
-        mx = warp_max(mx);
-        float se = 0.f;
-        for (int j = lane; j < A; j += 32) se += expf(o[j] - mx);
-        se = warp_sum(se);
-        const float lse = logf(se);
-        float h = 0.f;
+    __syncwarp();
+    const float value = o[A];
+    float lp, ent;
+    float pj[2] = {0.f, 0.f}, lpj[2] = {0.f, 0.f}, zj[2] = {0.f, 0.f};
+    if (p.head == BT_HEAD_CATEGORICAL) {
+      float mx = -INFINITY;
+      for (int j = lane; j < A; j += 32) mx = fmaxf(mx, o[j]);
+      mx = warp_max(mx);
+      float se = 0.f;
+      for (int j = lane; j < A; j += 32) se += expf(o[j] - mx);
+      se = warp_sum(se);
+      const float lse = logf(se);
+      float h = 0.f;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int j = lane + 32 * q;
-          if (j < A) {
-            lpj[q] = (o[j] - mx) - lse;
-            pj[q] = expf(lpj[q]);
-            h -= pj[q] * lpj[q];
-          }
-        }
-        ent = warp_sum(h);
-        lp = (o[action] - mx) - lse;
-      } else {
-        const float* act = reinterpret_cast<const float*>(p.action) + (size_t)flat * A;
-        float acc = 0.f;
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int j = lane + 32 * q;
-          if (j < A) {
-            zj[q] = (act[j] - o[j]) * isig_s[j];
-            acc += -0.5f * zj[q] * zj[q] - lsig_s[j] - 0.5f * kLog2Pi;
-          }
-        }
-        lp = warp_sum(acc);
-        float e = 0.f;
-        for (int j = lane; j < A; j += 32) e += 0.5f + 0.5f * kLog2Pi + lsig_s[j];
-        ent = warp_sum(e);
-      }
-      // Surrogate (ppo.py:90-103).
-      const float eps = p.clip;
-      const float ratio = expf(lp - lp_old);
-      const float lo = 1.f - eps, hi = 1.f + eps;
-      const float u = fmaxf(ratio, lo);
-      const float du = (ratio == u) ? ((lo == u) ? 0.5f : 1.f) : 0.f;
-      const float clipped = fminf(u, hi);
-      const float dm = (u == clipped) ? ((hi == clipped) ? 0.5f : 1.f) : 0.f;
-      const float s1 = ratio * adv, s2 = clipped * adv;
-      const float mn = fminf(s1, s2);
-      const float t1 = (s1 == mn) ? ((s2 == mn) ? 0.5f : 1.f) : 0.f;
-      const float t2 = (s2 == mn) ? ((s1 == mn) ? 0.5f : 1.f) : 0.f;
-      const float g_lp = -((t1 * adv + t2 * adv * (dm * du)) * ratio) * p.inv_mb;
-      const float g_ent = -p.ent_coef * p.inv_mb;
-      // Value loss (ppo.py:105-115).
-      const float c1 = 0.5f * ((value - ret) * (value - ret));
-      float crit, dcrit;
-      if (p.clip_value) {
-        const float dv = value - v_old;
-        const float uu = fmaxf(dv, -eps);
-        const float duu = (dv == uu) ? ((-eps == uu) ? 0.5f : 1.f) : 0.f;
-        const float cl = fminf(uu, eps);
-        const float dcl = (uu == cl) ? ((eps == cl) ? 0.5f : 1.f) : 0.f;
-        const float vc = v_old + cl;
-        const float c2 = 0.5f * ((vc - ret) * (vc - ret));
-        crit = fmaxf(c1, c2);
-        const float w1 = (c1 == crit) ? ((c2 == crit) ? 0.5f : 1.f) : 0.f;
-        const float w2 = (c2 == crit) ? ((c1 == crit) ? 0.5f : 1.f) : 0.f;
-        dcrit = w1 * (value - ret) + w2 * (vc - ret) * (dcl * duu);
-      } else {
-        crit = c1;
-        dcrit = value - ret;
-      }
-      const float d_value = p.vf_coef * p.inv_mb * dcrit;
-      // dL/d out
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int j = lane + 32 * q;
+      for (int qq = 0; qq < 2; ++qq) {
+        const int j = lane + 32 * qq;
         if (j < A) {
-          float g;
-          if (p.head == BT_HEAD_CATEGORICAL) {
-            g = g_lp * (((j == action) ? 1.f : 0.f) - pj[q]) + g_ent * (-pj[q] * (lpj[q] + ent));
-          } else {
-            g = g_lp * (zj[q] * isig_s[j]);
-            dscale_acc[q] += g_lp * ((zj[q] * zj[q] - 1.f) * isig_s[j]) + g_ent * isig_s[j];
-          }
-          d[j] = g;
-          p.d_out[(size_t)row * A + j] = g;
+          lpj[qq] = (o[j] - mx) - lse;
+          pj[qq] = expf(lpj[qq]);
+          h -= pj[qq] * lpj[qq];
         }
       }
-      if (lane == 0) {
-        d[A] = d_value;
-        p.d_val[row] = d_value;
-        st[0] += (double)mn;
-        st[1] += (double)ent;
-        st[2] += (double)(lp_old - lp);
-        st[3] += (fabsf(ratio - 1.f) > eps) ? 1.0 : 0.0;
-        st[4] += (double)adv;
-        st[5] += (double)crit;
-        const double res = (double)ret - (double)value;
-        st[6] += res;
-        st[7] += res * res;
-        st[8] += (double)ret;
-        st[9] += (double)ret * (double)ret;
-        st[10] += (double)value;
-        st[11] += 1.0;
+      ent = warp_sum(h);
+      lp = (o[action] - mx) - lse;
+    } else {
+      float acc = 0.f, e = 0.f;
+#pragma unroll
+      for (int qq = 0; qq < 2; ++qq) {
+        const int j = lane + 32 * qq;
+        if (j < A) {
+          zj[qq] = (act_j[qq] - o[j]) * isig_s[j];
+          acc += -0.5f * zj[qq] * zj[qq] - lsig_s[j] - 0.5f * kLog2Pi;
+          e += 0.5f + 0.5f * kLog2Pi + lsig_s[j];
+        }
+      }
+      lp = warp_sum(acc);
+      ent = warp_sum(e);
+    }
+    // Surrogate (ppo.py:90-103), with JAX's balanced tie rule for min/max/clip.
+    const float eps = p.clip;
+    const float ratio = expf(lp - lp_old);
+    const float lo = 1.f - eps, hi = 1.f + eps;
+    const float u = fmaxf(ratio, lo);
+    const float du = (ratio == u) ? ((lo == u) ? 0.5f : 1.f) : 0.f;
+    const float clipped = fminf(u, hi);
+    const float dm = (u == clipped) ? ((hi == clipped) ? 0.5f : 1.f) : 0.f;
+    const float s1 = ratio * adv, s2 = clipped * adv;
+    const float mn = fminf(s1, s2);
+    const float t1 = (s1 == mn) ? ((s2 == mn) ? 0.5f : 1.f) : 0.f;
+    const float t2 = (s2 == mn) ? ((s1 == mn) ? 0.5f : 1.f) : 0.f;
+    const float g_lp = -((t1 * adv + t2 * adv * (dm * du)) * ratio) * p.inv_mb;
+    const float g_ent = -p.ent_coef * p.inv_mb;
+    // Value loss (ppo.py:105-115).
+    const float c1 = 0.5f * ((value - ret) * (value - ret));
+    float crit, dcrit;
+    if (p.clip_value) {
+      const float dv = value - v_old;
+      const float uu = fmaxf(dv, -eps);
+      const float duu = (dv == uu) ? ((-eps == uu) ? 0.5f : 1.f) : 0.f;
+      const float cl = fminf(uu, eps);
+      const float dcl = (uu == cl) ? ((eps == cl) ? 0.5f : 1.f) : 0.f;
+      const float vc = v_old + cl;
+      const float c2 = 0.5f * ((vc - ret) * (vc - ret));
+      crit = fmaxf(c1, c2);
+      const float w1 = (c1 == crit) ? ((c2 == crit) ? 0.5f : 1.f) : 0.f;
+      const float w2 = (c2 == crit) ? ((c1 == crit) ? 0.5f : 1.f) : 0.f;
+      dcrit = w1 * (value - ret) + w2 * (vc - ret) * (dcl * duu);
+    } else {
+      crit = c1;
+      dcrit = value - ret;
+    }
+    const float d_value = p.vf_coef * p.inv_mb * dcrit;
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+      const int j = lane + 32 * qq;
+      if (j < A) {
+        float g;
+        if (p.head == BT_HEAD_CATEGORICAL) {
+          g = g_lp * (((j == action) ? 1.f : 0.f) - pj[qq]) + g_ent * (-pj[qq] * (lpj[qq] + ent));
+        } else {
+          g = g_lp * (zj[qq] * isig_s[j]);
+          dscale_acc[qq] += g_lp * ((zj[qq] * zj[qq] - 1.f) * isig_s[j]) + g_ent * isig_s[j];
+        }
+        d[j] = g;
+        p.d_out[(size_t)row * A + j] = g;
       }
     }
-    __syncthreads();
-    // dL/d f (times the last activation's derivative).
-    for (int i = tid; i < kHeadRows * F; i += kHeadThreads) {
-      const int r = i / F, k = i - r * F;
-      const int row = r0 + r;
-      if (row >= live) continue;
-      const float* d = dout_s + r * (A + 1);
-      float g = 0.f;
-      for (int j = 0; j < A; ++j) g = fmaf(d[j], wT[(size_t)j * sp + k], g);
-      if (shared) g = fmaf(d[A], wTv[k], g);
-      const size_t gi = (size_t)row * F + k;
-      if (p.act_pi != BT_ACT_NONE)
-        g *= act_grad(p.pre_pi ? p.pre_pi[gi] : 0.f, p.post_pi ? p.post_pi[gi] : 0.f, p.act_pi);
-      p.d_fpi[gi] = g;
+    if (lane == 0) {
+      d[A] = d_value;
+      p.d_val[row] = d_value;
+      st[0] += (double)mn;
+      st[1] += (double)ent;
+      st[2] += (double)(lp_old - lp);
+      st[3] += (fabsf(ratio - 1.f) > eps) ? 1.0 : 0.0;
+      st[4] += (double)adv;
+      st[5] += (double)crit;
+      const double res = (double)ret - (double)value;
+      st[6] += res;
+      st[7] += res * res;
+      st[8] += (double)ret;
+      st[9] += (double)ret * (double)ret;
+      st[10] += (double)value;
+      st[11] += 1.0;
+    }
+    __syncwarp();
+    // dL/d f = d_out W_pi^T (+ d_value w_v^T when shared), times act'.
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int q = lane + 32 * i;
+      if (4 * q >= F) continue;
+      float4 g = make_float4(0, 0, 0, 0);
+      for (int j = 0; j < A; ++j) {
+        const float dj = d[j];
+        const float4 w = reinterpret_cast<const float4*>(wT + (size_t)j * F)[q];
+        g.x = fmaf(dj, w.x, g.x);
+        g.y = fmaf(dj, w.y, g.y);
+        g.z = fmaf(dj, w.z, g.z);
+        g.w = fmaf(dj, w.w, g.w);
+      }
+      if (shared) {
+        const float4 w = reinterpret_cast<const float4*>(wTv)[q];
+        g.x = fmaf(d[A], w.x, g.x);
+        g.y = fmaf(d[A], w.y, g.y);
+        g.z = fmaf(d[A], w.z, g.z);
+        g.w = fmaf(d[A], w.w, g.w);
+      }
+      store_df(g, zp[i], p.act_pi, (size_t)row * F, q, p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
     }
     if (!shared) {
-      for (int i = tid; i < kHeadRows * Fv; i += kHeadThreads) {
-        const int r = i / Fv, k = i - r * Fv;
-        const int row = r0 + r;
-        if (row >= live) continue;
-        float g = dout_s[r * (A + 1) + A] * wTv[k];
-        const size_t gi = (size_t)row * Fv + k;
-        if (p.act_v != BT_ACT_NONE)
-          g *= act_grad(p.pre_v ? p.pre_v[gi] : 0.f, p.post_v ? p.post_v[gi] : 0.f, p.act_v);
-        p.d_fv[gi] = g;
+#pragma unroll
+      for (int i = 0; i < kMaxChunks; ++i) {
+        const int q = lane + 32 * i;
+        if (4 * q >= Fv) continue;
+        const float4 w = reinterpret_cast<const float4*>(wTv)[q];
+        const float4 g = make_float4(d[A] * w.x, d[A] * w.y, d[A] * w.z, d[A] * w.w);
+        store_df(g, zv[i], p.act_v, (size_t)row * Fv, q, p.d_fv, p.d_fv_b, p.d_fv_b_lo);
       }
     }
+    __syncwarp();
   }
 
   // Block partial sums in a fixed order: warps' lane 0 -> shared -> thread 0.
-  __syncthreads();
   if (lane == 0) {
     for (int s = 0; s < kNumStatSums; ++s) stat_s[warp * kNumStatSums + s] = st[s];
   }
   if (p.head == BT_HEAD_GAUSSIAN) {
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int j = lane + 32 * q;
-      if (j < A) red_s[warp * A + j] = dscale_acc[q];
+    for (int qq = 0; qq < 2; ++qq) {
+      const int j = lane + 32 * qq;
+      if (j < A) red_s[warp * A + j] = dscale_acc[qq];
     }
   }
   __syncthreads();
   if (tid < kNumStatSums) {
     double s = 0.0;
-    for (int w = 0; w < kHeadThreads / 32; ++w) s += stat_s[w * kNumStatSums + tid];
+    for (int w = 0; w < kHeadWarps; ++w) s += stat_s[w * kNumStatSums + tid];
     p.stat_partials[(size_t)blockIdx.x * kNumStatSums + tid] = s;
   }
   if (p.head == BT_HEAD_GAUSSIAN && p.dscale_partials) {
     for (int j = tid; j < A; j += kHeadThreads) {
       float s = 0.f;
-      for (int w = 0; w < kHeadThreads / 32; ++w) s += red_s[w * A + j];
+      for (int w = 0; w < kHeadWarps; ++w) s += red_s[w * A + j];
       const float sc = p.scale[j];
       const float sgm = 1.f / (1.f + expf(-sc));  // d softplus / d scale
       p.dscale_partials[(size_t)blockIdx.x * A + j] = s * sgm;
@@ -299,9 +330,19 @@ int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
   const bool shared = p.f_v == p.f_pi;
   const size_t smem = heads_smem_bytes(p.F_pi, p.F_v, p.A, shared);
   BT_CHECK_ARG(p.A <= 64, "heads: action_dim %d > 64 is not supported", p.A);
+  BT_CHECK_ARG(p.F_pi % 4 == 0 && p.F_v % 4 == 0 && p.F_pi <= 4 * 32 * kMaxChunks &&
+                   p.F_v <= 4 * 32 * kMaxChunks,
+               "heads: feature widths %d / %d must be multiples of 4 and at most %d", p.F_pi,
+               p.F_v, 4 * 32 * kMaxChunks);
   BT_CHECK_ARG(smem <= 227 * 1024, "heads: feature width too large for shared memory");
-  BT_CUDA(cudaFuncSetAttribute(heads_loss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
+  if (smem > 48 * 1024) {
+    static size_t configured = 0;
+    if (smem > configured) {
+      BT_CUDA(cudaFuncSetAttribute(heads_loss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
+      configured = smem;
+    }
+  }
   heads_loss_kernel<<<blocks, kHeadThreads, smem, stream>>>(p);
   BT_LAUNCH_CHECK("heads_loss_kernel");
   return BT_OK;

@@ -17,8 +17,8 @@ constexpr float kLnEps = 1e-6f;
 //   mean = E[z], var = max(E[z^2] - mean^2, 0), y = (z - mean) * (rsqrt(var + eps) * scale) + bias
 // One warp per row.
 __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int n, int act,
-                                  float* y, float* h, float* mean_out, float* rstd_out,
-                                  const int* count) {
+                                  float* y, float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo,
+                                  int ldhb, float* mean_out, float* rstd_out, const int* count) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= live_rows(count, rows)) return;
@@ -37,7 +37,9 @@ __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int
   for (int k = lane; k < n; k += 32) {
     const float yv = (zr[k] - mean) * (r * sb[k]) + sb[n + k];
     y[(size_t)row * n + k] = yv;
-    h[(size_t)row * n + k] = act_forward(yv, act);
+    const float hv = act_forward(yv, act);
+    if (h) h[(size_t)row * n + k] = hv;
+    if (hb) store_bf16(hb, hb_lo, (size_t)row * ldhb + k, hv);
   }
   if (lane == 0) {
     mean_out[row] = mean;
@@ -46,10 +48,12 @@ __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int
 }
 
 int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act, float* y,
-                      float* h, float* mean, float* rstd, const int* count, cudaStream_t stream) {
+                      float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb, float* mean,
+                      float* rstd, const int* count, cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
   ln_forward_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(z, scale_bias, rows, n, act, y,
-                                                                  h, mean, rstd, count);
+                                                                  h, hb, hb_lo, ldhb, mean, rstd,
+                                                                  count);
   BT_LAUNCH_CHECK("ln_forward_kernel");
   return BT_OK;
 }
@@ -61,8 +65,9 @@ constexpr int kLnMaxCols = 1024;
 __global__ void __launch_bounds__(256) ln_backward_kernel(const float* d_y, const float* z,
                                                           const float* mean, const float* rstd,
                                                           const float* scale, int rows, int n,
-                                                          float* d_z, float* partials,
-                                                          const int* count) {
+                                                          float* d_z, __nv_bfloat16* d_zb,
+                                                          __nv_bfloat16* d_zb_lo,
+                                                          float* partials, const int* count) {
   __shared__ float red[8][2 * 64];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int warps_total = gridDim.x * 8;
@@ -97,7 +102,9 @@ __global__ void __launch_bounds__(256) ln_backward_kernel(const float* d_y, cons
       if (k < n) {
         const float xhat = (zr[k] - mu) * r;
         const float dx = dyr[k] * scale[k];
-        d_z[(size_t)row * n + k] = r * (dx - m1 - xhat * m2);
+        const float g = r * (dx - m1 - xhat * m2);
+        if (d_z) d_z[(size_t)row * n + k] = g;
+        if (d_zb) store_bf16(d_zb, d_zb_lo, (size_t)row * n + k, g);
       }
     }
   }
@@ -125,11 +132,12 @@ __global__ void __launch_bounds__(256) ln_backward_kernel(const float* d_y, cons
 }
 
 int launch_ln_backward(const float* d_y, const float* z, const float* mean, const float* rstd,
-                       const float* scale, int rows, int n, float* d_z, float* partials,
-                       int blocks, const int* count, cudaStream_t stream) {
+                       const float* scale, int rows, int n, float* d_z, __nv_bfloat16* d_zb,
+                       __nv_bfloat16* d_zb_lo, float* partials, int blocks, const int* count,
+                       cudaStream_t stream) {
   BT_CHECK_ARG(n <= kLnMaxCols, "layernorm width %d > %d", n, kLnMaxCols);
-  ln_backward_kernel<<<blocks, 256, 0, stream>>>(d_y, z, mean, rstd, scale, rows, n, d_z,
-                                                 partials, count);
+  ln_backward_kernel<<<blocks, 256, 0, stream>>>(d_y, z, mean, rstd, scale, rows, n, d_z, d_zb,
+                                                 d_zb_lo, partials, count);
   BT_LAUNCH_CHECK("ln_backward_kernel");
   return BT_OK;
 }
@@ -148,31 +156,94 @@ __device__ __forceinline__ double block_sum_d(double v, double* sh) {
   return s;  // valid in thread 0
 }
 
-__global__ void __launch_bounds__(256) reduce_segments_kernel(const Segment* segs, float* grads,
+int count_reduce_chunks(const Segment* segs, int num_segments) {
+  int n = 0;
+  for (int i = 0; i < num_segments; ++i) n += ceil_div(segs[i].len, kReduceChunk);
+  return n;
+}
+
+void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out, int* count) {
+  int n = 0;
+  for (int i = 0; i < num_segments; ++i)
+    for (int b = 0; b < segs[i].len; b += kReduceChunk)
+      out[n++] = {i, b, b + kReduceChunk < segs[i].len ? b + kReduceChunk : segs[i].len};
+  *count = n;
+}
+
+// Wide chunks: each thread sums the splits of 8 elements spaced by the block size, eight
+// splits at a time (64 independent loads in flight per thread), in split order.
+// Narrow segments (fewer elements than a warp has lanes per split pass, e.g. the per-block
+// partial sums of the gaussian scale): one warp per element, lanes striding over the
+// splits, combined by a fixed shuffle tree. Both orders are fixed, so the result is
+// deterministic.
+__global__ void __launch_bounds__(256) reduce_segments_kernel(const Segment* segs,
+                                                              const ReduceChunk* chunks,
+                                                              float* grads,
                                                               double* norm_partials) {
   __shared__ double sh[8];
-  const Segment sg = segs[blockIdx.y];
+  const ReduceChunk ch = chunks[blockIdx.x];
+  const Segment sg = segs[ch.seg];
   double sq = 0.0;
-  const int per = ceil_div(sg.len, kReduceBlocksPerSegment);
-  const int b = blockIdx.x * per, e = min(sg.len, b + per);
-  for (int i = b + threadIdx.x; i < e; i += blockDim.x) {
-    float s = 0.f;
-    for (int k = 0; k < sg.nsplit; ++k) s += sg.src[(size_t)k * sg.stride + i];
-    grads[sg.dst + i] = s;
-    sq += (double)s * (double)s;
+  if (sg.len < 256) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = ch.begin + warp; i < ch.end; i += 8) {
+      float a = 0.f;
+      for (int k = lane; k < sg.nsplit; k += 32) a += __ldg(sg.src + (size_t)k * sg.stride + i);
+      a = warp_sum(a);
+      if (lane == 0) {
+        grads[sg.dst + i] = a;
+        sq += (double)a * (double)a;
+      }
+    }
+  } else {
+    constexpr int kPer = kReduceChunk / 256;
+    float acc[kPer];
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
+    int k = 0;
+    for (; k + 8 <= sg.nsplit; k += 8) {
+      float v[8][kPer];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float* src = sg.src + (size_t)(k + u) * sg.stride;
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const int i = ch.begin + threadIdx.x + e * 256;
+          v[u][e] = (i < ch.end) ? __ldg(src + i) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) acc[e] += v[u][e];
+    }
+    for (; k < sg.nsplit; ++k) {
+      const float* src = sg.src + (size_t)k * sg.stride;
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) {
+        const int i = ch.begin + threadIdx.x + e * 256;
+        if (i < ch.end) acc[e] += __ldg(src + i);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+      const int i = ch.begin + threadIdx.x + e * 256;
+      if (i < ch.end) {
+        grads[sg.dst + i] = acc[e];
+        sq += (double)acc[e] * (double)acc[e];
+      }
+    }
   }
   if (norm_partials) {
     const double t = block_sum_d(sq, sh);
-    if (threadIdx.x == 0)
-      norm_partials[(size_t)blockIdx.y * kReduceBlocksPerSegment + blockIdx.x] = t;
+    if (threadIdx.x == 0) norm_partials[blockIdx.x] = t;
   }
 }
 
-int launch_reduce_segments(const Segment* segs, int num_segments, float* grads,
-                           double* norm_partials, cudaStream_t stream) {
-  if (num_segments <= 0) return BT_OK;
-  dim3 grid(kReduceBlocksPerSegment, num_segments);
-  reduce_segments_kernel<<<grid, 256, 0, stream>>>(segs, grads, norm_partials);
+int launch_reduce_segments(const Segment* segs, const ReduceChunk* chunks, int num_chunks,
+                           float* grads, double* norm_partials, cudaStream_t stream) {
+  if (num_chunks <= 0) return BT_OK;
+  reduce_segments_kernel<<<num_chunks, 256, 0, stream>>>(segs, chunks, grads, norm_partials);
   BT_LAUNCH_CHECK("reduce_segments_kernel");
   return BT_OK;
 }
@@ -227,7 +298,7 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
     p.params[i] = np_;
     p.mu[i] = m;
     p.nu[i] = v;
-    if (p.shadow) p.shadow[i] = __float2bfloat16_rn(np_);
+    if (p.shadow) store_bf16(p.shadow, p.shadow_lo, i, np_);
   }
 }
 
@@ -246,16 +317,18 @@ int launch_increment(int* count, int by, cudaStream_t stream) {
 }
 
 // ---- statistics --------------------------------------------------------------------------
+// One warp per statistic: lanes stride over the block partials, then a fixed shuffle tree.
 __global__ void stat_reduce_kernel(const double* partials, int blocks, double* out) {
-  const int s = threadIdx.x;
+  const int s = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (s >= kNumStatSums) return;
   double t = 0.0;
-  for (int b = 0; b < blocks; ++b) t += partials[(size_t)b * kNumStatSums + s];
-  out[s] = t;
+  for (int b = lane; b < blocks; b += 32) t += partials[(size_t)b * kNumStatSums + s];
+  t = warp_sum_d(t);
+  if (lane == 0) out[s] = t;
 }
 
 int launch_stat_reduce(const double* partials, int blocks, double* out, cudaStream_t stream) {
-  stat_reduce_kernel<<<1, 32, 0, stream>>>(partials, blocks, out);
+  stat_reduce_kernel<<<1, 32 * kNumStatSums, 0, stream>>>(partials, blocks, out);
   BT_LAUNCH_CHECK("stat_reduce_kernel");
   return BT_OK;
 }
@@ -398,6 +471,66 @@ int launch_local_indices(const int* perm, int num_slices, int slice_len, int /*u
                                                         global_units, capacity, local_idx,
                                                         counts, err);
   BT_LAUNCH_CHECK("local_indices_kernel");
+  return BT_OK;
+}
+
+// ---- bf16 operand buffers of the tensor-core path ------------------------------------------
+// Minibatch gather of observation rows into a bf16 [rows, ld] operand: columns [0, d) the
+// observation, column d = 1 (the bias column of the dW GEMM), (d, ld) zero. One warp per
+// row (coalesced along the row).
+__global__ void gather_bf16_kernel(const float* obs, const int* idx, int rows, int d, int ld,
+                                   __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= live_rows(count, rows)) return;
+  const float* src = obs + (size_t)(idx ? idx[row] : row) * d;
+  for (int k = lane; k < ld; k += 32) {
+    const float v = k < d ? src[k] : (k == d ? 1.f : 0.f);
+    store_bf16(out, out_lo, (size_t)row * ld + k, v);
+  }
+}
+
+int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
+                       __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
+                       cudaStream_t stream) {
+  if (rows <= 0) return BT_OK;
+  gather_bf16_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(obs, idx, rows, d, ld, out,
+                                                                   out_lo, count);
+  BT_LAUNCH_CHECK("gather_bf16_kernel");
+  return BT_OK;
+}
+
+// Columns [n, ld) of a bf16 [rows, ld] buffer: column n = 1, the rest 0 (set once; the
+// forward epilogues only write columns < n).
+__global__ void ones_column_kernel(__nv_bfloat16* buf, int rows, int n, int ld, float one) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int w = ld - n;
+  if (i >= (int64_t)rows * w) return;
+  const int64_t row = i / w;
+  const int c = (int)(i - row * w);
+  buf[row * ld + n + c] = __float2bfloat16_rn(c == 0 ? one : 0.f);
+}
+
+int launch_ones_column(__nv_bfloat16* buf, int rows, int n, int ld, float one,
+                       cudaStream_t stream) {
+  const int64_t total = (int64_t)rows * (ld - n);
+  if (total <= 0) return BT_OK;
+  ones_column_kernel<<<(unsigned)ceil_div64(total, 256), 256, 0, stream>>>(buf, rows, n, ld, one);
+  BT_LAUNCH_CHECK("ones_column_kernel");
+  return BT_OK;
+}
+
+__global__ void to_bf16_kernel(const float* in, __nv_bfloat16* out, __nv_bfloat16* out_lo,
+                               int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    store_bf16(out, out_lo, i, in[i]);
+}
+
+int launch_to_bf16(const float* in, __nv_bfloat16* out, __nv_bfloat16* out_lo, int64_t n,
+                   cudaStream_t stream) {
+  to_bf16_kernel<<<2 * kNumSMs, 256, 0, stream>>>(in, out, out_lo, n);
+  BT_LAUNCH_CHECK("to_bf16_kernel");
   return BT_OK;
 }
 

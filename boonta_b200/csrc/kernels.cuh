@@ -38,6 +38,10 @@ struct HeadsParams {
   float* d_val;  // [rows]
   float* d_fpi;  // [rows, F_pi]
   float* d_fv;   // [rows, F_v] (separate towers)
+  __nv_bfloat16* d_fpi_b;  // when set: dL/d f_pi written as bf16 instead of fp32
+  __nv_bfloat16* d_fv_b;
+  __nv_bfloat16* d_fpi_b_lo;  // when set: the low halves of split bf16 pairs
+  __nv_bfloat16* d_fv_b_lo;
   const float* pre_pi;
   const float* post_pi;
   int act_pi;
@@ -56,13 +60,31 @@ int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, con
 
 // LayerNorm (flax, epsilon 1e-6, fast variance) fused with the following activation.
 int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act,
-                      float* y, float* h, float* mean, float* rstd, const int* count,
-                      cudaStream_t stream);
+                      float* y, float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb,
+                      float* mean, float* rstd, const int* count, cudaStream_t stream);
 // d_y already carries the activation derivative; writes d_z and per-block partial sums
 // [blocks][2n] of (d scale, d bias).
 int launch_ln_backward(const float* d_y, const float* z, const float* mean, const float* rstd,
-                       const float* scale, int rows, int n, float* d_z, float* partials,
-                       int blocks, const int* count, cudaStream_t stream);
+                       const float* scale, int rows, int n, float* d_z, __nv_bfloat16* d_zb,
+                       __nv_bfloat16* d_zb_lo, float* partials, int blocks, const int* count,
+                       cudaStream_t stream);
+
+// bf16 operands of the tensor-core path. Every bf16 writer takes an optional `lo` buffer:
+// when set, the value is stored as the pair hi = bf16(x), lo = bf16(x - hi) (the split
+// operands of BT_PREC_BF16X3).
+__device__ __forceinline__ void store_bf16(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i,
+                                           float x) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(x);
+  hi[i] = h;
+  if (lo) lo[i] = __float2bfloat16_rn(x - __bfloat162float(h));
+}
+int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
+                       __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
+                       cudaStream_t stream);
+int launch_ones_column(__nv_bfloat16* buf, int rows, int n, int ld, float one,
+                       cudaStream_t stream);
+int launch_to_bf16(const float* in, __nv_bfloat16* out, __nv_bfloat16* out_lo, int64_t n,
+                   cudaStream_t stream);
 
 // One gradient segment: dst[0:len] = sum over s of src[s * stride + 0:len] (fixed order).
 struct Segment {
@@ -72,11 +94,19 @@ struct Segment {
   int64_t stride;
   int64_t dst;  // offset in the flat gradient buffer
 };
-constexpr int kReduceBlocksPerSegment = 32;
-// Sums split partials into the gradient buffer; when `norm_partials` is non-null also
-// writes per-block sums of squares [num_segments][kReduceBlocksPerSegment].
-int launch_reduce_segments(const Segment* segs, int num_segments, float* grads,
-                           double* norm_partials, cudaStream_t stream);
+// A piece of a segment reduced by one block: elements [begin, end) of segment `seg`.
+struct ReduceChunk {
+  int seg;
+  int begin, end;
+};
+constexpr int kReduceChunk = 2048;
+// Builds the chunk table of a segment list (host side).
+void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out, int* count);
+int count_reduce_chunks(const Segment* segs, int num_segments);
+// Sums split partials into the gradient buffer, one block per chunk; when `norm_partials`
+// is non-null also writes each block's sum of squares [num_chunks].
+int launch_reduce_segments(const Segment* segs, const ReduceChunk* chunks, int num_chunks,
+                           float* grads, double* norm_partials, cudaStream_t stream);
 // Sum of squares of a flat buffer into norm_partials[kNormBlocks] (multi-GPU path).
 constexpr int kNormBlocks = 256;
 int launch_sumsq(const float* g, int64_t n, double* norm_partials, cudaStream_t stream);
@@ -92,7 +122,8 @@ struct AdamParams {
   const int* count;  // device adam count before this update block
   int step;          // optimizer steps already taken in this update (count offset)
   float lr, max_norm, b1, b2, eps, eps_root;
-  __nv_bfloat16* shadow;  // nullable bf16 copy of params
+  __nv_bfloat16* shadow;     // nullable bf16 copy of params
+  __nv_bfloat16* shadow_lo;  // nullable low halves (split bf16 pairs)
 };
 int launch_adam(const AdamParams& p, cudaStream_t stream);
 

@@ -21,6 +21,7 @@
 #include <cstring>
 
 #include "gemm_simt.cuh"
+#include "gemm_sm100.cuh"
 #include "learner.h"
 
 namespace bt {
@@ -96,6 +97,9 @@ int build_layout(bt_learner* L) {
       lp.kind = l.kind;
       lp.act = l.activation;
       lp.ln = l.layernorm ? 1 : 0;
+      lp.tc = L->cfg.precision != BT_PREC_FP32 && l.kind == BT_LAYER_DENSE;
+      BT_CHECK_ARG(!(L->cfg.precision != BT_PREC_FP32 && l.kind == BT_LAYER_CONV3X3),
+                   "Conv3x3 layers run in fp32 only (precision %d requested)", L->cfg.precision);
       std::string p = std::string(names[t]) + "/" + std::to_string(i);
       if (l.kind == BT_LAYER_CONV3X3) {
         lp.H = l.height;
@@ -174,6 +178,8 @@ int pick_splits(int M, int N, int K) {
 
 }  // namespace
 
+int allocate_tensor_core(bt_learner* L);
+
 int allocate(bt_learner* L) {
   const bt_learner_config& c = L->cfg;
   const int E = c.ppo.update_epochs, M = c.ppo.num_minibatches;
@@ -232,7 +238,18 @@ int allocate(bt_learner* L) {
       // dW GEMM: [kin + 1, ncol] over K = rows (dense) or rows * H*W (conv)
       const int dm = lp.kin + 1, dn = lp.ncol;
       const int dk = lp.kind == BT_LAYER_CONV3X3 ? L->rows_cap * lp.H * lp.W : L->rows_cap;
-      lp.dw_splits = pick_splits(dm, dn, dk);
+      if (lp.tc) {
+        // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1]; about one wave of CTAs,
+        // at least 8 K blocks (512 rows) per split
+        const int bn = c.precision == BT_PREC_BF16X3 ? 64 : 128;
+        const int tiles = ceil_div(lp.kout, 128) * ceil_div(lp.kin + 1, bn);
+        const int nkb = ceil_div(L->rows_cap, 64);
+        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 8));
+        lp.dw_kbps = ceil_div(nkb, splits);
+        lp.dw_splits = ceil_div(nkb, lp.dw_kbps);
+      } else {
+        lp.dw_splits = pick_splits(dm, dn, dk);
+      }
       BT_TRY(dalloc(L, &lp.dw_part, (size_t)lp.dw_splits * dm * dn));
       L->segs_h.push_back({lp.dw_part, lp.dw_splits, dm * dn, (int64_t)dm * dn, lp.w_off});
       if (lp.ln) {
@@ -251,7 +268,10 @@ int allocate(bt_learner* L) {
   BT_TRY(dalloc(L, &L->head_v_part, (size_t)L->head_v_splits * (L->F_v + 1)));
   L->segs_h.push_back({L->head_pi_part, L->head_pi_splits, (L->F_pi + 1) * A,
                        (int64_t)(L->F_pi + 1) * A, L->head_pi_off});
-  L->heads_blocks = kNumSMs;
+  {
+    const size_t hs = heads_smem_bytes(L->F_pi, L->F_v, A, L->shared);
+    L->heads_blocks = kNumSMs * std::max<int>(1, std::min<int>(4, (int)((200 * 1024) / hs)));
+  }
   BT_TRY(dalloc(L, &L->stat_part, (size_t)L->heads_blocks * kNumStatSums));
   if (c.network.head == BT_HEAD_GAUSSIAN) {
     BT_TRY(dalloc(L, &L->dscale_part, (size_t)L->heads_blocks * A));
@@ -262,8 +282,15 @@ int allocate(bt_learner* L) {
   BT_TRY(dalloc(L, &L->segs_d, L->segs_h.size()));
   BT_CUDA(cudaMemcpy(L->segs_d, L->segs_h.data(), L->segs_h.size() * sizeof(Segment),
                      cudaMemcpyHostToDevice));
-  BT_TRY(dalloc(L, &L->norm_part,
-                std::max<size_t>(L->segs_h.size() * kReduceBlocksPerSegment, kNormBlocks)));
+  {
+    std::vector<ReduceChunk> chunks(
+        count_reduce_chunks(L->segs_h.data(), (int)L->segs_h.size()));
+    build_reduce_chunks(L->segs_h.data(), (int)L->segs_h.size(), chunks.data(), &L->num_chunks);
+    BT_TRY(dalloc(L, &L->chunks_d, chunks.size()));
+    BT_CUDA(cudaMemcpy(L->chunks_d, chunks.data(), chunks.size() * sizeof(ReduceChunk),
+                       cudaMemcpyHostToDevice));
+  }
+  BT_TRY(dalloc(L, &L->norm_part, std::max<size_t>(L->num_chunks, kNormBlocks)));
   BT_TRY(dalloc(L, &L->stat_sums, (size_t)(E * M + 1) * kNumStatSums));
   BT_TRY(dalloc(L, &L->adv_part, 2 * kNormBlocks));
   // targets
@@ -276,10 +303,98 @@ int allocate(bt_learner* L) {
     BT_TRY(dalloc(L, &L->local_idx, (size_t)E * M * L->rows_cap));
     BT_TRY(dalloc(L, &L->local_counts, (size_t)E * M));
   }
+  return allocate_tensor_core(L);
+}
+
+// ---- tensor-core (bf16) operand buffers and TMA tensor maps -------------------------------
+int allocate_tensor_core(bt_learner* L) {
+  L->tc_any = false;
+  for (int t = 0; t < L->ntowers; ++t)
+    for (LayerPlan& lp : L->towers[t].layers) L->tc_any |= lp.tc;
+  if (!L->tc_any) return BT_OK;
+  L->x3 = L->cfg.precision == BT_PREC_BF16X3;
+  const int R = L->act_rows;
+  auto ru8 = [](int x) { return (x + 7) / 8 * 8; };
+  auto pair = [&](__nv_bfloat16** hi, __nv_bfloat16** lo, size_t n) -> int {
+    BT_TRY(dalloc(L, hi, n));
+    BT_CUDA(cudaMemset(*hi, 0, n * 2));
+    if (L->x3) {
+      BT_TRY(dalloc(L, lo, n));
+      BT_CUDA(cudaMemset(*lo, 0, n * 2));
+    }
+    return BT_OK;
+  };
+  BT_TRY(pair(&L->params_b, &L->params_b_lo, L->num_params));
+  L->ldx0 = ru8(L->cfg.network.obs_dim + 1);
+  BT_TRY(pair(&L->xg, &L->xg_lo, (size_t)R * L->ldx0));
+  for (int t = 0; t < L->ntowers; ++t) {
+    std::vector<LayerPlan>& layers = L->towers[t].layers;
+    for (size_t i = 0; i < layers.size(); ++i) {
+      LayerPlan& lp = layers[i];
+      if (!lp.tc) continue;
+      BT_CHECK_ARG(lp.kout % 8 == 0, "tensor-core layer width %d is not a multiple of 8", lp.kout);
+      lp.ldh = ru8(lp.kout + 1);
+      BT_TRY(pair(&lp.hb, &lp.hb_lo, (size_t)R * lp.ldh));
+      BT_TRY(launch_ones_column(lp.hb, R, lp.kout, lp.ldh, 1.f, 0));
+      BT_TRY(pair(&lp.dzb, &lp.dzb_lo, (size_t)R * lp.kout));
+      if (i == 0) {
+        lp.xin_b = L->xg;
+        lp.xin_lo = L->xg_lo;
+        lp.ldx = L->ldx0;
+      } else {
+        BT_CHECK_ARG(layers[i - 1].tc, "a tensor-core layer must follow a tensor-core layer");
+        lp.xin_b = layers[i - 1].hb;
+        lp.xin_lo = layers[i - 1].hb_lo;
+        lp.ldx = layers[i - 1].ldh;
+      }
+      const int mtiles = ceil_div(L->rows_cap, umma::BM);
+      lp.fwd_bn = (!L->x3 && lp.kout % 256 == 0 && mtiles * (lp.kout / 256) >= kNumSMs) ? 256 : 128;
+      // hi maps, then (split mode) the same maps over the lo halves
+      for (int part = 0; part < (L->x3 ? 2 : 1); ++part) {
+        const __nv_bfloat16* w = (part ? L->params_b_lo : L->params_b) + lp.w_off;
+        const __nv_bfloat16* xin = part ? lp.xin_lo : lp.xin_b;
+        const __nv_bfloat16* dz = part ? lp.dzb_lo : lp.dzb;
+        CUtensorMap* fa = part ? &lp.fwd_ops.a_lo : &lp.fwd_ops.a;
+        CUtensorMap* fb = part ? &lp.fwd_ops.b_lo : &lp.fwd_ops.b;
+        CUtensorMap* xa = part ? &lp.dx_ops.a_lo : &lp.dx_ops.a;
+        CUtensorMap* xb = part ? &lp.dx_ops.b_lo : &lp.dx_ops.b;
+        CUtensorMap* wa = part ? &lp.dw_ops.a_lo : &lp.dw_ops.a;
+        CUtensorMap* wb = part ? &lp.dw_ops.b_lo : &lp.dw_ops.b;
+        BT_TRY(umma::encode_map(fa, xin, lp.kin, R, (uint64_t)lp.ldx * 2, 64, 128));
+        BT_TRY(umma::encode_map(fb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64, 64));
+        BT_TRY(umma::encode_map(xa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 128));
+        BT_TRY(umma::encode_map(xb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64,
+                                L->x3 ? 64 : 128));
+        BT_TRY(umma::encode_map(wa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 64));
+        BT_TRY(umma::encode_map(wb, xin, lp.kin + 1, R, (uint64_t)lp.ldx * 2, 64, 64));
+      }
+      if (!L->x3) {
+        lp.fwd_ops.a_lo = lp.fwd_ops.a;
+        lp.fwd_ops.b_lo = lp.fwd_ops.b;
+        lp.dx_ops.a_lo = lp.dx_ops.a;
+        lp.dx_ops.b_lo = lp.dx_ops.b;
+        lp.dw_ops.a_lo = lp.dw_ops.a;
+        lp.dw_ops.b_lo = lp.dw_ops.b;
+      }
+    }
+  }
+  BT_CUDA(cudaDeviceSynchronize());
   return BT_OK;
 }
 
 // ---- forward / backward of one tower --------------------------------------------------
+// Layers marked `tc` run on the tcgen05 tensor-core GEMM with bf16 operands (activations
+// and dz stored as bf16 row-major buffers, weights from the bf16 shadow of the params);
+// the others run on the fp32 CUDA-core GEMM. A tensor-core tower's first layer reads the
+// minibatch gathered into L->xg (gather_obs).
+int gather_obs(bt_learner* L, const float* obs, const int* idx, int rows, const int* count,
+               cudaStream_t s) {
+  if (!L->tc_any) return BT_OK;
+  BT_K(L, kProfMisc, s, launch_gather_bf16(obs, idx, rows, L->cfg.network.obs_dim, L->ldx0, L->xg,
+                                           L->xg_lo, count, s));
+  return BT_OK;
+}
+
 int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
                   const int* count, cudaStream_t s) {
   const float* in = obs;
@@ -287,8 +402,27 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
   int in_ld = tp.in_dim;
   for (size_t i = 0; i < tp.layers.size(); ++i) {
     LayerPlan& lp = tp.layers[i];
+    const bool last = i + 1 == tp.layers.size();
     const float* w = L->params + lp.w_off;
-    if (lp.kind == BT_LAYER_CONV3X3) {
+    if (lp.tc) {
+      umma::GemmShape sh{rows, lp.kout, lp.kin, ceil_div(lp.kin, umma::BK), count, nullptr,
+                         L->err_d};
+      umma::EpiFwd ep{w + (size_t)lp.kin * lp.kout, lp.z, lp.kout, lp.ln ? nullptr : lp.hb,
+                      lp.ln ? nullptr : lp.hb_lo, lp.ldh, (last && !lp.ln) ? lp.h : nullptr,
+                      lp.kout, lp.ln ? BT_ACT_NONE : lp.act};
+      if (L->x3) {
+        BT_K(L, kProfGemmFwd, s, umma::launch_gemm<64, false, true, true>(lp.fwd_ops, sh, ep, 1, s));
+      } else if (lp.fwd_bn == 256) {
+        BT_K(L, kProfGemmFwd, s, umma::launch_gemm<256, false, true, false>(lp.fwd_ops, sh, ep, 1, s));
+      } else {
+        BT_K(L, kProfGemmFwd, s, umma::launch_gemm<128, false, true, false>(lp.fwd_ops, sh, ep, 1, s));
+      }
+      if (lp.ln) {
+        BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act,
+                                                 lp.y, last ? lp.h : nullptr, lp.hb, lp.hb_lo,
+                                                 lp.ldh, lp.mean, lp.rstd, count, s));
+      }
+    } else if (lp.kind == BT_LAYER_CONV3X3) {
       AIm2col a{in, gather, lp.H, lp.W, lp.C};
       BRows b{w, lp.ncol, lp.kin + 1};
       EpiForward ep{lp.z, lp.h, lp.ncol, lp.act};
@@ -301,7 +435,7 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       BT_K(L, kProfGemmFwd, s, launch_gemm_simt(a, b, ep, rows, lp.ncol, lp.kin + 1, 1, s, count, nullptr));
       if (lp.ln) {
         BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act, lp.y, lp.h,
-                                 lp.mean, lp.rstd, count, s));
+                                 nullptr, nullptr, 0, lp.mean, lp.rstd, count, s));
       }
     }
     in = lp.h;
@@ -318,9 +452,34 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
     const float* w = L->params + lp.w_off;
     if (lp.ln) {
       BT_K(L, kProfLnBwd, s, launch_ln_backward(lp.d_pre, lp.z, lp.mean, lp.rstd, L->params + lp.ln_off, rows,
-                                lp.kout, lp.d_z, lp.ln_part, lp.ln_blocks, count, s));
+                                lp.kout, lp.tc ? nullptr : lp.d_z, lp.tc ? lp.dzb : nullptr,
+                                lp.tc ? lp.dzb_lo : nullptr, lp.ln_part, lp.ln_blocks, count, s));
     }
     const int dm = lp.kin + 1, dn = lp.ncol;
+    if (lp.tc) {
+      // dW^T [kout, kin + 1] = dz^T [x, 1], stored transposed as [kin + 1, kout] partials
+      umma::GemmShape sh{lp.kout, lp.kin + 1, rows, lp.dw_kbps, nullptr, count, L->err_d};
+      umma::EpiDwT ep{lp.dw_part, lp.kout, (size_t)dm * dn, lp.kin + 1};
+      if (L->x3) {
+        BT_K(L, kProfGemmDw, s, umma::launch_gemm<64, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, s));
+      } else {
+        BT_K(L, kProfGemmDw, s, umma::launch_gemm<128, true, true, false>(lp.dw_ops, sh, ep, lp.dw_splits, s));
+      }
+      if (i > 0) {
+        LayerPlan& prev = tp.layers[i - 1];
+        umma::GemmShape shx{rows, lp.kin, lp.kout, ceil_div(lp.kout, umma::BK), count, nullptr,
+                            L->err_d};
+        umma::EpiDx epx{prev.pre(), prev.kout, prev.ln ? prev.d_pre : nullptr,
+                        prev.ln ? nullptr : prev.dzb, prev.ln ? nullptr : prev.dzb_lo, prev.kout,
+                        prev.act};
+        if (L->x3) {
+          BT_K(L, kProfGemmDx, s, umma::launch_gemm<64, false, false, true>(lp.dx_ops, shx, epx, 1, s));
+        } else {
+          BT_K(L, kProfGemmDx, s, umma::launch_gemm<128, false, false, false>(lp.dx_ops, shx, epx, 1, s));
+        }
+      }
+      continue;
+    }
     EpiPartial ep{lp.dw_part, dn, (size_t)dm * dn};
     if (lp.kind == BT_LAYER_CONV3X3) {
       AIm2colT a{AIm2col{obs, idx, lp.H, lp.W, lp.C}};
@@ -364,6 +523,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
                cudaStream_t s) {
   const int rows = L->rows_cap;
   const bt_learner_config& c = L->cfg;
+  BT_TRY(gather_obs(L, in.obs, in.idx, rows, in.count, s));
   for (int t = 0; t < L->ntowers; ++t)
     BT_TRY(forward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
   TowerPlan& t0 = L->towers[0];
@@ -397,6 +557,10 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   hp.d_val = L->d_val;
   hp.d_fpi = last_pi.d_pre;
   hp.d_fv = L->shared ? nullptr : last_v.d_pre;
+  hp.d_fpi_b = (last_pi.tc && !last_pi.ln) ? last_pi.dzb : nullptr;
+  hp.d_fv_b = (!L->shared && last_v.tc && !last_v.ln) ? last_v.dzb : nullptr;
+  hp.d_fpi_b_lo = hp.d_fpi_b ? last_pi.dzb_lo : nullptr;
+  hp.d_fv_b_lo = hp.d_fv_b ? last_v.dzb_lo : nullptr;
   hp.pre_pi = last_pi.pre();
   hp.post_pi = last_pi.h;
   hp.act_pi = last_pi.act;
@@ -424,7 +588,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   }
   for (int t = 0; t < L->ntowers; ++t)
     BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
-  BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, (int)L->segs_h.size(), L->grads,
+  BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
                                 with_norm ? L->norm_part : nullptr, s));
   return BT_OK;
 }
@@ -440,6 +604,7 @@ int check_batch(bt_learner* L, const bt_batch* b) {
 int bootstrap_and_gae(bt_learner* L, const bt_batch* b, cudaStream_t s) {
   // V(second.obs[T-1]) through the critic's tower (or the shared torso).
   TowerPlan& tv = L->towers[L->ntowers - 1];
+  BT_TRY(gather_obs(L, b->bootstrap_obs, nullptr, L->N, nullptr, s));
   BT_TRY(forward_tower(L, tv, b->bootstrap_obs, nullptr, L->N, nullptr, s));
   BT_K(L, kProfHeadsFwd, s, launch_heads_forward(tv.layers.back().h, L->F_v, tv.layers.back().h, L->F_v,
                               L->params + L->head_pi_off, L->params + L->head_v_off, L->A, L->N,
@@ -469,7 +634,7 @@ int optimizer_step(bt_learner* L, int step, cudaStream_t s) {
     BT_K(L, kProfReduce, s, launch_sumsq(L->grads, L->num_params, L->norm_part, s));
     ap.num_norm_partials = kNormBlocks;
   } else {
-    ap.num_norm_partials = (int)L->segs_h.size() * kReduceBlocksPerSegment;
+    ap.num_norm_partials = L->num_chunks;
   }
   ap.norm_partials = L->norm_part;
   ap.count = L->count_d;
@@ -480,7 +645,8 @@ int optimizer_step(bt_learner* L, int step, cudaStream_t s) {
   ap.b2 = o.b2;
   ap.eps = o.eps;
   ap.eps_root = o.eps_root;
-  ap.shadow = nullptr;
+  ap.shadow = L->params_b;
+  ap.shadow_lo = L->params_b_lo;
   BT_K(L, kProfAdam, s, launch_adam(ap, s));
   return BT_OK;
 }
@@ -496,8 +662,9 @@ extern "C" int bt_learner_create(const bt_learner_config* cfg, bt_learner** out)
   BT_CHECK_ARG(cfg->num_steps > 0 && cfg->num_envs > 0, "num_steps %d / num_envs %d",
                cfg->num_steps, cfg->num_envs);
   BT_CHECK_ARG(cfg->network.obs_dim > 0, "obs_dim %d", cfg->network.obs_dim);
-  BT_CHECK_ARG(cfg->precision == BT_PREC_FP32, "precision %d is not available in this build",
-               cfg->precision);
+  BT_CHECK_ARG(cfg->precision == BT_PREC_FP32 || cfg->precision == BT_PREC_BF16 ||
+                   cfg->precision == BT_PREC_BF16X3,
+               "precision %d is not available in this build", cfg->precision);
   BT_CHECK_ARG(cfg->world_size >= 1 && cfg->rank >= 0 && cfg->rank < cfg->world_size,
                "rank %d / world_size %d", cfg->rank, cfg->world_size);
   bt_learner* L = new bt_learner();
@@ -550,6 +717,8 @@ extern "C" int bt_learner_set_state(bt_learner* L, const float* params, const fl
   cudaStream_t s = (cudaStream_t)stream;
   const size_t bytes = (size_t)L->num_params * 4;
   BT_CUDA(cudaMemcpyAsync(L->params, params, bytes, cudaMemcpyDefault, s));
+  if (L->params_b)
+    BT_K(L, kProfMisc, s, launch_to_bf16(L->params, L->params_b, L->params_b_lo, L->num_params, s));
   if (mu) {
     BT_CUDA(cudaMemcpyAsync(L->mu, mu, bytes, cudaMemcpyDefault, s));
   } else {
@@ -681,6 +850,7 @@ extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, cons
   BT_CHECK_ARG(num >= 0 && num <= L->act_rows, "bt_learner_act: %d rows > capacity %d", num,
                L->act_rows);
   cudaStream_t s = (cudaStream_t)stream;
+  BT_TRY(gather_obs(L, obs, nullptr, num, nullptr, s));
   for (int t = 0; t < L->ntowers; ++t)
     BT_TRY(forward_tower(L, L->towers[t], obs, nullptr, num, nullptr, s));
   TowerPlan& t0 = L->towers[0];

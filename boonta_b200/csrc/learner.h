@@ -1,9 +1,12 @@
 // Internal state of a learner handle (one per GPU and stream).
 #pragma once
 
+#include <cuda.h>
+
 #include <string>
 #include <vector>
 
+#include "gemm_sm100.cuh"
 #include "kernels.cuh"
 
 struct ParamEntryC {
@@ -32,6 +35,19 @@ struct LayerPlan {
   int dw_splits = 1;
   float* ln_part = nullptr;
   int ln_blocks = 0;
+  // tensor-core (bf16) path
+  bool tc = false;
+  __nv_bfloat16* xin_b = nullptr;  // bf16 input operand [rows, ldx], ones column at kin
+  int ldx = 0;
+  __nv_bfloat16* hb = nullptr;  // bf16 output [rows, ldh], ones column at kout
+  int ldh = 0;
+  __nv_bfloat16* dzb = nullptr;  // bf16 dL/dz [rows, kout]
+  __nv_bfloat16* hb_lo = nullptr;   // split mode: low halves of hb / dzb / xin_b
+  __nv_bfloat16* dzb_lo = nullptr;
+  __nv_bfloat16* xin_lo = nullptr;
+  bt::umma::Operands fwd_ops, dx_ops, dw_ops;
+  int fwd_bn = 128;
+  int dw_kbps = 1;
   // GRU (recurrent torso)
   int hidden = 0;
   int64_t wi_off = 0, wh_off = 0, bhn_off = 0;
@@ -80,6 +96,14 @@ struct bt_learner {
   int* count_d = nullptr;   // adam count
   int* err_d = nullptr;     // device error word
   int* mb_count_d = nullptr;  // live rows for bt_learner_loss_grads
+  // tensor-core path
+  bool tc_any = false;
+  bool x3 = false;                    // split-bf16 (BT_PREC_BF16X3) operands
+  __nv_bfloat16* params_b = nullptr;  // bf16 shadow of params (written by every Adam step)
+  __nv_bfloat16* params_b_lo = nullptr;
+  __nv_bfloat16* xg = nullptr;        // gathered minibatch observations [rows, ldx0]
+  __nv_bfloat16* xg_lo = nullptr;
+  int ldx0 = 0;
   // network
   TowerPlan towers[2];
   int ntowers = 1;
@@ -112,6 +136,8 @@ struct bt_learner {
   // reductions
   std::vector<bt::Segment> segs_h;
   bt::Segment* segs_d = nullptr;
+  bt::ReduceChunk* chunks_d = nullptr;
+  int num_chunks = 0;
   double* norm_part = nullptr;
   double* stat_sums = nullptr;  // [E*M + 1][kNumStatSums]
   double* adv_part = nullptr;
@@ -127,14 +153,14 @@ cudaEvent_t prof_event(bt_learner* L);
 
 // Enqueue one kernel (or collective) launch `call`, counting it and, when profiling is
 // on, bracketing it with CUDA events on stream `s`.
-#define BT_K(L, cls, s, call)                                   \
+#define BT_K(L, cls, s, ...)                                    \
   do {                                                          \
     cudaEvent_t a_ = nullptr;                                   \
     if ((L)->prof.on) {                                         \
       a_ = prof_event(L);                                       \
       cudaEventRecord(a_, s);                                   \
     }                                                           \
-    BT_TRY(call);                                               \
+    BT_TRY((__VA_ARGS__));                                      \
     (L)->prof.launches++;                                       \
     if ((L)->prof.on) {                                         \
       cudaEvent_t b_ = prof_event(L);                           \
@@ -142,4 +168,4 @@ cudaEvent_t prof_event(bt_learner* L);
       (L)->prof.recs.push_back({cls, a_, b_});                  \
     }                                                           \
   } while (0)
-#define BT_C(L, cls, s, call) BT_K(L, cls, s, call)
+#define BT_C(L, cls, s, ...) BT_K(L, cls, s, __VA_ARGS__)

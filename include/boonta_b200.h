@@ -212,6 +212,11 @@ BT_API int bt_sample_categorical(const float* logits, const float* uniforms, int
  * layouts against a reference product. `splits`/`partial` are reserved (pass 1 / NULL). */
 BT_API int bt_gemm_bf16(const void* A, const void* B, float* D, int32_t M, int32_t N, int32_t K,
                         int32_t a_mn, int32_t b_mn, int32_t splits, float* partial, void* stream);
+/* Split-precision variant (the BT_PREC_BF16X3 arithmetic): fp32 operands given as bf16
+ * pairs x = hi + lo; D = A_hi B_hi + A_hi B_lo + A_lo B_hi, accumulated in fp32. */
+BT_API int bt_gemm_bf16x3(const void* A_hi, const void* A_lo, const void* B_hi, const void* B_lo,
+                          float* D, int32_t M, int32_t N, int32_t K, int32_t a_mn, int32_t b_mn,
+                          void* stream);
 
 /* ---- tracing ----------------------------------------------------------------------------
  * The reference profiles with jax.profiler traces (hangar/scripts/profile_boonta.py:25-65);

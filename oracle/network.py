@@ -15,7 +15,9 @@ flax semantics restated (flax 0.12.8 is not vendored or installed):
 `precision="bf16"` rounds both GEMM operands (the layer input and the kernel in the
 forward pass; the output gradient and the kernel/input in the backward pass) to bfloat16
 with round-to-nearest-even before an fp32 product, the arithmetic of the CUDA path's bf16
-tensor-core GEMMs. Bias, LayerNorm, activations and the heads stay fp32.
+tensor-core GEMMs (whose dW GEMM also yields the bias gradient, as the sum of the
+bf16-rounded output gradient). The forward bias add, LayerNorm, activations and the heads
+stay fp32. Convolutions always run in fp32.
 """
 from __future__ import annotations
 
@@ -128,7 +130,7 @@ def forward(spec: NetworkSpec, params: dict, obs: np.ndarray, precision: str = "
                 cols = im2col3x3(img).reshape(-1, 9 * layer.in_channels)
                 x_in = cols
                 k2 = kernel.reshape(9 * layer.in_channels, layer.features)
-                z = quantize(cols, precision) @ quantize(k2, precision) + bias
+                z = cols @ k2 + bias
                 z = z.reshape(h.shape[0], -1)
             elif isinstance(layer, Dense):
                 x_in = h
@@ -191,15 +193,15 @@ def backward(spec: NetworkSpec, params: dict, cache, d_out, d_value, precision: 
             if isinstance(layer, Conv3x3):
                 dzc = dz.reshape(-1, layer.features)
                 k2 = kernel.reshape(9 * layer.in_channels, layer.features)
-                grads[f"{p}/kernel"] = (
-                    quantize(ent["x"], precision).T @ quantize(dzc, precision)
-                ).reshape(kernel.shape)
+                grads[f"{p}/kernel"] = (ent["x"].T @ dzc).reshape(kernel.shape)
                 grads[f"{p}/bias"] = dzc.sum(0)
                 if i > 0:
                     raise NotImplementedError("a conv layer is only supported as the first layer")
             else:
                 grads[f"{p}/kernel"] = quantize(ent["x"], precision).T @ quantize(dz, precision)
-                grads[f"{p}/bias"] = dz.sum(0)
+                # the bias gradient rides the dW GEMM as a ones row of the input, so in
+                # bf16 mode it sums the bf16-rounded dz
+                grads[f"{p}/bias"] = quantize(dz, precision).sum(0)
                 if i > 0:
                     dh = quantize(dz, precision) @ quantize(kernel, precision).T
     return grads
