@@ -176,7 +176,7 @@ void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out
 // partial sums of the gaussian scale): one warp per element, lanes striding over the
 // splits, combined by a fixed shuffle tree. Both orders are fixed, so the result is
 // deterministic.
-__global__ void __launch_bounds__(256) reduce_segments_kernel(const Segment* segs,
+__global__ void __launch_bounds__(256, 4) reduce_segments_kernel(const Segment* segs,
                                                               const ReduceChunk* chunks,
                                                               float* grads,
                                                               double* norm_partials) {
@@ -471,6 +471,72 @@ int launch_local_indices(const int* perm, int num_slices, int slice_len, int /*u
                                                         global_units, capacity, local_idx,
                                                         counts, err);
   BT_LAUNCH_CHECK("local_indices_kernel");
+  return BT_OK;
+}
+
+// ---- head weight gradients ------------------------------------------------------------------
+// [F + 1, n] split partials of [f, 1]^T d for a narrow output gradient d (n <= NMAX <= 64):
+// one thread per input feature k (k == F is the constant-one row whose sum is the bias
+// gradient), the rows of a split staged 64 at a time in shared memory; each thread keeps
+// its n accumulators in registers and sums rows in order.
+template <int NMAX>
+__global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, const float* d,
+                                                        int n, int rows, const int* count,
+                                                        int rows_per_split, float* out) {
+  __shared__ float ds[64][NMAX];
+  const int k = blockIdx.x * 128 + threadIdx.x;
+  const int live = live_rows(count, rows);
+  const int r0 = blockIdx.y * rows_per_split;
+  const int r1 = min(live, r0 + rows_per_split);
+  float acc[NMAX];
+#pragma unroll
+  for (int j = 0; j < NMAX; ++j) acc[j] = 0.f;
+  for (int rb = r0; rb < r1; rb += 64) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * NMAX; i += 128) {
+      const int rr = i / NMAX, j = i - rr * NMAX;
+      ds[rr][j] = (rb + rr < r1 && j < n) ? d[(size_t)(rb + rr) * n + j] : 0.f;
+    }
+    __syncthreads();
+    const int nr = min(64, r1 - rb);
+    // eight rows' loads in flight before their FMAs
+    for (int r8 = 0; r8 < nr; r8 += 8) {
+      float fk[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int rr = r8 + u;
+        fk[u] = (rr < nr && k < F) ? __ldg(f + (size_t)(rb + rr) * F + k)
+                                   : ((rr < nr && k == F) ? 1.f : 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(fk[u], ds[r8 + u][j], acc[j]);
+    }
+  }
+  if (k <= F) {
+    float* o = out + ((size_t)blockIdx.y * (F + 1) + k) * n;
+    for (int j = 0; j < n; ++j) o[j] = acc[j];
+  }
+}
+
+int launch_skinny_dw(const float* f, int F, const float* d, int n, int rows, const int* count,
+                     int splits, float* out, cudaStream_t stream) {
+  const int rps = ceil_div(rows, splits);
+  dim3 grid(ceil_div(F + 1, 128), splits);
+  if (n <= 1) {
+    skinny_dw_kernel<1><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+  } else if (n <= 8) {
+    skinny_dw_kernel<8><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+  } else if (n <= 16) {
+    skinny_dw_kernel<16><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+  } else if (n <= 32) {
+    skinny_dw_kernel<32><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+  } else {
+    BT_CHECK_ARG(n <= 64, "skinny dW with %d outputs", n);
+    skinny_dw_kernel<64><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+  }
+  BT_LAUNCH_CHECK("skinny_dw_kernel");
   return BT_OK;
 }
 

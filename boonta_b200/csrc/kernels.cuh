@@ -69,6 +69,10 @@ int launch_ln_backward(const float* d_y, const float* z, const float* mean, cons
                        __nv_bfloat16* d_zb_lo, float* partials, int blocks, const int* count,
                        cudaStream_t stream);
 
+// [F + 1, n] split partials [splits][F + 1][n] of [f, 1]^T d, for narrow d (n <= 64).
+int launch_skinny_dw(const float* f, int F, const float* d, int n, int rows, const int* count,
+                     int splits, float* out, cudaStream_t stream);
+
 // bf16 operands of the tensor-core path. Every bf16 writer takes an optional `lo` buffer:
 // when set, the value is stored as the pair hi = bf16(x), lo = bf16(x - hi) (the split
 // operands of BT_PREC_BF16X3).
@@ -99,7 +103,7 @@ struct ReduceChunk {
   int seg;
   int begin, end;
 };
-constexpr int kReduceChunk = 2048;
+constexpr int kReduceChunk = 1024;
 // Builds the chunk table of a segment list (host side).
 void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out, int* count);
 int count_reduce_chunks(const Segment* segs, int num_segments);

@@ -262,8 +262,12 @@ int allocate(bt_learner* L) {
   const int A = L->A;
   BT_TRY(dalloc(L, &L->d_out, (size_t)R * A));
   BT_TRY(dalloc(L, &L->d_val, R));
-  L->head_pi_splits = pick_splits(L->F_pi + 1, A, L->rows_cap);
-  L->head_v_splits = pick_splits(L->F_v + 1, 1, L->rows_cap);
+  // skinny head dW: about 8 blocks of 128 threads per SM (enough loads in flight), at
+  // least 32 rows per split
+  L->head_pi_splits = std::max(1, std::min(ceil_div(L->rows_cap, 32),
+                                           8 * kNumSMs / ceil_div(L->F_pi + 1, 128)));
+  L->head_v_splits = std::max(1, std::min(ceil_div(L->rows_cap, 32),
+                                          8 * kNumSMs / ceil_div(L->F_v + 1, 128)));
   BT_TRY(dalloc(L, &L->head_pi_part, (size_t)L->head_pi_splits * (L->F_pi + 1) * A));
   BT_TRY(dalloc(L, &L->head_v_part, (size_t)L->head_v_splits * (L->F_v + 1)));
   L->segs_h.push_back({L->head_pi_part, L->head_pi_splits, (L->F_pi + 1) * A,
@@ -571,21 +575,11 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   hp.dscale_partials = L->dscale_part;
   BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
   BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
-  // head weight gradients: [F + 1, A] = [f, 1]^T d_out
-  {
-    ACols a{last_pi.h, nullptr, L->F_pi, L->F_pi};
-    BRows b{L->d_out, L->A, rows};
-    EpiPartial ep{L->head_pi_part, L->A, (size_t)(L->F_pi + 1) * L->A};
-    BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, L->F_pi + 1, L->A, rows, L->head_pi_splits, s, nullptr,
-                            in.count));
-  }
-  {
-    ACols a{last_v.h, nullptr, L->F_v, L->F_v};
-    BRows b{L->d_val, 1, rows};
-    EpiPartial ep{L->head_v_part, 1, (size_t)(L->F_v + 1)};
-    BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, L->F_v + 1, 1, rows, L->head_v_splits, s, nullptr,
-                            in.count));
-  }
+  // head weight gradients: [F + 1, A] = [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value
+  BT_K(L, kProfGemmDw, s, launch_skinny_dw(last_pi.h, L->F_pi, L->d_out, L->A, rows, in.count,
+                                           L->head_pi_splits, L->head_pi_part, s));
+  BT_K(L, kProfGemmDw, s, launch_skinny_dw(last_v.h, L->F_v, L->d_val, 1, rows, in.count,
+                                           L->head_v_splits, L->head_v_part, s));
   for (int t = 0; t < L->ntowers; ++t)
     BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
   BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
