@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
   __syncthreads();
   const float g_norm = s_norm;
   const bool clip = !(g_norm < p.max_norm);
-  const int count = *p.count + p.step + 1;
+  const int count = (p.count ? *p.count : 0) + p.step + 1;
   const float bc1 = __fsub_rn(1.f, powf(p.b1, (float)count));
   const float bc2 = __fsub_rn(1.f, powf(p.b2, (float)count));
   const float omb1 = __fsub_rn(1.f, p.b1), omb2 = __fsub_rn(1.f, p.b2);
@@ -305,6 +305,25 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
 int launch_adam(const AdamParams& p, cudaStream_t stream) {
   adam_kernel<<<2 * kNumSMs, 256, 0, stream>>>(p);
   BT_LAUNCH_CHECK("adam_kernel");
+  return BT_OK;
+}
+
+__global__ void __launch_bounds__(256) sumsq_chunks_kernel(const float* g, int64_t n,
+                                                           double* out) {
+  __shared__ double sh[8];
+  const int64_t b = (int64_t)blockIdx.x * kNormChunk;
+  const int64_t e = min(n, b + kNormChunk);
+  double sq = 0.0;
+  for (int64_t i = b + threadIdx.x; i < e; i += blockDim.x) sq += (double)g[i] * (double)g[i];
+  const double t = block_sum_d(sq, sh);
+  if (threadIdx.x == 0) out[blockIdx.x] = t;
+}
+
+int launch_sumsq_chunks(const float* g, int64_t n, double* out, cudaStream_t stream) {
+  const int64_t chunks = ceil_div64(n, kNormChunk);
+  if (chunks <= 0) return BT_OK;
+  sumsq_chunks_kernel<<<(unsigned)chunks, 256, 0, stream>>>(g, n, out);
+  BT_LAUNCH_CHECK("sumsq_chunks_kernel");
   return BT_OK;
 }
 

@@ -123,13 +123,18 @@ struct AdamParams {
   int64_t n;
   const double* norm_partials;
   int num_norm_partials;
-  const int* count;  // device adam count before this update block
-  int step;          // optimizer steps already taken in this update (count offset)
+  const int* count;  // device adam count before this update block (nullable: 0)
+  int step;          // optimizer steps already taken (added to *count)
   float lr, max_norm, b1, b2, eps, eps_root;
   __nv_bfloat16* shadow;     // nullable bf16 copy of params
   __nv_bfloat16* shadow_lo;  // nullable low halves (split bf16 pairs)
 };
 int launch_adam(const AdamParams& p, cudaStream_t stream);
+
+// Sum of squares of g in chunks of kNormChunk elements: out[c] = sum over chunk c (one
+// block per chunk, fixed order). The standalone optimizer entry points use it.
+constexpr int kNormChunk = 8192;
+int launch_sumsq_chunks(const float* g, int64_t n, double* out, cudaStream_t stream);
 
 // Per-minibatch statistics.
 int launch_stat_reduce(const double* partials, int blocks, double* out, cudaStream_t stream);

@@ -1,0 +1,61 @@
+// K10 as a standalone entry point: optax.chain(clip_by_global_norm(max_norm),
+// adam(lr, b1, b2, eps, eps_root)) followed by optax.apply_updates, on flat fp32 device
+// buffers — the optimizer step of boonta/algorithms/ppo.py:182-191 — for callers that run
+// their own forward/backward. The learner handle uses the same kernels inside its update.
+//
+// The global norm is summed in two fixed-order stages: per-chunk sums of squares (8192
+// elements per block) into scratch, then every Adam block adds the chunk sums in index
+// order, so the result is deterministic.
+#include "kernels.cuh"
+
+using namespace bt;
+
+namespace {
+
+int check_opt_args(float* params, float* mu, float* nu, const float* grads, int64_t n,
+                   int32_t count, const bt_optimizer* opt) {
+  BT_CHECK_ARG(params && mu && nu && grads && opt, "clip_adam: null argument");
+  BT_CHECK_ARG(n >= 0, "clip_adam: negative size %lld", (long long)n);
+  BT_CHECK_ARG(count >= 0, "clip_adam: negative step count %d", count);
+  return BT_OK;
+}
+
+int run_clip_adam(float* params, float* mu, float* nu, const float* grads, int64_t n,
+                  int32_t count, const bt_optimizer* opt, double* scratch, cudaStream_t s) {
+  BT_TRY(launch_sumsq_chunks(grads, n, scratch, s));
+  AdamParams ap{};
+  ap.params = params;
+  ap.mu = mu;
+  ap.nu = nu;
+  ap.grads = grads;
+  ap.n = n;
+  ap.norm_partials = scratch;
+  ap.num_norm_partials = (int)ceil_div64(n, kNormChunk);
+  ap.count = nullptr;
+  ap.step = count;
+  ap.lr = opt->lr;
+  ap.max_norm = opt->max_grad_norm;
+  ap.b1 = opt->b1;
+  ap.b2 = opt->b2;
+  ap.eps = opt->eps;
+  ap.eps_root = opt->eps_root;
+  ap.shadow = nullptr;
+  ap.shadow_lo = nullptr;
+  return launch_adam(ap, s);
+}
+
+}  // namespace
+
+// Scratch for the chunk sums comes from CUDA's stream-ordered allocator
+// (cudaMallocAsync / cudaFreeAsync on the caller's stream).
+extern "C" int bt_clip_adam(float* params, float* mu, float* nu, const float* grads, int64_t n,
+                            int32_t count, const bt_optimizer* opt, void* stream) {
+  BT_TRY(check_opt_args(params, mu, nu, grads, n, count, opt));
+  if (n == 0) return BT_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  double* scratch = nullptr;
+  BT_CUDA(cudaMallocAsync(&scratch, (size_t)ceil_div64(n, kNormChunk) * sizeof(double), s));
+  const int rc = run_clip_adam(params, mu, nu, grads, n, count, opt, scratch, s);
+  BT_CUDA(cudaFreeAsync(scratch, s));
+  return rc;
+}

@@ -230,6 +230,15 @@ BT_API int bt_learner_profile_read(bt_learner* learner, int32_t cls, char* name,
                                    int32_t name_len, double* total_ms, int64_t* launches);
 BT_API int64_t bt_learner_launch_count(const bt_learner* learner);
 
+/* ---- optimizer step (boonta/algorithms/ppo.py:182-191) ------------------------------------
+ * optax.chain(clip_by_global_norm(opt->max_grad_norm), adam(opt->lr, b1, b2, eps, eps_root))
+ * then optax.apply_updates, on flat fp32 device buffers of n elements, in place: params,
+ * mu, nu updated from grads. `count` = Adam steps already taken (the optax count before
+ * this step). Scratch (8 bytes per 8192 elements) comes from the stream-ordered allocator
+ * on `stream`. */
+BT_API int bt_clip_adam(float* params, float* mu, float* nu, const float* grads, int64_t n,
+                        int32_t count, const bt_optimizer* opt, void* stream);
+
 /* ---- multi-GPU (NCCL over NVLink) -------------------------------------------------------- */
 BT_API int bt_nccl_unique_id(void* out, int32_t size); /* size >= 128 bytes */
 BT_API int bt_learner_comm_init(bt_learner* learner, const void* unique_id, int32_t size);
