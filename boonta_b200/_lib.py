@@ -36,6 +36,7 @@ EXPORTS = (
     "bt_learner_loss_grads", "bt_learner_act", "bt_sample_categorical", "bt_nccl_unique_id",
     "bt_learner_comm_init", "bt_learner_profile", "bt_learner_profile_read",
     "bt_learner_launch_count", "bt_gemm_bf16", "bt_gemm_bf16x3", "bt_clip_adam",
+    "bt_clip_adam_noalloc",
 )
 
 
@@ -131,6 +132,7 @@ def lib() -> C.CDLL:
         "bt_gemm_bf16": (C.c_int, [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
         "bt_gemm_bf16x3": (C.c_int, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
         "bt_clip_adam": (C.c_int, [vp, vp, vp, vp, i64, i32, C.POINTER(OptimizerC), vp]),
+        "bt_clip_adam_noalloc": (C.c_int, [vp, vp, vp, vp, i64, i32, C.POINTER(OptimizerC), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -6,6 +6,8 @@
 // The global norm is summed in two fixed-order stages: per-chunk sums of squares (8192
 // elements per block) into scratch, then every Adam block adds the chunk sums in index
 // order, so the result is deterministic.
+#include <mutex>
+
 #include "kernels.cuh"
 
 using namespace bt;
@@ -58,4 +60,59 @@ extern "C" int bt_clip_adam(float* params, float* mu, float* nu, const float* gr
   const int rc = run_clip_adam(params, mu, nu, grads, n, count, opt, scratch, s);
   BT_CUDA(cudaFreeAsync(scratch, s));
   return rc;
+}
+
+// ---- the allocation-free variant ----------------------------------------------------------
+// Some callers cannot allocate device memory at the point where they run the optimizer: a
+// step running inside another framework's memory pool (an XLA FFI custom call runs after
+// XLA has reserved most of the device for its own allocator, so a cudaMalloc there can fail
+// or fragment memory XLA counts on), or a host with a fixed device-memory budget set at
+// start-up. bt_clip_adam_noalloc takes its scratch from a fixed array compiled into this
+// library instead.
+//
+// The array holds one partial sum per 8192-element chunk for up to kNoAllocChunks chunks:
+// 128 KB, so at most 134,217,728 elements per call. It lives in device memory of every GPU
+// that loads the library until the process exits. Every call writes all the chunk slots it
+// reads before reading them, so nothing has to be cleared between calls; the array keeps
+// the last call's partial sums. All calls share it: calls whose GPU work overlaps (two
+// streams, or two host threads) race on it and must be ordered by the caller.
+namespace {
+
+constexpr int kNoAllocChunks = 16384;
+constexpr int kNoAllocMaxDevices = 64;
+__device__ __align__(256) double g_noalloc_scratch[kNoAllocChunks];
+
+// Device address of g_noalloc_scratch per device, looked up once with that device current
+// (host code cannot use the symbol itself as a device pointer).
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mutex;
+
+int noalloc_scratch(double** out) {
+  int dev = 0;
+  BT_CUDA(cudaGetDevice(&dev));
+  BT_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    BT_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = static_cast<double*>(g_noalloc_ptr[dev]);
+  return BT_OK;
+}
+
+}  // namespace
+
+extern "C" int bt_clip_adam_noalloc(float* params, float* mu, float* nu, const float* grads,
+                                    int64_t n, int32_t count, const bt_optimizer* opt,
+                                    void* stream) {
+  BT_TRY(check_opt_args(params, mu, nu, grads, n, count, opt));
+  BT_CHECK_ARG(ceil_div64(n, kNormChunk) <= kNoAllocChunks,
+               "bt_clip_adam_noalloc: %lld elements exceed the fixed scratch limit of %lld "
+               "(use bt_clip_adam)",
+               (long long)n, (long long)kNoAllocChunks * kNormChunk);
+  if (n == 0) return BT_OK;
+  double* scratch = nullptr;
+  BT_TRY(noalloc_scratch(&scratch));
+  return run_clip_adam(params, mu, nu, grads, n, count, opt, scratch, (cudaStream_t)stream);
 }

@@ -239,6 +239,16 @@ BT_API int64_t bt_learner_launch_count(const bt_learner* learner);
 BT_API int bt_clip_adam(float* params, float* mu, float* nu, const float* grads, int64_t n,
                         int32_t count, const bt_optimizer* opt, void* stream);
 
+/* The same optimizer step without allocating anything (no counterpart in the reference).
+ * For callers that cannot allocate device memory where they run the optimizer, e.g. an XLA
+ * FFI custom call, which runs after XLA has reserved most of the GPU for its own pool.
+ * Scratch is a fixed 128 KB array compiled into the library (resident on every GPU that
+ * loads it until exit), so n is limited to 134,217,728 elements; larger n is rejected with
+ * BT_ERR_INVALID. The first call on a device looks the array's address up once. All calls
+ * share the array: calls whose GPU work overlaps race and must be ordered by the caller. */
+BT_API int bt_clip_adam_noalloc(float* params, float* mu, float* nu, const float* grads,
+                                int64_t n, int32_t count, const bt_optimizer* opt, void* stream);
+
 /* ---- multi-GPU (NCCL over NVLink) -------------------------------------------------------- */
 BT_API int bt_nccl_unique_id(void* out, int32_t size); /* size >= 128 bytes */
 BT_API int bt_learner_comm_init(bt_learner* learner, const void* unique_id, int32_t size);
