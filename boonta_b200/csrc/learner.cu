@@ -55,7 +55,8 @@ struct LayoutBuilder {
   void end() { off = align_up(off); }
 };
 
-int check_layer(const bt_layer& l, int in_dim, bool first) {
+int check_layer(const bt_layer& l, int in_dim, bool first, bool last, bool shared,
+                int precision) {
   BT_CHECK_ARG(l.features > 0, "layer with %d features", l.features);
   BT_CHECK_ARG(l.activation >= BT_ACT_NONE && l.activation <= BT_ACT_SILU, "bad activation %d",
                l.activation);
@@ -66,8 +67,12 @@ int check_layer(const bt_layer& l, int in_dim, bool first) {
                  in_dim);
     BT_CHECK_ARG(!l.layernorm, "LayerNorm after a conv is not supported");
   } else if (l.kind == BT_LAYER_GRU) {
-    ::bt::set_error("GRU layers are not supported by this learner build yet");
-    return BT_ERR_UNSUPPORTED;
+    if (!last || !shared || first || precision != BT_PREC_FP32) {
+      ::bt::set_error(
+          "a GRU layer is supported as the last layer of a shared torso after a Dense layer, "
+          "in fp32");
+      return BT_ERR_UNSUPPORTED;
+    }
   } else {
     BT_CHECK_ARG(l.kind == BT_LAYER_DENSE, "bad layer kind %d", l.kind);
   }
@@ -92,7 +97,7 @@ int build_layout(bt_learner* L) {
     int dim = net.obs_dim;
     for (int i = 0; i < n; ++i) {
       const bt_layer& l = layers[i];
-      BT_TRY(check_layer(l, dim, i == 0));
+      BT_TRY(check_layer(l, dim, i == 0, i == n - 1, L->shared, L->cfg.precision));
       LayerPlan lp;
       lp.kind = l.kind;
       lp.act = l.activation;
@@ -101,7 +106,25 @@ int build_layout(bt_learner* L) {
       BT_CHECK_ARG(!(L->cfg.precision != BT_PREC_FP32 && l.kind == BT_LAYER_CONV3X3),
                    "Conv3x3 layers run in fp32 only (precision %d requested)", L->cfg.precision);
       std::string p = std::string(names[t]) + "/" + std::to_string(i);
-      if (l.kind == BT_LAYER_CONV3X3) {
+      if (l.kind == BT_LAYER_GRU) {
+        const int H = l.features;
+        lp.kin = dim;
+        lp.kout = H;
+        lp.ncol = 3 * H;
+        lp.hidden = H;
+        lp.wi_off = b.off;
+        b.part(p + "/input_kernel", {dim, 3 * H});
+        b.part(p + "/input_bias", {3 * H});
+        b.end();
+        lp.wh_off = b.off;
+        b.part(p + "/recurrent_kernel", {H, 3 * H});
+        b.end();
+        lp.bhn_off = b.off;
+        b.part(p + "/hn_bias", {H});
+        b.end();
+        lp.w_off = lp.wi_off;
+        L->recurrent = true;
+      } else if (l.kind == BT_LAYER_CONV3X3) {
         lp.H = l.height;
         lp.W = l.width;
         lp.C = l.in_channels;
@@ -157,16 +180,6 @@ int build_layout(bt_learner* L) {
 
 namespace {
 
-template <class T>
-int dalloc(bt_learner* L, T** p, size_t count) {
-  if (count == 0) count = 1;
-  void* q = nullptr;
-  BT_CUDA(cudaMalloc(&q, count * sizeof(T)));
-  L->allocations.push_back(q);
-  *p = static_cast<T*>(q);
-  return BT_OK;
-}
-
 // Split-K factor for a dW GEMM: enough CTAs for ~2 waves on 148 SMs, at least 256
 // reduction rows per split.
 int pick_splits(int M, int N, int K) {
@@ -189,18 +202,25 @@ int allocate(bt_learner* L) {
   L->B = (int64_t)L->T * L->N;
   const int64_t B_global = L->B * world;
   BT_CHECK_ARG(M >= 1 && E >= 1, "num_minibatches %d / update_epochs %d", M, E);
-  BT_CHECK_ARG(B_global % M == 0, "batch %lld not divisible by num_minibatches %d",
-               (long long)B_global, M);
-  L->mb = (int)(B_global / M);
+  // Minibatches are over samples (t, n), or over whole env sequences for a recurrent torso
+  // (recurrent_ppo.py:269-276); `units` is what the permutation runs over.
+  const int64_t units_local = L->recurrent ? L->N : L->B;
+  const int64_t units_global = units_local * world;
+  BT_CHECK_ARG(units_global % M == 0, "%lld %s not divisible by num_minibatches %d",
+               (long long)units_global, L->recurrent ? "envs" : "samples", M);
+  L->mb = (int)(units_global / M);
+  int units_cap;
   if (world == 1) {
-    L->rows_cap = L->mb;
+    units_cap = L->mb;
   } else {
     // Hypergeometric share of a global minibatch: mean mb/world, std < sqrt(mb/world).
     const double mean = (double)L->mb / world;
     int cap = (int)std::ceil(mean + 16.0 * std::sqrt(mean) + 64.0);
-    L->rows_cap = std::min<int64_t>(std::min<int64_t>(cap, L->mb), L->B);
+    units_cap = (int)std::min<int64_t>(std::min<int64_t>(cap, L->mb), units_local);
   }
-  L->act_rows = std::max(L->rows_cap, L->N);
+  L->units_cap = units_cap;
+  L->rows_cap = L->recurrent ? units_cap * L->T : units_cap;
+  L->act_rows = std::max(L->rows_cap, L->recurrent ? 2 * L->N : L->N);
   const int R = L->act_rows;
 
   const int64_t P = L->num_params;
@@ -221,6 +241,10 @@ int allocate(bt_learner* L) {
   for (int t = 0; t < L->ntowers; ++t) {
     for (size_t i = 0; i < L->towers[t].layers.size(); ++i) {
       LayerPlan& lp = L->towers[t].layers[i];
+      if (lp.kind == BT_LAYER_GRU) {
+        BT_TRY(allocate_gru(L, lp));
+        continue;
+      }
       const size_t n = (size_t)R * lp.kout;
       BT_TRY(dalloc(L, &lp.z, n));
       BT_TRY(dalloc(L, &lp.h, n));
@@ -304,7 +328,7 @@ int allocate(bt_learner* L) {
   BT_TRY(dalloc(L, &L->act_out, (size_t)R * A));
   BT_TRY(dalloc(L, &L->act_val, R));
   if (world > 1) {
-    BT_TRY(dalloc(L, &L->local_idx, (size_t)E * M * L->rows_cap));
+    BT_TRY(dalloc(L, &L->local_idx, (size_t)E * M * L->units_cap));
     BT_TRY(dalloc(L, &L->local_counts, (size_t)E * M));
   }
   return allocate_tensor_core(L);
@@ -406,6 +430,7 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
   int in_ld = tp.in_dim;
   for (size_t i = 0; i < tp.layers.size(); ++i) {
     LayerPlan& lp = tp.layers[i];
+    if (lp.kind == BT_LAYER_GRU) break;  // the recurrent path runs the GRU (recurrent.cu)
     const bool last = i + 1 == tp.layers.size();
     const float* w = L->params + lp.w_off;
     if (lp.tc) {
@@ -450,8 +475,9 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
 }
 
 int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
-                   const int* count, cudaStream_t s) {
-  for (int i = (int)tp.layers.size() - 1; i >= 0; --i) {
+                   const int* count, cudaStream_t s, int top) {
+  if (top < 0) top = (int)tp.layers.size() - 1;
+  for (int i = top; i >= 0; --i) {
     LayerPlan& lp = tp.layers[i];
     const float* w = L->params + lp.w_off;
     if (lp.ln) {
@@ -508,18 +534,6 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
   }
   return BT_OK;
 }
-
-struct MinibatchInputs {
-  const float* obs;
-  const void* action;
-  const float* lp_old;
-  const float* v_old;
-  const float* adv;
-  const float* ret;
-  const int* idx;
-  const int* count;  // nullable
-  float inv_mb;
-};
 
 // Forward + loss + backward + gradient reduction for one minibatch. Leaves the
 // (unreduced across ranks) gradients in L->grads and the statistic sums in stat_slot.
@@ -581,7 +595,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   BT_K(L, kProfGemmDw, s, launch_skinny_dw(last_v.h, L->F_v, L->d_val, 1, rows, in.count,
                                            L->head_v_splits, L->head_v_part, s));
   for (int t = 0; t < L->ntowers; ++t)
-    BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
+    BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s, -1));
   BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
                                 with_norm ? L->norm_part : nullptr, s));
   return BT_OK;
@@ -749,6 +763,7 @@ extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int
                                  float* stats, void* stream) {
   BT_CHECK_ARG(L && perm, "bt_learner_update: null argument");
   BT_TRY(check_batch(L, batch));
+  if (L->recurrent) return recurrent_update(L, batch, perm, stats, (cudaStream_t)stream);
   const int world = std::max(1, L->cfg.world_size);
   BT_CHECK_ARG(world == 1 || L->comm, "world_size %d needs bt_learner_comm_init", world);
   cudaStream_t s = (cudaStream_t)stream;
@@ -771,7 +786,7 @@ extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int
     for (int m = 0; m < M; ++m) {
       const int i = e * M + m;
       if (world > 1) {
-        in.idx = L->local_idx + (size_t)i * L->rows_cap;
+        in.idx = L->local_idx + (size_t)i * L->units_cap;
         in.count = L->local_counts + i;
       } else {
         in.idx = perm + (size_t)e * Bg + (size_t)m * L->mb;
@@ -803,6 +818,10 @@ extern "C" int bt_learner_loss_grads(bt_learner* L, const bt_batch* batch, const
                                      const float* ret, const int32_t* indices, int32_t count,
                                      float* grads, float* stats, void* stream) {
   BT_CHECK_ARG(L && indices && adv && ret, "bt_learner_loss_grads: null argument");
+  if (L->recurrent) {
+    set_error("bt_learner_loss_grads: recurrent networks train through bt_learner_update");
+    return BT_ERR_UNSUPPORTED;
+  }
   BT_TRY(check_batch(L, batch));
   BT_CHECK_ARG(count >= 1 && count <= L->rows_cap, "count %d outside [1, %d]", count,
                L->rows_cap);
@@ -841,6 +860,10 @@ extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, cons
                               float temperature, void* action, float* log_prob, float* value,
                               void* stream) {
   BT_CHECK_ARG(L && obs && action && log_prob, "bt_learner_act: null argument");
+  if (L->recurrent) {
+    set_error("bt_learner_act: recurrent networks need a carry; not available in this build");
+    return BT_ERR_UNSUPPORTED;
+  }
   BT_CHECK_ARG(num >= 0 && num <= L->act_rows, "bt_learner_act: %d rows > capacity %d", num,
                L->act_rows);
   cudaStream_t s = (cudaStream_t)stream;

@@ -48,9 +48,24 @@ struct LayerPlan {
   bt::umma::Operands fwd_ops, dx_ops, dw_ops;
   int fwd_bn = 128;
   int dw_kbps = 1;
-  // GRU (recurrent torso)
+  // GRU (recurrent torso); rows are env-major (row = env * T + t)
   int hidden = 0;
   int64_t wi_off = 0, wh_off = 0, bhn_off = 0;
+  float* xp = nullptr;    // input projections [rows, 3H] (+ input bias)
+  float* hin = nullptr;   // carry entering each step (after the reset) [rows, H]
+  float* gr = nullptr;    // saved gates r, z, n and (h W_hn + b_hn) [rows, H] each
+  float* gz = nullptr;
+  float* gn = nullptr;
+  float* ghn = nullptr;
+  float* hp = nullptr;    // one step's hidden projection [envs, 3H]
+  float* dxp = nullptr;   // dL/d input projections [rows, 3H]
+  float* dhp = nullptr;   // dL/d hidden projections [rows, 3H]
+  float* dh_direct = nullptr;  // dh * z of the current step [envs, H]
+  float* dh_carry = nullptr;   // gradient flowing into the previous step's output [envs, H]
+  float* wi_part = nullptr;    // split partials of d[W_i; b_i], dW_h, db_hn
+  float* wh_part = nullptr;
+  float* bhn_part = nullptr;
+  int wi_splits = 1, wh_splits = 1, bhn_splits = 1;
   const float* pre() const { return ln ? y : z; }
 };
 
@@ -115,7 +130,14 @@ struct bt_learner {
   int T = 0, N = 0;
   int64_t B = 0;     // T*N on this rank
   int mb = 0;        // global minibatch size (rows, or envs for recurrent)
+  int units_cap = 0; // local minibatch capacity in permutation units (rows, or envs)
   int rows_cap = 0;  // local minibatch capacity (rows)
+  bool recurrent = false;
+  // recurrent path: per-minibatch row metadata
+  int* rnn_idx = nullptr;       // [rows] flat sample index t*N + n of row env*T + t
+  uint8_t* rnn_reset = nullptr; // [rows] reset the carry before this step
+  int* rnn_rows = nullptr;      // live rows (device) = live envs * T
+  float* tail_obs = nullptr;    // [2N, obs_dim] (first.obs[T-1], second.obs[T-1]) per env
   int act_rows = 0;  // rows of the activation buffers
   // heads
   float* d_out = nullptr;
@@ -150,6 +172,42 @@ struct bt_learner {
 };
 
 cudaEvent_t prof_event(bt_learner* L);
+
+template <class T>
+int dalloc(bt_learner* L, T** p, size_t count) {
+  if (count == 0) count = 1;
+  void* q = nullptr;
+  BT_CUDA(cudaMalloc(&q, count * sizeof(T)));
+  L->allocations.push_back(q);
+  *p = static_cast<T*>(q);
+  return BT_OK;
+}
+
+struct MinibatchInputs {
+  const float* obs;
+  const void* action;
+  const float* lp_old;
+  const float* v_old;
+  const float* adv;
+  const float* ret;
+  const int* idx;
+  const int* count;  // nullable
+  float inv_mb;
+};
+
+namespace bt {
+int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
+                  const int* count, cudaStream_t s);
+int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
+                   const int* count, cudaStream_t s, int top);
+int optimizer_step(bt_learner* L, int step, cudaStream_t s);
+int launch_gae_internal(const float* reward, const uint8_t* term, const uint8_t* trunc,
+                        const float* values, const float* bootstrap, int T, int N, double gamma,
+                        double lam, float* adv, float* ret, int* err, cudaStream_t stream);
+int allocate_gru(bt_learner* L, LayerPlan& lp);
+int recurrent_update(bt_learner* L, const bt_batch* b, const int32_t* perm, float* stats,
+                     cudaStream_t s);
+}  // namespace bt
 
 // Enqueue one kernel (or collective) launch `call`, counting it and, when profiling is
 // on, bracketing it with CUDA events on stream `s`.

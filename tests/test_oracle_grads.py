@@ -76,3 +76,40 @@ def test_statistics_follow_the_reference_definitions():
     assert stats[6] == pytest.approx(ev, rel=1e-5)
     assert stats[7] == pytest.approx(value.mean(), rel=1e-5, abs=1e-7)
     assert stats[4] == pytest.approx(mb["advantages"].mean(), rel=1e-6)
+
+
+def test_recurrent_bptt_gradient_matches_finite_differences():
+    """GRU torso (rnn.py:30-54 + flax GRUCell) with resets: analytic BPTT vs central
+    differences in float64."""
+    from boonta_b200.spec import GRU
+    from oracle import recurrent
+
+    spec = NetworkSpec(5, (Dense(6, "relu"), GRU(4)), head="categorical", action_dim=3)
+    rng = np.random.default_rng(3)
+    params = {k: v.astype(np.float64) + 0.1 * rng.standard_normal(v.shape)
+              for k, v in init_params(spec, seed=2).items()}
+    b, t = 3, 5
+    traj = {
+        "obs": rng.standard_normal((b, t, 5)),
+        "done": (rng.random((b, t)) < 0.3).astype(np.uint8),
+        "action": rng.integers(0, 3, (b, t)),
+        "log_prob": rng.standard_normal((b, t)) * 0.3 - 1.0,
+        "value": rng.standard_normal((b, t)),
+        "advantages": rng.standard_normal((b, t)),
+        "returns": rng.standard_normal((b, t)),
+    }
+    carry = rng.standard_normal((b, 4)) * 0.5
+    _, _, grads = recurrent.loss_and_grads(spec, PPO, params, traj, carry, dtype=np.float64)
+    h = 1e-6
+    for k, p in params.items():
+        flat = p.ravel()
+        for i in rng.choice(flat.size, size=min(5, flat.size), replace=False):
+            orig = flat[i]
+            flat[i] = orig + h
+            lp, _, _ = recurrent.loss_and_grads(spec, PPO, params, traj, carry, dtype=np.float64)
+            flat[i] = orig - h
+            lm, _, _ = recurrent.loss_and_grads(spec, PPO, params, traj, carry, dtype=np.float64)
+            flat[i] = orig
+            fd = (lp - lm) / (2 * h)
+            an = grads[k].ravel()[i]
+            assert abs(fd - an) <= 1e-6 + 1e-4 * abs(fd), (k, i, fd, an)
