@@ -605,6 +605,26 @@ int launch_ones_column(__nv_bfloat16* buf, int rows, int n, int ld, float one,
   return BT_OK;
 }
 
+// Zero rows [live, rows) of a bf16 [rows, ld] buffer: the tensor-core dW GEMMs read whole
+// 64-row K blocks, so the padding rows of a rank's minibatch must contribute nothing.
+__global__ void zero_tail_rows_kernel(__nv_bfloat16* buf, __nv_bfloat16* lo, int rows, int ld,
+                                      const int* count) {
+  const int live = live_rows(count, rows);
+  const int64_t n = (int64_t)(rows - live) * ld;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    buf[(int64_t)live * ld + i] = __float2bfloat16_rn(0.f);
+    if (lo) lo[(int64_t)live * ld + i] = __float2bfloat16_rn(0.f);
+  }
+}
+
+int launch_zero_tail_rows(__nv_bfloat16* buf, __nv_bfloat16* lo, int rows, int ld,
+                          const int* count, cudaStream_t stream) {
+  zero_tail_rows_kernel<<<kNumSMs, 256, 0, stream>>>(buf, lo, rows, ld, count);
+  BT_LAUNCH_CHECK("zero_tail_rows_kernel");
+  return BT_OK;
+}
+
 __global__ void to_bf16_kernel(const float* in, __nv_bfloat16* out, __nv_bfloat16* out_lo,
                                int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;

@@ -87,6 +87,8 @@ int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld
                        cudaStream_t stream);
 int launch_ones_column(__nv_bfloat16* buf, int rows, int n, int ld, float one,
                        cudaStream_t stream);
+int launch_zero_tail_rows(__nv_bfloat16* buf, __nv_bfloat16* lo, int rows, int ld,
+                          const int* count, cudaStream_t stream);
 int launch_to_bf16(const float* in, __nv_bfloat16* out, __nv_bfloat16* out_lo, int64_t n,
                    cudaStream_t stream);
 

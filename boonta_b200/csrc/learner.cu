@@ -594,6 +594,14 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
                                            L->head_pi_splits, L->head_pi_part, s));
   BT_K(L, kProfGemmDw, s, launch_skinny_dw(last_v.h, L->F_v, L->d_val, 1, rows, in.count,
                                            L->head_v_splits, L->head_v_part, s));
+  if (in.count) {
+    // padded minibatch (multi-GPU): the tensor-core dW GEMMs read whole 64-row blocks, so the
+    // dz rows past the live count must be zero
+    for (int t = 0; t < L->ntowers; ++t)
+      for (LayerPlan& lp : L->towers[t].layers)
+        if (lp.tc)
+          BT_K(L, kProfMisc, s, launch_zero_tail_rows(lp.dzb, lp.dzb_lo, rows, lp.kout, in.count, s));
+  }
   for (int t = 0; t < L->ntowers; ++t)
     BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s, -1));
   BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
