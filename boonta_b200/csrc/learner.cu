@@ -474,9 +474,21 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
   return BT_OK;
 }
 
+int stream_dep(bt_learner* L, cudaStream_t from, cudaStream_t to) {
+  if (from == to) return BT_OK;
+  cudaEvent_t e = L->fork_events[L->next_event++ % L->fork_events.size()];
+  BT_CUDA(cudaEventRecord(e, from));
+  BT_CUDA(cudaStreamWaitEvent(to, e, 0));
+  return BT_OK;
+}
+
+// Backward of layers top..0 of a tower. When s_dw is given, each layer's weight-gradient
+// GEMM runs on s_dw (after the layer's dz is ready) while the dX chain continues on s; s
+// waits for s_dw before returning.
 int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
-                   const int* count, cudaStream_t s, int top) {
+                   const int* count, cudaStream_t s, int top, cudaStream_t s_dw) {
   if (top < 0) top = (int)tp.layers.size() - 1;
+  const cudaStream_t sw = s_dw ? s_dw : s;
   for (int i = top; i >= 0; --i) {
     LayerPlan& lp = tp.layers[i];
     const float* w = L->params + lp.w_off;
@@ -485,15 +497,16 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
                                 lp.kout, lp.tc ? nullptr : lp.d_z, lp.tc ? lp.dzb : nullptr,
                                 lp.tc ? lp.dzb_lo : nullptr, lp.ln_part, lp.ln_blocks, count, s));
     }
+    BT_TRY(stream_dep(L, s, sw));  // dz of this layer is ready
     const int dm = lp.kin + 1, dn = lp.ncol;
     if (lp.tc) {
       // dW^T [kout, kin + 1] = dz^T [x, 1], stored transposed as [kin + 1, kout] partials
       umma::GemmShape sh{lp.kout, lp.kin + 1, rows, lp.dw_kbps, nullptr, count, L->err_d};
       umma::EpiDwT ep{lp.dw_part, lp.kout, (size_t)dm * dn, lp.kin + 1};
       if (L->x3) {
-        BT_K(L, kProfGemmDw, s, umma::launch_gemm<64, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, s));
+        BT_K(L, kProfGemmDw, sw, umma::launch_gemm<64, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
       } else {
-        BT_K(L, kProfGemmDw, s, umma::launch_gemm<128, true, true, false>(lp.dw_ops, sh, ep, lp.dw_splits, s));
+        BT_K(L, kProfGemmDw, sw, umma::launch_gemm<128, true, true, false>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
       }
       if (i > 0) {
         LayerPlan& prev = tp.layers[i - 1];
@@ -515,14 +528,14 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
       AIm2colT a{AIm2col{obs, idx, lp.H, lp.W, lp.C}};
       const int K = rows * lp.H * lp.W;
       BRows b{lp.d_z, lp.ncol, K};
-      BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, dm, dn, K, lp.dw_splits, s, nullptr, count,
+      BT_K(L, kProfGemmDw, sw, launch_gemm_simt(a, b, ep, dm, dn, K, lp.dw_splits, sw, nullptr, count,
                               lp.H * lp.W));
     } else {
       const float* in = i == 0 ? obs : tp.layers[i - 1].h;
       const int* gather = i == 0 ? idx : nullptr;
       ACols a{in, gather, lp.kin, lp.kin};
       BRows b{lp.d_z, lp.ncol, rows};
-      BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, dm, dn, rows, lp.dw_splits, s, nullptr, count));
+      BT_K(L, kProfGemmDw, sw, launch_gemm_simt(a, b, ep, dm, dn, rows, lp.dw_splits, sw, nullptr, count));
     }
     if (i > 0) {
       LayerPlan& prev = tp.layers[i - 1];
@@ -532,6 +545,7 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
       BT_K(L, kProfGemmDx, s, launch_gemm_simt(a, b, ep2, rows, lp.kin, lp.ncol, 1, s, count, nullptr));
     }
   }
+  BT_TRY(stream_dep(L, sw, s));
   return BT_OK;
 }
 
@@ -542,8 +556,13 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   const int rows = L->rows_cap;
   const bt_learner_config& c = L->cfg;
   BT_TRY(gather_obs(L, in.obs, in.idx, rows, in.count, s));
-  for (int t = 0; t < L->ntowers; ++t)
-    BT_TRY(forward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s));
+  // separate actor and critic towers run side by side (the critic on a side stream)
+  if (L->ntowers > 1) {
+    BT_TRY(stream_dep(L, s, L->side[0]));
+    BT_TRY(forward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, L->side[0]));
+  }
+  BT_TRY(forward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s));
+  if (L->ntowers > 1) BT_TRY(stream_dep(L, L->side[0], s));
   TowerPlan& t0 = L->towers[0];
   TowerPlan& tv = L->towers[L->ntowers - 1];
   LayerPlan& last_pi = t0.layers.back();
@@ -602,8 +621,13 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
         if (lp.tc)
           BT_K(L, kProfMisc, s, launch_zero_tail_rows(lp.dzb, lp.dzb_lo, rows, lp.kout, in.count, s));
   }
-  for (int t = 0; t < L->ntowers; ++t)
-    BT_TRY(backward_tower(L, L->towers[t], in.obs, in.idx, rows, in.count, s, -1));
+  if (L->ntowers > 1) {
+    BT_TRY(stream_dep(L, s, L->side[0]));
+    BT_TRY(backward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, L->side[0], -1,
+                          L->side[2]));
+  }
+  BT_TRY(backward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s, -1, L->side[1]));
+  if (L->ntowers > 1) BT_TRY(stream_dep(L, L->side[0], s));
   BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
                                 with_norm ? L->norm_part : nullptr, s));
   return BT_OK;
@@ -686,6 +710,17 @@ extern "C" int bt_learner_create(const bt_learner_config* cfg, bt_learner** out)
   bt_learner* L = new bt_learner();
   L->cfg = *cfg;
   int rc = cudaGetDevice(&L->device) == cudaSuccess ? BT_OK : BT_ERR_CUDA;
+  for (int i = 0; i < 4 && rc == BT_OK; ++i)
+    if (cudaStreamCreateWithFlags(&L->side[i], cudaStreamNonBlocking) != cudaSuccess) rc = BT_ERR_CUDA;
+  for (int i = 0; i < 64 && rc == BT_OK; ++i) {
+    cudaEvent_t e;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      rc = BT_ERR_CUDA;
+    } else {
+      L->fork_events.push_back(e);
+    }
+  }
+  if (rc != BT_OK) set_error("bt_learner_create: stream/event creation failed");
   if (rc == BT_OK) rc = build_layout(L);
   if (rc == BT_OK) rc = allocate(L);
   if (rc != BT_OK) {
@@ -700,6 +735,9 @@ extern "C" void bt_learner_destroy(bt_learner* L) {
   if (!L) return;
   if (L->comm) comm_destroy(L->comm);
   for (cudaEvent_t e : L->prof.pool) cudaEventDestroy(e);
+  for (cudaEvent_t e : L->fork_events) cudaEventDestroy(e);
+  for (cudaStream_t st : L->side)
+    if (st) cudaStreamDestroy(st);
   for (void* p : L->allocations) cudaFree(p);
   delete L;
 }

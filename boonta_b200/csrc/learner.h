@@ -169,7 +169,14 @@ struct bt_learner {
   Comm* comm = nullptr;
   std::vector<void*> allocations;
   Profiler prof;
+  // Side streams for independent work inside one update (the critic tower next to the
+  // actor's; dW GEMMs next to the dX chain). Work forks from and joins back into the
+  // caller's stream through events, so the call keeps the caller's stream order.
+  cudaStream_t side[4] = {nullptr, nullptr, nullptr, nullptr};
+  std::vector<cudaEvent_t> fork_events;
+  size_t next_event = 0;
 };
+
 
 cudaEvent_t prof_event(bt_learner* L);
 
@@ -196,10 +203,12 @@ struct MinibatchInputs {
 };
 
 namespace bt {
+// Make `to` wait for all work enqueued so far on `from`.
+int stream_dep(bt_learner* L, cudaStream_t from, cudaStream_t to);
 int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
                   const int* count, cudaStream_t s);
 int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
-                   const int* count, cudaStream_t s, int top);
+                   const int* count, cudaStream_t s, int top, cudaStream_t s_dw = nullptr);
 int optimizer_step(bt_learner* L, int step, cudaStream_t s);
 int launch_gae_internal(const float* reward, const uint8_t* term, const uint8_t* trunc,
                         const float* values, const float* bootstrap, int T, int N, double gamma,
