@@ -46,33 +46,88 @@ def peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
-# ---- algorithmic work per minibatch ------------------------------------------------------
-def gemm_flops(w) -> dict:
-    """FLOPs of one minibatch's GEMMs by class (forward, dX, dW), dense count, incl. heads."""
+# ---- algorithmic work per update, by kernel class ---------------------------------------
+def class_work(w) -> dict:
+    """{kernel class: (FLOPs, bytes)} of one learner update, counted algorithmically: every
+    GEMM as 2*M*N*K (the split-bf16 mode issues three products per term; they are not
+    counted), every operand read once and every output written once, in the precision the
+    path stores it (bf16 2 B, split-bf16 pairs 4 B, fp32 4 B)."""
     net = w.network
     rows = w.minibatch_size
-    f = {"gemm_fwd": 0.0, "gemm_dx": 0.0, "gemm_dw": 0.0}
+    steps = w.ppo.update_epochs * w.ppo.num_minibatches
+    tc = w.precision in ("bf16", "bf16x3")
+    e = {"fp32": 4, "bf16": 2, "bf16x3": 4}[w.precision]
+    out = {k: [0.0, 0.0] for k in ("gemm_fwd", "gemm_dx", "gemm_dw", "heads_loss")}
+    feats = []
     for tower in net.towers():
         dim = net.obs_dim
         for i, layer in enumerate(tower):
+            last = i + 1 == len(tower)
             if isinstance(layer, Conv3x3):
                 m = rows * layer.height * layer.width
                 k, n = 9 * layer.in_channels + 1, layer.features
-                out = layer.height * layer.width * layer.features
+                width = layer.height * layer.width * layer.features
+                a_bytes = rows * dim * 4
             else:
                 m, k, n = rows, dim + 1, layer.features
-                out = layer.features
-            f["gemm_fwd"] += 2.0 * m * k * n
-            f["gemm_dw"] += 2.0 * m * k * n
+                width = n
+                a_bytes = rows * dim * (e if tc else 4)
+            w_bytes = k * n * (e if tc else 4)
+            out_fwd = rows * width * (4 + (e if tc else 4) + (4 if (last and tc) else 0))
+            out["gemm_fwd"][0] += 2.0 * m * k * n
+            out["gemm_fwd"][1] += a_bytes + w_bytes + out_fwd
+            dz_bytes = rows * width * (e if tc else 4)
+            out["gemm_dw"][0] += 2.0 * m * k * n
+            out["gemm_dw"][1] += dz_bytes + a_bytes + rows * 0 + k * n * 4
             if i > 0:
-                f["gemm_dx"] += 2.0 * m * (k - 1) * n
-            dim = out
-    # head weight gradients ([F+1, A] and [F+1, 1]) run as dW GEMMs
-    lay = param_layout(net)
-    fpi = lay["actor_head/kernel"].shape[0]
-    fv = lay["critic_head/kernel"].shape[0]
-    f["gemm_dw"] += 2.0 * rows * ((fpi + 1) * net.action_dim + (fv + 1))
-    return f
+                out["gemm_dx"][0] += 2.0 * m * (k - 1) * n
+                out["gemm_dx"][1] += dz_bytes + w_bytes + rows * dim * (4 + (e if tc else 4))
+            dim = width
+        feats.append(dim)
+    f_pi = feats[0]
+    f_v = feats[-1]
+    a = net.action_dim
+    nf = f_pi + (0 if net.shared else f_v)
+    # heads: features + pre-activations read, dz written, head outputs' gradients written
+    out["heads_loss"][0] += 2.0 * rows * (f_pi * a + f_v) * 2
+    out["heads_loss"][1] += rows * nf * (4 + 4 + (e if tc else 4)) + rows * (a + 1) * 4 + rows * 20
+    return {k: (v[0] * steps, v[1] * steps) for k, v in out.items()}
+
+
+def roofline(w, prof: dict, pk: dict, pk_kind: str) -> dict:
+    """Roofline of the class with the most device time: its algorithmic FLOPs and bytes per
+    update against the measured bf16 tensor peak and HBM copy bandwidth; the bound is the
+    resource whose roofline time is longer."""
+    work = class_work(w)
+    if not prof:
+        return {"bound": None, "achieved": None, "peak": None, "unit": None, "frac": None,
+                "traffic": None}
+    cls, (ms, n) = max(prof.items(), key=lambda kv: kv[1][0])
+    sec = ms / 1000.0
+    tflops_peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    gbs_peak = pk["hbm_gbs"]
+    line = {"kernel": cls, "launches": n, "device_ms": ms, "peaks": pk_kind}
+    if cls in work:
+        flops, nbytes = work[cls]
+        t_tensor = flops / (tflops_peak * 1e12)
+        t_hbm = nbytes / (gbs_peak * 1e9)
+        if t_tensor >= t_hbm:
+            ach = flops / sec / 1e12
+            line.update(bound="tensor", achieved=ach, peak=tflops_peak, unit="TFLOP/s",
+                        frac=ach / tflops_peak, algorithmic_per_launch=flops / n)
+        else:
+            ach = nbytes / sec / 1e9
+            line.update(bound="hbm", achieved=ach, peak=gbs_peak, unit="GB/s",
+                        frac=ach / gbs_peak, algorithmic_per_launch=nbytes / n)
+    else:
+        line.update(bound="hbm", achieved=None, peak=gbs_peak, unit="GB/s", frac=None)
+    line["traffic"] = TRAFFIC.get((w.name, w.precision, cls))
+    return line
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch, from ncu captures of the same
+# workload (profiles/ summaries give the commands); None when not captured.
+TRAFFIC = {}
 
 
 def gae_bytes(w) -> float:
@@ -313,11 +368,15 @@ def main():
     ms = float(t.item())
     value = world * w.batch_size / (ms / 1000.0)
 
-    # per-kernel-class device time of one more update (events around every launch)
+    # Per-kernel-class device time: the same K steps again, with CUDA events recorded around
+    # every launch on the stream it is launched on (a second timed region, so the events'
+    # host cost cannot touch the headline number).
     lrn.profile(True)
-    lrn.update(roll, perms[0], stats=True)
+    for i in range(args.steps):
+        lrn.update(roll, perms[args.warmup + i], stats=True)
     torch.cuda.synchronize()
-    prof = lrn.profile_read()
+    prof = {k: (ms_ / max(args.steps, 1), n_ // max(args.steps, 1))
+            for k, (ms_, n_) in lrn.profile_read().items()}
     lrn.profile(False)
 
     # end to end: rollout from pinned host memory, statistics back to the host, every step
@@ -352,21 +411,7 @@ def main():
         return
 
     pk, pk_kind = peaks()
-    flops = gemm_flops(w)
-    updates_mb = w.ppo.update_epochs * w.ppo.num_minibatches
-    top = max(prof.items(), key=lambda kv: kv[1][0]) if prof else ("none", (0.0, 1))
-    cls, (tot_ms, n_launch) = top
-    avg_s = tot_ms / 1000.0 / max(n_launch, 1)
-    if cls.startswith("gemm"):
-        per_launch = flops[cls] * updates_mb / max(n_launch, 1)
-        achieved = per_launch / avg_s / 1e12
-        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None, "kernel": cls,
-                "note": f"peak = bf16 sustained ({pk_kind}); fp32 CUDA-core GEMM in this build"}
-    else:
-        roof = {"bound": "hbm", "achieved": None, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": None, "traffic": None, "kernel": cls}
+    roof = roofline(w, prof, pk, pk_kind)
     if "gae" in prof:
         g_ms, g_n = prof["gae"]
         gae_gbs = gae_bytes(w) / (g_ms / 1000.0 / g_n) / 1e9

@@ -33,6 +33,11 @@ size_t heads_smem_bytes(int F_pi, int F_v, int A, bool /*shared*/) {
   return floats * 4 + (size_t)kHeadWarps * kNumStatSums * 8 + 64;
 }
 
+__device__ __forceinline__ float4 act4(float4 z, int act) {
+  return make_float4(act_forward(z.x, act), act_forward(z.y, act), act_forward(z.z, act),
+                     act_forward(z.w, act));
+}
+
 __device__ __forceinline__ void load_row(const float* src, int F, int lane, float4 (&v)[kMaxChunks]) {
 #pragma unroll
   for (int i = 0; i < kMaxChunks; ++i) {
@@ -101,8 +106,6 @@ __global__ void __launch_bounds__(kHeadThreads) heads_loss_kernel(HeadsParams p)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int live = live_rows(p.count, p.rows);
-  // the critic's pre-activations: the actor's when the torso is shared
-  const float* pre_v = shared ? p.pre_pi : p.pre_v;
 
   for (int i = tid; i < F * A; i += kHeadThreads) {
     const int k = i / A, j = i - k * A;
@@ -131,11 +134,15 @@ __global__ void __launch_bounds__(kHeadThreads) heads_loss_kernel(HeadsParams p)
 
   for (int row = blockIdx.x * kHeadWarps + warp; row < live; row += gridDim.x * kHeadWarps) {
     const int flat = p.idx ? p.idx[row] : row;
+    // the towers' pre-activations; the head input is act(pre), recomputed here
     float4 f[kMaxChunks], fv[kMaxChunks], zp[kMaxChunks], zv[kMaxChunks];
-    load_row(p.f_pi + (size_t)row * F, F, lane, f);
-    if (!shared) load_row(p.f_v + (size_t)row * Fv, Fv, lane, fv);
-    if (p.act_pi != BT_ACT_NONE) load_row(p.pre_pi + (size_t)row * F, F, lane, zp);
-    if (!shared && p.act_v != BT_ACT_NONE) load_row(pre_v + (size_t)row * Fv, Fv, lane, zv);
+    load_row(p.f_pi + (size_t)row * F, F, lane, zp);
+    if (!shared) load_row(p.f_v + (size_t)row * Fv, Fv, lane, zv);
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      f[i] = act4(zp[i], p.act_pi);
+      if (!shared) fv[i] = act4(zv[i], p.act_v);
+    }
     const float lp_old = p.lp_old[flat];
     const float adv = p.adv[flat];
     const float ret = p.ret[flat];
@@ -348,10 +355,10 @@ int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
   return BT_OK;
 }
 
-// Head outputs only (bootstrap values, act): one warp per row.
+// Head outputs only (bootstrap values, act): one warp per row; the head input is act(f).
 __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v, int Fv,
                                      const float* w_pi, const float* w_v, int A, int rows,
-                                     float* out, float* value) {
+                                     int act_pi, int act_v, float* out, float* value) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -359,7 +366,8 @@ __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v,
   if (out) {
     for (int j = 0; j < A; ++j) {
       float acc = 0.f;
-      for (int k = lane; k < F; k += 32) acc = fmaf(f[k], w_pi[(size_t)k * A + j], acc);
+      for (int k = lane; k < F; k += 32)
+        acc = fmaf(act_forward(f[k], act_pi), w_pi[(size_t)k * A + j], acc);
       acc = warp_sum(acc);
       if (lane == 0) out[(size_t)warp * A + j] = acc + w_pi[(size_t)F * A + j];
     }
@@ -367,18 +375,18 @@ __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v,
   if (value) {
     const float* fv = f_v + (size_t)warp * Fv;
     float acc = 0.f;
-    for (int k = lane; k < Fv; k += 32) acc = fmaf(fv[k], w_v[k], acc);
+    for (int k = lane; k < Fv; k += 32) acc = fmaf(act_forward(fv[k], act_v), w_v[k], acc);
     acc = warp_sum(acc);
     if (lane == 0) value[warp] = acc + w_v[Fv];
   }
 }
 
 int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
-                         const float* w_v, int A, int rows, float* out, float* value,
-                         cudaStream_t stream) {
+                         const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
+                         float* value, cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
-  heads_forward_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(f_pi, F, f_v, Fv, w_pi, w_v,
-                                                                     A, rows, out, value);
+  heads_forward_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(
+      f_pi, F, f_v, Fv, w_pi, w_v, A, rows, act_pi, act_v, out, value);
   BT_LAUNCH_CHECK("heads_forward_kernel");
   return BT_OK;
 }

@@ -499,9 +499,10 @@ int launch_local_indices(const int* perm, int num_slices, int slice_len, int /*u
 // gradient), the rows of a split staged 64 at a time in shared memory; each thread keeps
 // its n accumulators in registers and sums rows in order.
 template <int NMAX>
-__global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, const float* d,
-                                                        int n, int rows, const int* count,
-                                                        int rows_per_split, float* out) {
+__global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, int act,
+                                                        const float* d, int n, int rows,
+                                                        const int* count, int rows_per_split,
+                                                        float* out) {
   __shared__ float ds[64][NMAX];
   const int k = blockIdx.x * 128 + threadIdx.x;
   const int live = live_rows(count, rows);
@@ -528,6 +529,10 @@ __global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, c
                                    : ((rr < nr && k == F) ? 1.f : 0.f);
       }
 #pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (k < F) fk[u] = act_forward(fk[u], act);
+      }
+#pragma unroll
       for (int u = 0; u < 8; ++u)
 #pragma unroll
         for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(fk[u], ds[r8 + u][j], acc[j]);
@@ -539,21 +544,21 @@ __global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, c
   }
 }
 
-int launch_skinny_dw(const float* f, int F, const float* d, int n, int rows, const int* count,
-                     int splits, float* out, cudaStream_t stream) {
+int launch_skinny_dw(const float* f, int F, int act, const float* d, int n, int rows,
+                     const int* count, int splits, float* out, cudaStream_t stream) {
   const int rps = ceil_div(rows, splits);
   dim3 grid(ceil_div(F + 1, 128), splits);
   if (n <= 1) {
-    skinny_dw_kernel<1><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+    skinny_dw_kernel<1><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
   } else if (n <= 8) {
-    skinny_dw_kernel<8><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+    skinny_dw_kernel<8><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
   } else if (n <= 16) {
-    skinny_dw_kernel<16><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+    skinny_dw_kernel<16><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
   } else if (n <= 32) {
-    skinny_dw_kernel<32><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+    skinny_dw_kernel<32><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
   } else {
     BT_CHECK_ARG(n <= 64, "skinny dW with %d outputs", n);
-    skinny_dw_kernel<64><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+    skinny_dw_kernel<64><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
   }
   BT_LAUNCH_CHECK("skinny_dw_kernel");
   return BT_OK;

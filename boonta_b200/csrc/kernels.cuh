@@ -15,7 +15,7 @@ struct HeadsParams {
   int rows;          // capacity rows of the minibatch buffers
   const int* count;  // nullable: live rows
   const int* idx;    // [rows] flat sample index (into [T*N] arrays); nullable = identity
-  const float* f_pi;
+  const float* f_pi;  // pre-activations of the tower outputs; the head input is act(f)
   int F_pi;
   const float* f_v;  // == f_pi when the torso is shared
   int F_v;
@@ -42,11 +42,7 @@ struct HeadsParams {
   __nv_bfloat16* d_fv_b;
   __nv_bfloat16* d_fpi_b_lo;  // when set: the low halves of split bf16 pairs
   __nv_bfloat16* d_fv_b_lo;
-  const float* pre_pi;
-  const float* post_pi;
-  int act_pi;
-  const float* pre_v;
-  const float* post_v;
+  int act_pi;  // activation of the tower outputs (applied to f, differentiated for dL/dpre)
   int act_v;
   double* stat_partials;   // [gridDim.x][kNumStatSums]
   float* dscale_partials;  // [gridDim.x][A] (gaussian)
@@ -55,8 +51,8 @@ struct HeadsParams {
 int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream);
 size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared);
 int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
-                         const float* w_v, int A, int rows, float* out, float* value,
-                         cudaStream_t stream);
+                         const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
+                         float* value, cudaStream_t stream);
 
 // LayerNorm (flax, epsilon 1e-6, fast variance) fused with the following activation.
 int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act,
@@ -69,9 +65,9 @@ int launch_ln_backward(const float* d_y, const float* z, const float* mean, cons
                        __nv_bfloat16* d_zb_lo, float* partials, int blocks, const int* count,
                        cudaStream_t stream);
 
-// [F + 1, n] split partials [splits][F + 1][n] of [f, 1]^T d, for narrow d (n <= 64).
-int launch_skinny_dw(const float* f, int F, const float* d, int n, int rows, const int* count,
-                     int splits, float* out, cudaStream_t stream);
+// [F + 1, n] split partials [splits][F + 1][n] of [act(f), 1]^T d, for narrow d (n <= 64).
+int launch_skinny_dw(const float* f, int F, int act, const float* d, int n, int rows,
+                     const int* count, int splits, float* out, cudaStream_t stream);
 
 // bf16 operands of the tensor-core path. Every bf16 writer takes an optional `lo` buffer:
 // when set, the value is stored as the pair hi = bf16(x), lo = bf16(x - hi) (the split

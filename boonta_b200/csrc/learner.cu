@@ -263,12 +263,14 @@ int allocate(bt_learner* L) {
       const int dm = lp.kin + 1, dn = lp.ncol;
       const int dk = lp.kind == BT_LAYER_CONV3X3 ? L->rows_cap * lp.H * lp.W : L->rows_cap;
       if (lp.tc) {
-        // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1]; about one wave of CTAs,
-        // at least 8 K blocks (512 rows) per split
+        // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1]. These GEMMs run on a side
+        // stream next to the dX chain, so they need not fill the GPU: at most one wave of
+        // CTAs and at least 32 K blocks (2048 rows) per split keep the split-K partials
+        // (written and re-read by the reduction) small.
         const int bn = c.precision == BT_PREC_BF16X3 ? 64 : 128;
         const int tiles = ceil_div(lp.kout, 128) * ceil_div(lp.kin + 1, bn);
         const int nkb = ceil_div(L->rows_cap, 64);
-        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 8));
+        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 32));
         lp.dw_kbps = ceil_div(nkb, splits);
         lp.dw_splits = ceil_div(nkb, lp.dw_kbps);
       } else {
@@ -431,14 +433,15 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
   for (size_t i = 0; i < tp.layers.size(); ++i) {
     LayerPlan& lp = tp.layers[i];
     if (lp.kind == BT_LAYER_GRU) break;  // the recurrent path runs the GRU (recurrent.cu)
-    const bool last = i + 1 == tp.layers.size();
     const float* w = L->params + lp.w_off;
     if (lp.tc) {
       umma::GemmShape sh{rows, lp.kout, lp.kin, ceil_div(lp.kin, umma::BK), count, nullptr,
                          L->err_d};
+      // the last layer's output is consumed through its pre-activation (the heads apply
+      // the activation), so no fp32 copy of it is written
       umma::EpiFwd ep{w + (size_t)lp.kin * lp.kout, lp.z, lp.kout, lp.ln ? nullptr : lp.hb,
-                      lp.ln ? nullptr : lp.hb_lo, lp.ldh, (last && !lp.ln) ? lp.h : nullptr,
-                      lp.kout, lp.ln ? BT_ACT_NONE : lp.act};
+                      lp.ln ? nullptr : lp.hb_lo, lp.ldh, nullptr, lp.kout,
+                      lp.ln ? BT_ACT_NONE : lp.act};
       if (L->x3) {
         BT_K(L, kProfGemmFwd, s, umma::launch_gemm<64, false, true, true>(lp.fwd_ops, sh, ep, 1, s));
       } else if (lp.fwd_bn == 256) {
@@ -448,8 +451,8 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       }
       if (lp.ln) {
         BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act,
-                                                 lp.y, last ? lp.h : nullptr, lp.hb, lp.hb_lo,
-                                                 lp.ldh, lp.mean, lp.rstd, count, s));
+                                                 lp.y, nullptr, lp.hb, lp.hb_lo, lp.ldh, lp.mean,
+                                                 lp.rstd, count, s));
       }
     } else if (lp.kind == BT_LAYER_CONV3X3) {
       AIm2col a{in, gather, lp.H, lp.W, lp.C};
@@ -571,9 +574,9 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   hp.rows = rows;
   hp.count = in.count;
   hp.idx = in.idx;
-  hp.f_pi = last_pi.h;
+  hp.f_pi = last_pi.pre();  // the heads apply the activation themselves
   hp.F_pi = L->F_pi;
-  hp.f_v = last_v.h;
+  hp.f_v = last_v.pre();
   hp.F_v = L->F_v;
   hp.w_pi = L->params + L->head_pi_off;
   hp.w_v = L->params + L->head_v_off;
@@ -598,21 +601,21 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   hp.d_fv_b = (!L->shared && last_v.tc && !last_v.ln) ? last_v.dzb : nullptr;
   hp.d_fpi_b_lo = hp.d_fpi_b ? last_pi.dzb_lo : nullptr;
   hp.d_fv_b_lo = hp.d_fv_b ? last_v.dzb_lo : nullptr;
-  hp.pre_pi = last_pi.pre();
-  hp.post_pi = last_pi.h;
   hp.act_pi = last_pi.act;
-  hp.pre_v = last_v.pre();
-  hp.post_v = last_v.h;
   hp.act_v = last_v.act;
   hp.stat_partials = L->stat_part;
   hp.dscale_partials = L->dscale_part;
   BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
   BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
-  // head weight gradients: [F + 1, A] = [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value
-  BT_K(L, kProfGemmDw, s, launch_skinny_dw(last_pi.h, L->F_pi, L->d_out, L->A, rows, in.count,
-                                           L->head_pi_splits, L->head_pi_part, s));
-  BT_K(L, kProfGemmDw, s, launch_skinny_dw(last_v.h, L->F_v, L->d_val, 1, rows, in.count,
-                                           L->head_v_splits, L->head_v_part, s));
+  // head weight gradients: [F + 1, A] = [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value,
+  // on a side stream next to the towers' backward
+  cudaStream_t sh = L->side[3];
+  BT_TRY(stream_dep(L, s, sh));
+  BT_K(L, kProfGemmDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out, L->A,
+                                            rows, in.count, L->head_pi_splits, L->head_pi_part,
+                                            sh));
+  BT_K(L, kProfGemmDw, sh, launch_skinny_dw(last_v.pre(), L->F_v, last_v.act, L->d_val, 1, rows,
+                                            in.count, L->head_v_splits, L->head_v_part, sh));
   if (in.count) {
     // padded minibatch (multi-GPU): the tensor-core dW GEMMs read whole 64-row blocks, so the
     // dz rows past the live count must be zero
@@ -628,6 +631,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   }
   BT_TRY(backward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s, -1, L->side[1]));
   if (L->ntowers > 1) BT_TRY(stream_dep(L, L->side[0], s));
+  BT_TRY(stream_dep(L, sh, s));
   BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
                                 with_norm ? L->norm_part : nullptr, s));
   return BT_OK;
@@ -646,9 +650,9 @@ int bootstrap_and_gae(bt_learner* L, const bt_batch* b, cudaStream_t s) {
   TowerPlan& tv = L->towers[L->ntowers - 1];
   BT_TRY(gather_obs(L, b->bootstrap_obs, nullptr, L->N, nullptr, s));
   BT_TRY(forward_tower(L, tv, b->bootstrap_obs, nullptr, L->N, nullptr, s));
-  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(tv.layers.back().h, L->F_v, tv.layers.back().h, L->F_v,
+  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(tv.layers.back().pre(), L->F_v, tv.layers.back().pre(), L->F_v,
                               L->params + L->head_pi_off, L->params + L->head_v_off, L->A, L->N,
-                              nullptr, L->boot, s));
+                              tv.layers.back().act, tv.layers.back().act, nullptr, L->boot, s));
   BT_K(L, kProfGae, s, launch_gae_internal(b->reward, b->terminated, b->truncated, b->value, L->boot, L->T,
                              L->N, L->cfg.ppo.gamma, L->cfg.ppo.gae_lambda, L->adv, L->ret,
                              L->err_d, s));
@@ -918,9 +922,10 @@ extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, cons
     BT_TRY(forward_tower(L, L->towers[t], obs, nullptr, num, nullptr, s));
   TowerPlan& t0 = L->towers[0];
   TowerPlan& tv = L->towers[L->ntowers - 1];
-  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(t0.layers.back().h, L->F_pi, tv.layers.back().h, L->F_v,
+  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(t0.layers.back().pre(), L->F_pi, tv.layers.back().pre(), L->F_v,
                               L->params + L->head_pi_off, L->params + L->head_v_off, L->A, num,
-                              L->act_out, value ? value : L->act_val, s));
+                              t0.layers.back().act, tv.layers.back().act, L->act_out,
+                              value ? value : L->act_val, s));
   BT_K(L, kProfMisc, s, launch_sample(L->act_out,
                        L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr,
                        L->cfg.network.head, L->A, num, noise, temperature, action, log_prob, s));

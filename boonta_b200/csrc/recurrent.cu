@@ -270,10 +270,11 @@ int recurrent_heads(bt_learner* L, LayerPlan& g, const MinibatchInputs& in, cons
   hp.dscale_partials = L->dscale_part;
   BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
   BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
-  BT_K(L, kProfGemmDw, s, launch_skinny_dw(g.h, L->F_pi, L->d_out, L->A, L->rows_cap, rows_live,
-                                           L->head_pi_splits, L->head_pi_part, s));
-  BT_K(L, kProfGemmDw, s, launch_skinny_dw(g.h, L->F_v, L->d_val, 1, L->rows_cap, rows_live,
-                                           L->head_v_splits, L->head_v_part, s));
+  BT_K(L, kProfGemmDw, s, launch_skinny_dw(g.h, L->F_pi, BT_ACT_NONE, L->d_out, L->A,
+                                           L->rows_cap, rows_live, L->head_pi_splits,
+                                           L->head_pi_part, s));
+  BT_K(L, kProfGemmDw, s, launch_skinny_dw(g.h, L->F_v, BT_ACT_NONE, L->d_val, 1, L->rows_cap,
+                                           rows_live, L->head_v_splits, L->head_v_part, s));
   return BT_OK;
 }
 
@@ -343,8 +344,8 @@ int recurrent_update(bt_learner* L, const bt_batch* b, const int32_t* perm, floa
   BT_TRY(gru_forward(L, g, prev.h, b->last_carry, nullptr, nullptr, L->rnn_rows, N, 2, s));
   BT_K(L, kProfHeadsFwd, s, launch_heads_forward(g.h, L->F_v, g.h, L->F_v,
                                                  L->params + L->head_pi_off,
-                                                 L->params + L->head_v_off, L->A, 2 * N, nullptr,
-                                                 L->act_val, s));
+                                                 L->params + L->head_v_off, L->A, 2 * N,
+                                                 BT_ACT_NONE, BT_ACT_NONE, nullptr, L->act_val, s));
   BT_CUDA(cudaMemcpy2DAsync(L->boot, 4, L->act_val + 1, 8, 4, N, cudaMemcpyDeviceToDevice, s));
   BT_K(L, kProfGae, s, launch_gae_internal(b->reward, b->terminated, b->truncated, b->value,
                                            L->boot, T, N, L->cfg.ppo.gamma, L->cfg.ppo.gae_lambda,
