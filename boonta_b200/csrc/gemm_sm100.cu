@@ -49,6 +49,33 @@ int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t oute
   return BT_OK;
 }
 
+int encode_tile_map(CUtensorMap* map, const void* base, bool f32, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, int swizzle_bytes) {
+  BT_TRY(resolve_encode());
+  const uint32_t esize = f32 ? 4 : 2;
+  BT_CHECK_ARG(((uintptr_t)base & 15) == 0, "tensor map base %p not 16-byte aligned", base);
+  BT_CHECK_ARG(row_bytes % 16 == 0, "tensor map row stride %llu not a multiple of 16",
+               (unsigned long long)row_bytes);
+  BT_CHECK_ARG(32 * esize == (uint32_t)swizzle_bytes, "epilogue tile map: %d-byte swizzle for "
+               "%u-byte elements", swizzle_bytes, esize);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for an epilogue tile map: dims %llu x %llu, "
+              "stride %llu", (int)r, (unsigned long long)inner, (unsigned long long)outer,
+              (unsigned long long)row_bytes);
+    return BT_ERR_CUDA;
+  }
+  return BT_OK;
+}
+
 }  // namespace umma
 }  // namespace bt
 

@@ -36,7 +36,13 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle span of bf16
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each on half the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13;
+constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13,
+              kErrTimeoutEpiIn = 14;
+// Store epilogues (kTma): each epilogue warp owns an 8 KB piece of the (then idle) stage
+// ring: a 32 x 32 fp32 sub-tile (4 KB, 128-byte swizzle) and two 32 x 32 bf16 sub-tiles
+// (2 KB each, 64-byte swizzle), written in the swizzled order the tensor maps expect and
+// sent out by TMA stores.
+constexpr int kEpiWarpBytes = 8192;
 
 // Shared-memory budget: a ring of stages of A (and, in the split mode, A_lo) and B (B_lo)
 // tiles, each stage 1024-byte aligned. The ring is sized so that two to three CTAs fit on
@@ -63,6 +69,27 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Tiled bulk store shared -> global (coordinates {x = column, y = row}); the engine clips
+// the box at the tensor's bounds. Completion is tracked per thread through bulk groups.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The source shared memory of every committed store may be overwritten.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every committed store has been performed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
@@ -164,15 +191,19 @@ struct Operands {
 
 template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
 __global__ void __launch_bounds__(kThreads)
-    umma_gemm_kernel(const __grid_constant__ Operands ops, GemmShape sh, Epi epi) {
+    umma_gemm_kernel(const __grid_constant__ Operands ops, GemmShape sh,
+                     const __grid_constant__ Epi epi) {
   using C = Cfg<BN, X3, Epi::kDeep>;
+  static_assert(!Epi::kTma || C::kStages * C::kStageBytes >= kEpiWarps * kEpiWarpBytes,
+                "store epilogue needs 8 KB of the stage ring per epilogue warp");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* acc_full = empty + C::kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* epi_in = acc_full + 1;  // one per epilogue warp (store epilogues' input tiles)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_in + kEpiWarps);
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -193,6 +224,8 @@ __global__ void __launch_bounds__(kThreads)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
+    if (Epi::kTma)
+      for (int w = 0; w < kEpiWarps; ++w) mbar_init(&epi_in[w], 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, BN);
@@ -279,6 +312,65 @@ __global__ void __launch_bounds__(kThreads)
       }
       mma_commit(acc_full);
     }
+  } else if constexpr (Epi::kTma) {
+    // Store epilogue, warps 2..9: lane quarter q = warp % 4 (rows q*32 .. q*32+31, thread =
+    // row), column half = (warp - 2) / 4, 32 columns at a time. The warp stages its outputs
+    // in its own 8 KB of the idle stage ring and one lane sends them out with TMA stores; an
+    // input tile (the previous layer's pre-activation, dX) comes in by a TMA load on the
+    // warp's own mbarrier. Rows at or past the live row count are written as zeros.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* wbuf = smem + (warp - 2) * kEpiWarpBytes;
+    uint64_t* ibar = &epi_in[warp - 2];
+    uint8_t* in_f32 = wbuf;
+    uint8_t* out_f32 = wbuf + (Epi::kIn ? 4096 : 0);
+    uint8_t* out_hi = wbuf + 4096;
+    uint8_t* out_lo = wbuf + 6144;
+    const bool ok = mbar_wait_bounded(acc_full, 0);
+    if (!ok && lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
+    fence_after_sync();
+    const bool have = ok && nk > 0;
+    const int row0 = m0 + q * 32;
+    const bool live = row0 + lane < M;
+    const bool load_in = Epi::kIn && epi.uses_in();
+    constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
+    int n = 0;
+#pragma unroll 1
+    for (int c = half * kHalf; c < (half + 1) * kHalf && c < BN; c += 32, ++n) {
+      const int col0 = n0 + c;
+      if (col0 >= sh.N) break;
+      if (load_in && lane == 0) {
+        mbar_arrive_expect_tx(ibar, 32 * 32 * 4);
+        tma_load_2d(in_f32, &epi.in_map, col0, row0, ibar);
+      }
+      float v[32];
+      if (have) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+      if (load_in && !mbar_wait_bounded(ibar, n & 1)) {
+        if (lane == 0) atomicExch(&s_fail, kErrTimeoutEpiIn);
+        mbar_wait_bounded(ibar, n & 1);  // let the copy land before the CTA may leave
+        break;
+      }
+      if (n > 0) {
+        if (lane == 0) bulk_wait_read_all();  // the previous chunk's stores have read the tile
+        __syncwarp();
+      }
+      epi.stage(v, in_f32, out_f32, out_hi, out_lo, lane, col0, live, sh.N);
+      fence_proxy_async_smem();  // generic-proxy smem accesses before the async proxy's
+      __syncwarp();
+      if (lane == 0) {
+        if (epi.has_f32) tma_store_2d(&epi.f32_map, out_f32, col0, row0);
+        if (epi.has_hi) tma_store_2d(&epi.hi_map, out_hi, col0, row0);
+        if (epi.has_lo) tma_store_2d(&epi.lo_map, out_lo, col0, row0);
+        bulk_commit();
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   } else {
     // Epilogue warps 2..9: TMEM lane quarter = warp % 4 (the hardware's access rule), column
     // half = (warp - 2) / 4. After the final commit the stage ring is idle, so each warp
@@ -337,81 +429,118 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bflo
 // Staged epilogues (kStaged) see one element at a time with consecutive lanes on
 // consecutive columns; unstaged ones see a thread's 32 consecutive columns of one row.
 
-// Forward: z = acc + bias; writes z (fp32, nullable), h = act(z) as bf16 (split into
-// hi/lo when hb_lo is set) and as fp32 (nullable). apply_col: one column, rows
-// [row0, row0 + nrows), consecutive lanes on consecutive columns (coalesced).
-struct EpiFwd {
-  static constexpr bool kStaged = true;
-  static constexpr bool kDeep = false;
-  const float* bias;
-  float* z;
-  int ldz;
-  __nv_bfloat16* hb;
-  __nv_bfloat16* hb_lo;
-  int ldhb;
-  float* hf;
-  int ldhf;
-  int act;
-  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
-    const float b = bias[col];
+// Swizzled staging of one thread's row of a 32 x 32 sub-tile (thread = row `lane`). The
+// orders are the TMA engine's: 128-byte swizzle for fp32 rows (16-byte chunk j of row r at
+// chunk j ^ (r % 8)), 64-byte swizzle for bf16 rows (chunk j at j ^ ((r / 2) % 4)); both keep
+// the warp's 16-byte shared stores free of bank conflicts.
+__device__ __forceinline__ void stage_row_f32(uint8_t* tile, int lane, const float (&v)[32]) {
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      if (r >= nrows) break;
-      const size_t row = (size_t)(row0 + r);
-      const float zz = v[r] + b;
-      if (z) z[row * ldz + col] = zz;
-      const float h = act_forward(zz, act);
-      if (hb) {
-        if (hb_lo) {
-          split_bf16(h, hb[row * ldhb + col], hb_lo[row * ldhb + col]);
-        } else {
-          hb[row * ldhb + col] = __float2bfloat16_rn(h);
-        }
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+__device__ __forceinline__ float4 load_row_f32(const uint8_t* tile, int lane, int j) {
+  return *reinterpret_cast<const float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+// bf16 of v (hi) and, when `lo` is set, of the remainders v - hi.
+__device__ __forceinline__ void stage_row_bf16(uint8_t* hi, uint8_t* lo, int lane,
+                                               const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = v[8 * j + 2 * i], b = v[8 * j + 2 * i + 1];
+      h[i] = pack_bf16(a, b);
+      if (lo) {
+        const __nv_bfloat162 hp = *reinterpret_cast<__nv_bfloat162*>(&h[i]);
+        l[i] = pack_bf16(a - __low2float(hp), b - __high2float(hp));
       }
-      if (hf) hf[row * ldhf + col] = h;
+    }
+    const int off = lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    if (lo) *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Forward: z = acc + bias; stores z (fp32, when has_f32) and h = act(z) as bf16 (split into
+// hi/lo halves when has_lo) through TMA. Maps: f32_map over z (fp32, box 32 x 32, 128-byte
+// swizzle), hi_map / lo_map over the bf16 outputs (box 32 x 32, 64-byte swizzle).
+struct EpiFwd {
+  static constexpr bool kStaged = false;
+  static constexpr bool kDeep = false;
+  static constexpr bool kTma = true;
+  static constexpr bool kIn = false;
+  CUtensorMap in_map;  // unused
+  CUtensorMap f32_map, hi_map, lo_map;
+  const float* bias;
+  int act;
+  bool has_f32, has_hi, has_lo;
+  __device__ __forceinline__ bool uses_in() const { return false; }
+  __device__ __forceinline__ void stage(float (&v)[32], const uint8_t*, uint8_t* of, uint8_t* oh,
+                                        uint8_t* ol, int lane, int col0, bool live, int N) const {
+    if (col0 + 32 <= N) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bias + col0) + j);
+        v[4 * j] += b.x;
+        v[4 * j + 1] += b.y;
+        v[4 * j + 2] += b.z;
+        v[4 * j + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += col0 + j < N ? __ldg(bias + col0 + j) : 0.f;
+    }
+    if (!live) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    }
+    if (has_f32) stage_row_f32(of, lane, v);
+    if (has_hi) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = act_forward(v[j], act);
+      stage_row_bf16(oh, has_lo ? ol : nullptr, lane, v);
     }
   }
 };
 
-// dX of a layer: g = acc * act'(pre) of the previous layer (from its pre-activation alone);
-// writes g as fp32 (LayerNorm previous layer) or bf16 (hi/lo when gb_lo is set). All 32
-// pre-activations of the column are loaded before any store, so each lane keeps 32 loads
-// in flight.
+// dX of a layer: g = acc * act'(pre) of the previous layer, from its pre-activation alone
+// (loaded as a TMA tile through in_map: fp32, box 32 x 32, 128-byte swizzle); stores g as
+// fp32 (LayerNorm previous layer, has_f32) or bf16 (hi/lo halves when has_lo).
 struct EpiDx {
-  static constexpr bool kStaged = true;
+  static constexpr bool kStaged = false;
   static constexpr bool kDeep = false;
-  const float* pre;
-  int ldpre;
-  float* gf;
-  __nv_bfloat16* gb;
-  __nv_bfloat16* gb_lo;
-  int ldg;
+  static constexpr bool kTma = true;
+  static constexpr bool kIn = true;
+  CUtensorMap in_map;
+  CUtensorMap f32_map, hi_map, lo_map;
   int act;
-  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
-    float zr[32];
+  bool has_f32, has_hi, has_lo;
+  __device__ __forceinline__ bool uses_in() const { return act != BT_ACT_NONE; }
+  __device__ __forceinline__ void stage(float (&v)[32], const uint8_t* in, uint8_t* of,
+                                        uint8_t* oh, uint8_t* ol, int lane, int, bool live,
+                                        int) const {
     if (act != BT_ACT_NONE) {
 #pragma unroll
-      for (int r = 0; r < 32; ++r)
-        zr[r] = r < nrows ? __ldg(pre + (size_t)(row0 + r) * ldpre + col) : 0.f;
-    }
+      for (int j = 0; j < 8; ++j) {
+        const float4 p = load_row_f32(in, lane, j);
+        const float z[4] = {p.x, p.y, p.z, p.w};
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      if (r >= nrows) break;
-      const size_t row = (size_t)(row0 + r);
-      float g = v[r];
-      if (act != BT_ACT_NONE) {
-        const float z = zr[r];
-        g *= act_grad(z, act == BT_ACT_TANH ? tanhf(z) : 0.f, act);
-      }
-      if (gf) gf[row * ldg + col] = g;
-      if (gb) {
-        if (gb_lo) {
-          split_bf16(g, gb[row * ldg + col], gb_lo[row * ldg + col]);
-        } else {
-          gb[row * ldg + col] = __float2bfloat16_rn(g);
-        }
+        for (int i = 0; i < 4; ++i)
+          v[4 * j + i] *= act_grad(z[i], act == BT_ACT_TANH ? tanhf(z[i]) : 0.f, act);
       }
     }
+    if (!live) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    }
+    if (has_f32) stage_row_f32(of, lane, v);
+    if (has_hi) stage_row_bf16(oh, has_lo ? ol : nullptr, lane, v);
   }
 };
 
@@ -421,6 +550,7 @@ struct EpiDx {
 struct EpiDwT {
   static constexpr bool kStaged = false;
   static constexpr bool kDeep = true;
+  static constexpr bool kTma = false;
   float* out;
   int ld;  // N_out
   size_t split_stride;
@@ -440,6 +570,7 @@ struct EpiDwT {
 struct EpiStore {
   static constexpr bool kStaged = true;
   static constexpr bool kDeep = false;
+  static constexpr bool kTma = false;
   float* out;
   int ld;
   __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
@@ -453,6 +584,11 @@ struct EpiStore {
 // `row_bytes`), `outer` rows; box {box_inner, box_outer}.
 int encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+
+// Epilogue tile map: 32 x 32 box over a row-major [outer, inner] fp32 (128-byte swizzle) or
+// bf16 (64-byte swizzle) tensor with row stride `row_bytes`.
+int encode_tile_map(CUtensorMap* map, const void* base, bool f32, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, int swizzle_bytes);
 
 template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
 int launch_gemm(const Operands& ops, const GemmShape& sh, const Epi& epi, int splits,

@@ -398,6 +398,22 @@ int allocate_tensor_core(bt_learner* L) {
         BT_TRY(umma::encode_map(wa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 64));
         BT_TRY(umma::encode_map(wb, xin, lp.kin + 1, R, (uint64_t)lp.ldx * 2, 64, 64));
       }
+      const uint64_t rows = (uint64_t)R, f32_ld = (uint64_t)lp.kout * 4;
+      BT_TRY(umma::encode_tile_map(&lp.map_z, lp.z, true, lp.kout, rows, f32_ld, 128));
+      BT_TRY(umma::encode_tile_map(&lp.map_pre, lp.pre(), true, lp.kout, rows, f32_ld, 128));
+      BT_TRY(umma::encode_tile_map(&lp.map_dpre, lp.d_pre, true, lp.kout, rows, f32_ld, 128));
+      BT_TRY(umma::encode_tile_map(&lp.map_hb, lp.hb, false, lp.kout, rows,
+                                   (uint64_t)lp.ldh * 2, 64));
+      BT_TRY(umma::encode_tile_map(&lp.map_dzb, lp.dzb, false, lp.kout, rows,
+                                   (uint64_t)lp.kout * 2, 64));
+      lp.map_hb_lo = lp.map_hb;
+      lp.map_dzb_lo = lp.map_dzb;
+      if (L->x3) {
+        BT_TRY(umma::encode_tile_map(&lp.map_hb_lo, lp.hb_lo, false, lp.kout, rows,
+                                     (uint64_t)lp.ldh * 2, 64));
+        BT_TRY(umma::encode_tile_map(&lp.map_dzb_lo, lp.dzb_lo, false, lp.kout, rows,
+                                     (uint64_t)lp.kout * 2, 64));
+      }
       if (!L->x3) {
         lp.fwd_ops.a_lo = lp.fwd_ops.a;
         lp.fwd_ops.b_lo = lp.fwd_ops.b;
@@ -437,11 +453,18 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
     if (lp.tc) {
       umma::GemmShape sh{rows, lp.kout, lp.kin, ceil_div(lp.kin, umma::BK), count, nullptr,
                          L->err_d};
-      // the last layer's output is consumed through its pre-activation (the heads apply
-      // the activation), so no fp32 copy of it is written
-      umma::EpiFwd ep{w + (size_t)lp.kin * lp.kout, lp.z, lp.kout, lp.ln ? nullptr : lp.hb,
-                      lp.ln ? nullptr : lp.hb_lo, lp.ldh, nullptr, lp.kout,
-                      lp.ln ? BT_ACT_NONE : lp.act};
+      // The last layer's output is consumed through its pre-activation (the heads apply
+      // the activation), so only z is stored for it; the bf16 outputs feed the next layer.
+      const bool last = i + 1 == tp.layers.size();
+      umma::EpiFwd ep;
+      ep.f32_map = lp.map_z;
+      ep.hi_map = lp.map_hb;
+      ep.lo_map = lp.map_hb_lo;
+      ep.bias = w + (size_t)lp.kin * lp.kout;
+      ep.act = lp.act;
+      ep.has_f32 = true;
+      ep.has_hi = !lp.ln && !last;
+      ep.has_lo = ep.has_hi && L->x3;
       if (L->x3) {
         BT_K(L, kProfGemmFwd, s, umma::launch_gemm<64, false, true, true>(lp.fwd_ops, sh, ep, 1, s));
       } else if (lp.fwd_bn == 256) {
@@ -451,7 +474,8 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       }
       if (lp.ln) {
         BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act,
-                                                 lp.y, nullptr, lp.hb, lp.hb_lo, lp.ldh, lp.mean,
+                                                 lp.y, nullptr, last ? nullptr : lp.hb,
+                                                 last ? nullptr : lp.hb_lo, lp.ldh, lp.mean,
                                                  lp.rstd, count, s));
       }
     } else if (lp.kind == BT_LAYER_CONV3X3) {
@@ -515,9 +539,15 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
         LayerPlan& prev = tp.layers[i - 1];
         umma::GemmShape shx{rows, lp.kin, lp.kout, ceil_div(lp.kout, umma::BK), count, nullptr,
                             L->err_d};
-        umma::EpiDx epx{prev.pre(), prev.kout, prev.ln ? prev.d_pre : nullptr,
-                        prev.ln ? nullptr : prev.dzb, prev.ln ? nullptr : prev.dzb_lo, prev.kout,
-                        prev.act};
+        umma::EpiDx epx;
+        epx.in_map = prev.map_pre;
+        epx.f32_map = prev.map_dpre;
+        epx.hi_map = prev.map_dzb;
+        epx.lo_map = prev.map_dzb_lo;
+        epx.act = prev.act;
+        epx.has_f32 = prev.ln;
+        epx.has_hi = !prev.ln;
+        epx.has_lo = !prev.ln && L->x3;
         if (L->x3) {
           BT_K(L, kProfGemmDx, s, umma::launch_gemm<64, false, false, true>(lp.dx_ops, shx, epx, 1, s));
         } else {

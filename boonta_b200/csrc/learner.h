@@ -46,6 +46,9 @@ struct LayerPlan {
   __nv_bfloat16* dzb_lo = nullptr;
   __nv_bfloat16* xin_lo = nullptr;
   bt::umma::Operands fwd_ops, dx_ops, dw_ops;
+  // epilogue tile maps (32 x 32 boxes): z and pre() (fp32), hb / hb_lo and dzb / dzb_lo (bf16),
+  // d_pre (fp32, LayerNorm layers)
+  CUtensorMap map_z, map_pre, map_hb, map_hb_lo, map_dzb, map_dzb_lo, map_dpre;
   int fwd_bn = 128;
   int dw_kbps = 1;
   // GRU (recurrent torso); rows are env-major (row = env * T + t)
