@@ -73,7 +73,9 @@ def class_work(w) -> dict:
                 width = n
                 a_bytes = rows * dim * (e if tc else 4)
             w_bytes = k * n * (e if tc else 4)
-            out_fwd = rows * width * (4 + (e if tc else 4) + (4 if (last and tc) else 0))
+            # z (fp32) and the layer output: bf16 (pair) for the next tensor-core layer, none
+            # after a tensor-core tower's last layer (the heads read z), fp32 otherwise
+            out_fwd = rows * width * (4 + ((0 if last else e) if tc else 4))
             out["gemm_fwd"][0] += 2.0 * m * k * n
             out["gemm_fwd"][1] += a_bytes + w_bytes + out_fwd
             dz_bytes = rows * width * (e if tc else 4)

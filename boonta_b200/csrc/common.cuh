@@ -70,17 +70,56 @@ __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a 
 
 // Activation and its derivative. The derivative is evaluated from the pre-activation
 // `z` and the output `h` (tanh uses h, relu and silu use z). The sigmoid inside silu uses
-// the hardware exp2-based __expf and a fast reciprocal (relative error ~1e-6, far inside
-// the learner's 1e-4 gradient tolerance); for z < -88 it correctly tends to 0.
+// the hardware exp2-based __expf and the approximate division __fdividef (relative error
+// ~2e-7, far inside the learner's 1e-4 gradient tolerance); for z < -88 it tends to 0.
 __device__ __forceinline__ float fast_sigmoid(float z) {
-  return __frcp_rn(1.f + __expf(-z));
+  return __fdividef(1.f, 1.f + __expf(-z));
+}
+
+// Compile-time activation A (BT_ACT_*): act_fwd<A>(z) and its derivative act_dz<A>(z) from
+// the pre-activation alone.
+template <int A>
+__device__ __forceinline__ float act_fwd(float z) {
+  if constexpr (A == BT_ACT_TANH) return tanhf(z);
+  if constexpr (A == BT_ACT_RELU) return z > 0.f ? z : 0.f;
+  if constexpr (A == BT_ACT_SILU) return z * fast_sigmoid(z);
+  return z;
+}
+template <int A>
+__device__ __forceinline__ float act_dz(float z) {
+  if constexpr (A == BT_ACT_TANH) {
+    const float t = tanhf(z);
+    return 1.f - t * t;
+  }
+  if constexpr (A == BT_ACT_RELU) return z > 0.f ? 1.f : 0.f;
+  if constexpr (A == BT_ACT_SILU) {
+    const float s = fast_sigmoid(z);
+    return s * (1.f + z * (1.f - s));
+  }
+  return 1.f;
+}
+
+template <int A>
+struct ActTag {
+  static constexpr int value = A;
+};
+// Calls f(ActTag<A>{}) with the runtime activation resolved once, so that element loops
+// inside f are branch-free and the SFU latencies of their elements overlap.
+template <class F>
+__device__ __forceinline__ void with_act(int act, F&& f) {
+  switch (act) {
+    case BT_ACT_TANH: f(ActTag<BT_ACT_TANH>{}); break;
+    case BT_ACT_RELU: f(ActTag<BT_ACT_RELU>{}); break;
+    case BT_ACT_SILU: f(ActTag<BT_ACT_SILU>{}); break;
+    default: f(ActTag<BT_ACT_NONE>{}); break;
+  }
 }
 
 __device__ __forceinline__ float act_forward(float z, int act) {
   switch (act) {
-    case BT_ACT_TANH: return tanhf(z);
-    case BT_ACT_RELU: return z > 0.f ? z : 0.f;
-    case BT_ACT_SILU: return z * fast_sigmoid(z);
+    case BT_ACT_TANH: return act_fwd<BT_ACT_TANH>(z);
+    case BT_ACT_RELU: return act_fwd<BT_ACT_RELU>(z);
+    case BT_ACT_SILU: return act_fwd<BT_ACT_SILU>(z);
     default: return z;
   }
 }
@@ -88,11 +127,8 @@ __device__ __forceinline__ float act_forward(float z, int act) {
 __device__ __forceinline__ float act_grad(float z, float h, int act) {
   switch (act) {
     case BT_ACT_TANH: return 1.f - h * h;
-    case BT_ACT_RELU: return z > 0.f ? 1.f : 0.f;
-    case BT_ACT_SILU: {
-      const float s = fast_sigmoid(z);
-      return s * (1.f + z * (1.f - s));
-    }
+    case BT_ACT_RELU: return act_dz<BT_ACT_RELU>(z);
+    case BT_ACT_SILU: return act_dz<BT_ACT_SILU>(z);
     default: return 1.f;
   }
 }

@@ -502,8 +502,10 @@ struct EpiFwd {
     }
     if (has_f32) stage_row_f32(of, lane, v);
     if (has_hi) {
+      with_act(act, [&](auto tag) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = act_forward(v[j], act);
+        for (int j = 0; j < 32; ++j) v[j] = act_fwd<decltype(tag)::value>(v[j]);
+      });
       stage_row_bf16(oh, has_lo ? ol : nullptr, lane, v);
     }
   }
@@ -525,16 +527,19 @@ struct EpiDx {
   __device__ __forceinline__ void stage(float (&v)[32], const uint8_t* in, uint8_t* of,
                                         uint8_t* oh, uint8_t* ol, int lane, int, bool live,
                                         int) const {
-    if (act != BT_ACT_NONE) {
+    with_act(act, [&](auto tag) {
+      constexpr int A = decltype(tag)::value;
+      if constexpr (A != BT_ACT_NONE) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 p = load_row_f32(in, lane, j);
-        const float z[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          v[4 * j + i] *= act_grad(z[i], act == BT_ACT_TANH ? tanhf(z[i]) : 0.f, act);
+        for (int j = 0; j < 8; ++j) {
+          const float4 p = load_row_f32(in, lane, j);
+          v[4 * j] *= act_dz<A>(p.x);
+          v[4 * j + 1] *= act_dz<A>(p.y);
+          v[4 * j + 2] *= act_dz<A>(p.z);
+          v[4 * j + 3] *= act_dz<A>(p.w);
+        }
       }
-    }
+    });
     if (!live) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = 0.f;

@@ -33,9 +33,18 @@ size_t heads_smem_bytes(int F_pi, int F_v, int A, bool /*shared*/) {
   return floats * 4 + (size_t)kHeadWarps * kNumStatSums * 8 + 64;
 }
 
-__device__ __forceinline__ float4 act4(float4 z, int act) {
-  return make_float4(act_forward(z.x, act), act_forward(z.y, act), act_forward(z.z, act),
-                     act_forward(z.w, act));
+template <int A>
+__device__ __forceinline__ float4 act4(float4 z) {
+  return make_float4(act_fwd<A>(z.x), act_fwd<A>(z.y), act_fwd<A>(z.z), act_fwd<A>(z.w));
+}
+
+// f = act(pre) for all of a lane's chunks, the activation resolved once.
+__device__ __forceinline__ void act_row(const float4 (&z)[kMaxChunks], int act,
+                                        float4 (&f)[kMaxChunks]) {
+  with_act(act, [&](auto tag) {
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) f[i] = act4<decltype(tag)::value>(z[i]);
+  });
 }
 
 __device__ __forceinline__ void load_row(const float* src, int F, int lane, float4 (&v)[kMaxChunks]) {
@@ -67,12 +76,13 @@ __device__ __forceinline__ float dot_row(const float4 (&f)[kMaxChunks], const fl
 // fp32 or bf16 (hi/lo) at row `row`.
 __device__ __forceinline__ void store_df(float4 g, const float4& pre, int act, size_t base, int q,
                                          float* df, __nv_bfloat16* dfb, __nv_bfloat16* dfb_lo) {
-  if (act != BT_ACT_NONE) {
-    g.x *= act_grad(pre.x, act == BT_ACT_TANH ? tanhf(pre.x) : 0.f, act);
-    g.y *= act_grad(pre.y, act == BT_ACT_TANH ? tanhf(pre.y) : 0.f, act);
-    g.z *= act_grad(pre.z, act == BT_ACT_TANH ? tanhf(pre.z) : 0.f, act);
-    g.w *= act_grad(pre.w, act == BT_ACT_TANH ? tanhf(pre.w) : 0.f, act);
-  }
+  with_act(act, [&](auto tag) {
+    constexpr int A = decltype(tag)::value;
+    g.x *= act_dz<A>(pre.x);
+    g.y *= act_dz<A>(pre.y);
+    g.z *= act_dz<A>(pre.z);
+    g.w *= act_dz<A>(pre.w);
+  });
   const size_t i = base + 4 * (size_t)q;
   if (dfb) {
     store_bf16(dfb, dfb_lo, i, g.x);
@@ -138,11 +148,8 @@ __global__ void __launch_bounds__(kHeadThreads) heads_loss_kernel(HeadsParams p)
     float4 f[kMaxChunks], fv[kMaxChunks], zp[kMaxChunks], zv[kMaxChunks];
     load_row(p.f_pi + (size_t)row * F, F, lane, zp);
     if (!shared) load_row(p.f_v + (size_t)row * Fv, Fv, lane, zv);
-#pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
-      f[i] = act4(zp[i], p.act_pi);
-      if (!shared) fv[i] = act4(zv[i], p.act_v);
-    }
+    act_row(zp, p.act_pi, f);
+    if (!shared) act_row(zv, p.act_v, fv);
     const float lp_old = p.lp_old[flat];
     const float adv = p.adv[flat];
     const float ret = p.ret[flat];

@@ -34,13 +34,15 @@ __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int
   const float mean = s / n;
   const float var = fmaxf(s2 / n - mean * mean, 0.f);
   const float r = rsqrtf(var + kLnEps);
-  for (int k = lane; k < n; k += 32) {
-    const float yv = (zr[k] - mean) * (r * sb[k]) + sb[n + k];
-    y[(size_t)row * n + k] = yv;
-    const float hv = act_forward(yv, act);
-    if (h) h[(size_t)row * n + k] = hv;
-    if (hb) store_bf16(hb, hb_lo, (size_t)row * ldhb + k, hv);
-  }
+  with_act(act, [&](auto tag) {
+    for (int k = lane; k < n; k += 32) {
+      const float yv = (zr[k] - mean) * (r * sb[k]) + sb[n + k];
+      y[(size_t)row * n + k] = yv;
+      const float hv = act_fwd<decltype(tag)::value>(yv);
+      if (h) h[(size_t)row * n + k] = hv;
+      if (hb) store_bf16(hb, hb_lo, (size_t)row * ldhb + k, hv);
+    }
+  });
   if (lane == 0) {
     mean_out[row] = mean;
     rstd_out[row] = r;
@@ -498,8 +500,8 @@ int launch_local_indices(const int* perm, int num_slices, int slice_len, int /*u
 // one thread per input feature k (k == F is the constant-one row whose sum is the bias
 // gradient), the rows of a split staged 64 at a time in shared memory; each thread keeps
 // its n accumulators in registers and sums rows in order.
-template <int NMAX>
-__global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, int act,
+template <int NMAX, int ACT>
+__global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F,
                                                         const float* d, int n, int rows,
                                                         const int* count, int rows_per_split,
                                                         float* out) {
@@ -530,7 +532,7 @@ __global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, i
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        if (k < F) fk[u] = act_forward(fk[u], act);
+        if (k < F) fk[u] = act_fwd<ACT>(fk[u]);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u)
@@ -544,21 +546,40 @@ __global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F, i
   }
 }
 
+template <int NMAX>
+void launch_skinny_n(dim3 grid, const float* f, int F, int act, const float* d, int n, int rows,
+                     const int* count, int rps, float* out, cudaStream_t stream) {
+  switch (act) {
+    case BT_ACT_TANH:
+      skinny_dw_kernel<NMAX, BT_ACT_TANH><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+      break;
+    case BT_ACT_RELU:
+      skinny_dw_kernel<NMAX, BT_ACT_RELU><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+      break;
+    case BT_ACT_SILU:
+      skinny_dw_kernel<NMAX, BT_ACT_SILU><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+      break;
+    default:
+      skinny_dw_kernel<NMAX, BT_ACT_NONE><<<grid, 128, 0, stream>>>(f, F, d, n, rows, count, rps, out);
+      break;
+  }
+}
+
 int launch_skinny_dw(const float* f, int F, int act, const float* d, int n, int rows,
                      const int* count, int splits, float* out, cudaStream_t stream) {
   const int rps = ceil_div(rows, splits);
   dim3 grid(ceil_div(F + 1, 128), splits);
   if (n <= 1) {
-    skinny_dw_kernel<1><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
+    launch_skinny_n<1>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   } else if (n <= 8) {
-    skinny_dw_kernel<8><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
+    launch_skinny_n<8>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   } else if (n <= 16) {
-    skinny_dw_kernel<16><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
+    launch_skinny_n<16>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   } else if (n <= 32) {
-    skinny_dw_kernel<32><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
+    launch_skinny_n<32>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   } else {
     BT_CHECK_ARG(n <= 64, "skinny dW with %d outputs", n);
-    skinny_dw_kernel<64><<<grid, 128, 0, stream>>>(f, F, act, d, n, rows, count, rps, out);
+    launch_skinny_n<64>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   }
   BT_LAUNCH_CHECK("skinny_dw_kernel");
   return BT_OK;

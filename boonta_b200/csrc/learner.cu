@@ -590,12 +590,13 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   const bt_learner_config& c = L->cfg;
   BT_TRY(gather_obs(L, in.obs, in.idx, rows, in.count, s));
   // separate actor and critic towers run side by side (the critic on a side stream)
+  const cudaStream_t sc = side_stream(L, 0, s);
   if (L->ntowers > 1) {
-    BT_TRY(stream_dep(L, s, L->side[0]));
-    BT_TRY(forward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, L->side[0]));
+    BT_TRY(stream_dep(L, s, sc));
+    BT_TRY(forward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, sc));
   }
   BT_TRY(forward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s));
-  if (L->ntowers > 1) BT_TRY(stream_dep(L, L->side[0], s));
+  if (L->ntowers > 1) BT_TRY(stream_dep(L, sc, s));
   TowerPlan& t0 = L->towers[0];
   TowerPlan& tv = L->towers[L->ntowers - 1];
   LayerPlan& last_pi = t0.layers.back();
@@ -639,7 +640,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
   // head weight gradients: [F + 1, A] = [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value,
   // on a side stream next to the towers' backward
-  cudaStream_t sh = L->side[3];
+  cudaStream_t sh = side_stream(L, 3, s);
   BT_TRY(stream_dep(L, s, sh));
   BT_K(L, kProfGemmDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out, L->A,
                                             rows, in.count, L->head_pi_splits, L->head_pi_part,
@@ -655,12 +656,13 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
           BT_K(L, kProfMisc, s, launch_zero_tail_rows(lp.dzb, lp.dzb_lo, rows, lp.kout, in.count, s));
   }
   if (L->ntowers > 1) {
-    BT_TRY(stream_dep(L, s, L->side[0]));
-    BT_TRY(backward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, L->side[0], -1,
-                          L->side[2]));
+    BT_TRY(stream_dep(L, s, sc));
+    BT_TRY(backward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, sc, -1,
+                          side_stream(L, 2, s)));
   }
-  BT_TRY(backward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s, -1, L->side[1]));
-  if (L->ntowers > 1) BT_TRY(stream_dep(L, L->side[0], s));
+  BT_TRY(backward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s, -1,
+                        side_stream(L, 1, s)));
+  if (L->ntowers > 1) BT_TRY(stream_dep(L, sc, s));
   BT_TRY(stream_dep(L, sh, s));
   BT_K(L, kProfReduce, s, launch_reduce_segments(L->segs_d, L->chunks_d, L->num_chunks, L->grads,
                                 with_norm ? L->norm_part : nullptr, s));

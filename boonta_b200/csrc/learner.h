@@ -183,6 +183,12 @@ struct bt_learner {
 
 cudaEvent_t prof_event(bt_learner* L);
 
+// Side stream i for work that may overlap the caller's stream s. While profiling, every
+// launch stays on s, so that each recorded event pair times one kernel alone on the GPU.
+inline cudaStream_t side_stream(bt_learner* L, int i, cudaStream_t s) {
+  return L->prof.on ? s : L->side[i];
+}
+
 template <class T>
 int dalloc(bt_learner* L, T** p, size_t count) {
   if (count == 0) count = 1;

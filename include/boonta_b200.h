@@ -223,7 +223,9 @@ BT_API int bt_gemm_bf16x3(const void* A_hi, const void* A_lo, const void* B_hi, 
  * here every kernel the learner enqueues can be bracketed with CUDA events on its stream.
  * bt_learner_profile(1) clears and starts recording, (0) stops. profile_read returns, for
  * kernel class `cls` (0 .. until it returns BT_ERR_INVALID), its name, the summed device
- * time in ms and the number of launches recorded (it synchronises on the events).
+ * time in ms and the number of launches recorded (it synchronises on the events). While
+ * recording, the work that otherwise overlaps on side streams runs on the caller's stream,
+ * so each recorded time is one kernel alone on the GPU.
  * bt_learner_launch_count: kernels and collectives enqueued since creation. */
 BT_API int bt_learner_profile(bt_learner* learner, int32_t enable);
 BT_API int bt_learner_profile_read(bt_learner* learner, int32_t cls, char* name,
