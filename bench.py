@@ -309,6 +309,8 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-profile", action="store_true",
+                    help="skip the per-kernel-class profiled pass (for ncu launch lists)")
     args = ap.parse_args()
 
     kw = {"precision": args.precision} if args.precision else {}
@@ -373,13 +375,15 @@ def main():
     # Per-kernel-class device time: the same K steps again, with CUDA events recorded around
     # every launch on the stream it is launched on (a second timed region, so the events'
     # host cost cannot touch the headline number).
-    lrn.profile(True)
-    for i in range(args.steps):
-        lrn.update(roll, perms[args.warmup + i], stats=True)
-    torch.cuda.synchronize()
-    prof = {k: (ms_ / max(args.steps, 1), n_ // max(args.steps, 1))
-            for k, (ms_, n_) in lrn.profile_read().items()}
-    lrn.profile(False)
+    prof = {}
+    if not args.no_profile:
+        lrn.profile(True)
+        for i in range(args.steps):
+            lrn.update(roll, perms[args.warmup + i], stats=True)
+        torch.cuda.synchronize()
+        prof = {k: (ms_ / max(args.steps, 1), n_ // max(args.steps, 1))
+                for k, (ms_, n_) in lrn.profile_read().items()}
+        lrn.profile(False)
 
     # end to end: rollout from pinned host memory, statistics back to the host, every step
     e2e = None

@@ -160,20 +160,25 @@ __device__ __forceinline__ double block_sum_d(double v, double* sh) {
 
 int count_reduce_chunks(const Segment* segs, int num_segments) {
   int n = 0;
-  for (int i = 0; i < num_segments; ++i) n += ceil_div(segs[i].len, kReduceChunk);
+  for (int i = 0; i < num_segments; ++i)
+    n += ceil_div(segs[i].len, reduce_chunk_len(segs[i].len, segs[i].nsplit));
   return n;
 }
 
 void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out, int* count) {
   int n = 0;
-  for (int i = 0; i < num_segments; ++i)
-    for (int b = 0; b < segs[i].len; b += kReduceChunk)
-      out[n++] = {i, b, b + kReduceChunk < segs[i].len ? b + kReduceChunk : segs[i].len};
+  for (int i = 0; i < num_segments; ++i) {
+    const int c = reduce_chunk_len(segs[i].len, segs[i].nsplit);
+    for (int b = 0; b < segs[i].len; b += c)
+      out[n++] = {i, b, b + c < segs[i].len ? b + c : segs[i].len};
+  }
   *count = n;
 }
 
-// Wide chunks: each thread sums the splits of 8 elements spaced by the block size, eight
-// splits at a time (64 independent loads in flight per thread), in split order.
+// Wide chunks: each thread sums the splits of 4 elements spaced by the block size, eight
+// splits at a time (32 independent loads in flight per thread), in split order.
+// Tall chunks (many splits, kTallChunk elements): warp w sums splits w, w + 8, ... of the
+// lane's element, then the eight warp sums are added in warp order.
 // Narrow segments (fewer elements than a warp has lanes per split pass, e.g. the per-block
 // partial sums of the gaussian scale): one warp per element, lanes striding over the
 // splits, combined by a fixed shuffle tree. Both orders are fixed, so the result is
@@ -196,6 +201,31 @@ __global__ void __launch_bounds__(256, 4) reduce_segments_kernel(const Segment* 
         grads[sg.dst + i] = a;
         sq += (double)a * (double)a;
       }
+    }
+  } else if (sg.nsplit >= kTallSplits) {
+    __shared__ float tall[8][kTallChunk];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int i = ch.begin + lane;
+    float a = 0.f;
+    if (i < ch.end) {
+      int k = warp;
+      for (; k + 56 < sg.nsplit; k += 64) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldg(sg.src + (size_t)(k + 8 * u) * sg.stride + i);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a += v[u];
+      }
+      for (; k < sg.nsplit; k += 8) a += __ldg(sg.src + (size_t)k * sg.stride + i);
+    }
+    tall[warp][lane] = a;
+    __syncthreads();
+    if (warp == 0 && i < ch.end) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) s += tall[w][lane];
+      grads[sg.dst + i] = s;
+      sq = (double)s * (double)s;
     }
   } else {
     constexpr int kPer = kReduceChunk / 256;

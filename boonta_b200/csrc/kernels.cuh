@@ -102,6 +102,14 @@ struct ReduceChunk {
   int begin, end;
 };
 constexpr int kReduceChunk = 1024;
+// Segments with at least kTallSplits partials are reduced in chunks of kTallChunk elements,
+// the block's eight warps each summing every eighth partial (so the dependent load chain
+// per thread is nsplit / 8 long instead of nsplit).
+constexpr int kTallSplits = 64;
+constexpr int kTallChunk = 32;
+__host__ __device__ inline int reduce_chunk_len(int len, int nsplit) {
+  return (len >= 256 && nsplit >= kTallSplits) ? kTallChunk : kReduceChunk;
+}
 // Builds the chunk table of a segment list (host side).
 void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out, int* count);
 int count_reduce_chunks(const Segment* segs, int num_segments);

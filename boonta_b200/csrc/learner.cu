@@ -288,11 +288,11 @@ int allocate(bt_learner* L) {
   const int A = L->A;
   BT_TRY(dalloc(L, &L->d_out, (size_t)R * A));
   BT_TRY(dalloc(L, &L->d_val, R));
-  // skinny head dW: about 8 blocks of 128 threads per SM (enough loads in flight), at
-  // least 32 rows per split
-  L->head_pi_splits = std::max(1, std::min(ceil_div(L->rows_cap, 32),
+  // skinny head dW: up to 8 blocks of 128 threads per SM (enough loads in flight), at
+  // least 128 rows per split (fewer partials for the reduction to read)
+  L->head_pi_splits = std::max(1, std::min(ceil_div(L->rows_cap, 128),
                                            8 * kNumSMs / ceil_div(L->F_pi + 1, 128)));
-  L->head_v_splits = std::max(1, std::min(ceil_div(L->rows_cap, 32),
+  L->head_v_splits = std::max(1, std::min(ceil_div(L->rows_cap, 128),
                                           8 * kNumSMs / ceil_div(L->F_v + 1, 128)));
   BT_TRY(dalloc(L, &L->head_pi_part, (size_t)L->head_pi_splits * (L->F_pi + 1) * A));
   BT_TRY(dalloc(L, &L->head_v_part, (size_t)L->head_v_splits * (L->F_v + 1)));
