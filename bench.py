@@ -57,7 +57,7 @@ def class_work(w) -> dict:
     steps = w.ppo.update_epochs * w.ppo.num_minibatches
     tc = w.precision in ("bf16", "bf16x3")
     e = {"fp32": 4, "bf16": 2, "bf16x3": 4}[w.precision]
-    out = {k: [0.0, 0.0] for k in ("gemm_fwd", "gemm_dx", "gemm_dw", "heads_loss")}
+    out = {k: [0.0, 0.0] for k in ("gemm_fwd", "gemm_dx", "gemm_dw", "heads_loss", "head_dw")}
     feats = []
     for tower in net.towers():
         dim = net.obs_dim
@@ -93,6 +93,9 @@ def class_work(w) -> dict:
     # heads: features + pre-activations read, dz written, head outputs' gradients written
     out["heads_loss"][0] += 2.0 * rows * (f_pi * a + f_v) * 2
     out["heads_loss"][1] += rows * nf * (4 + 4 + (e if tc else 4)) + rows * (a + 1) * 4 + rows * 20
+    # head weight gradients: [f, 1]^T d_out and [f, 1]^T d_value (features re-read)
+    out["head_dw"][0] += 2.0 * rows * ((f_pi + 1) * a + (f_v + 1))
+    out["head_dw"][1] += rows * (f_pi + f_v) * 4 + rows * (a + 1) * 4
     return {k: (v[0] * steps, v[1] * steps) for k, v in out.items()}
 
 
@@ -123,13 +126,23 @@ def roofline(w, prof: dict, pk: dict, pk_kind: str) -> dict:
                         frac=ach / gbs_peak, algorithmic_per_launch=nbytes / n)
     else:
         line.update(bound="hbm", achieved=None, peak=gbs_peak, unit="GB/s", frac=None)
-    line["traffic"] = TRAFFIC.get((w.name, w.precision, cls))
+    cap = TRAFFIC.get((w.name, w.precision, cls))
+    line["traffic"] = None
+    if cap and "algorithmic_per_launch" in line:
+        # the captured launch's DRAM bytes, scaled to the class's average launch by the ratio
+        # of algorithmic bytes (traffic grows in proportion to the rows and widths processed)
+        line["traffic"] = cap[0] * (nbytes / n) / cap[1]
     return line
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch, from ncu captures of the same
-# workload (profiles/ summaries give the commands); None when not captured.
-TRAFFIC = {}
+# {(workload, precision, class): (dram__bytes_read.sum + dram__bytes_write.sum of one captured
+# launch, that launch's algorithmic bytes)}, from the ncu --set full captures summarised in
+# profiles/<class>_<workload>_<precision>.md.
+TRAFFIC = {
+    ("c2_brax", "bf16x3", "gemm_dw"): (34.11e6, 35.9e6),    # a 256-wide layer
+    ("c2_brax", "bf16x3", "gemm_fwd"): (6.05e6, 39.4e6),    # first layer, outputs stay in L2
+    ("c2_brax", "bf16x3", "heads_loss"): (42.2e6, 67.8e6),
+}
 
 
 def gae_bytes(w) -> float:

@@ -642,10 +642,10 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   // on a side stream next to the towers' backward
   cudaStream_t sh = side_stream(L, 3, s);
   BT_TRY(stream_dep(L, s, sh));
-  BT_K(L, kProfGemmDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out, L->A,
+  BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out, L->A,
                                             rows, in.count, L->head_pi_splits, L->head_pi_part,
                                             sh));
-  BT_K(L, kProfGemmDw, sh, launch_skinny_dw(last_v.pre(), L->F_v, last_v.act, L->d_val, 1, rows,
+  BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_v.pre(), L->F_v, last_v.act, L->d_val, 1, rows,
                                             in.count, L->head_v_splits, L->head_v_part, sh));
   if (in.count) {
     // padded minibatch (multi-GPU): the tensor-core dW GEMMs read whole 64-row blocks, so the
@@ -967,7 +967,7 @@ extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, cons
 // ---- profiling ---------------------------------------------------------------------------
 const char* const kProfNames[kProfNumClasses] = {
     "gae", "gemm_fwd", "gemm_dx", "gemm_dw", "heads_loss", "heads_fwd", "ln_fwd",
-    "ln_bwd", "grad_reduce", "clip_adam", "stats", "allreduce", "misc"};
+    "ln_bwd", "grad_reduce", "clip_adam", "stats", "allreduce", "misc", "head_dw"};
 
 cudaEvent_t prof_event(bt_learner* L) {
   Profiler& p = L->prof;

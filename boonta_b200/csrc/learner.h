@@ -83,7 +83,8 @@ struct Comm;  // NCCL communicator (comm.cu)
 // Kernel classes of the per-class device-time profile (bt_learner_profile_read).
 enum ProfClass {
   kProfGae = 0, kProfGemmFwd, kProfGemmDx, kProfGemmDw, kProfHeads, kProfHeadsFwd, kProfLnFwd,
-  kProfLnBwd, kProfReduce, kProfAdam, kProfStats, kProfAllreduce, kProfMisc, kProfNumClasses
+  kProfLnBwd, kProfReduce, kProfAdam, kProfStats, kProfAllreduce, kProfMisc, kProfHeadDw,
+  kProfNumClasses
 };
 extern const char* const kProfNames[kProfNumClasses];
 
