@@ -194,16 +194,14 @@ __global__ void __launch_bounds__(kThreads)
     umma_gemm_kernel(const __grid_constant__ Operands ops, GemmShape sh,
                      const __grid_constant__ Epi epi) {
   using C = Cfg<BN, X3, Epi::kDeep>;
-  static_assert(!Epi::kTma || C::kStages * C::kStageBytes >= kEpiWarps * kEpiWarpBytes,
-                "store epilogue needs 8 KB of the stage ring per epilogue warp");
+  static_assert(!Epi::kTma, "store epilogues run in the persistent kernel");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* acc_full = empty + C::kStages;
-  uint64_t* epi_in = acc_full + 1;  // one per epilogue warp (store epilogues' input tiles)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_in + kEpiWarps);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -224,8 +222,6 @@ __global__ void __launch_bounds__(kThreads)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    if (Epi::kTma)
-      for (int w = 0; w < kEpiWarps; ++w) mbar_init(&epi_in[w], 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, BN);
@@ -312,65 +308,6 @@ __global__ void __launch_bounds__(kThreads)
       }
       mma_commit(acc_full);
     }
-  } else if constexpr (Epi::kTma) {
-    // Store epilogue, warps 2..9: lane quarter q = warp % 4 (rows q*32 .. q*32+31, thread =
-    // row), column half = (warp - 2) / 4, 32 columns at a time. The warp stages its outputs
-    // in its own 8 KB of the idle stage ring and one lane sends them out with TMA stores; an
-    // input tile (the previous layer's pre-activation, dX) comes in by a TMA load on the
-    // warp's own mbarrier. Rows at or past the live row count are written as zeros.
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    uint8_t* wbuf = smem + (warp - 2) * kEpiWarpBytes;
-    uint64_t* ibar = &epi_in[warp - 2];
-    uint8_t* in_f32 = wbuf;
-    uint8_t* out_f32 = wbuf + (Epi::kIn ? 4096 : 0);
-    uint8_t* out_hi = wbuf + 4096;
-    uint8_t* out_lo = wbuf + 6144;
-    const bool ok = mbar_wait_bounded(acc_full, 0);
-    if (!ok && lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
-    fence_after_sync();
-    const bool have = ok && nk > 0;
-    const int row0 = m0 + q * 32;
-    const bool live = row0 + lane < M;
-    const bool load_in = Epi::kIn && epi.uses_in();
-    constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
-    int n = 0;
-#pragma unroll 1
-    for (int c = half * kHalf; c < (half + 1) * kHalf && c < BN; c += 32, ++n) {
-      const int col0 = n0 + c;
-      if (col0 >= sh.N) break;
-      if (load_in && lane == 0) {
-        mbar_arrive_expect_tx(ibar, 32 * 32 * 4);
-        tma_load_2d(in_f32, &epi.in_map, col0, row0, ibar);
-      }
-      float v[32];
-      if (have) {
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-      }
-      if (load_in && !mbar_wait_bounded(ibar, n & 1)) {
-        if (lane == 0) atomicExch(&s_fail, kErrTimeoutEpiIn);
-        mbar_wait_bounded(ibar, n & 1);  // let the copy land before the CTA may leave
-        break;
-      }
-      if (n > 0) {
-        if (lane == 0) bulk_wait_read_all();  // the previous chunk's stores have read the tile
-        __syncwarp();
-      }
-      epi.stage(v, in_f32, out_f32, out_hi, out_lo, lane, col0, live, sh.N);
-      fence_proxy_async_smem();  // generic-proxy smem accesses before the async proxy's
-      __syncwarp();
-      if (lane == 0) {
-        if (epi.has_f32) tma_store_2d(&epi.f32_map, out_f32, col0, row0);
-        if (epi.has_hi) tma_store_2d(&epi.hi_map, out_hi, col0, row0);
-        if (epi.has_lo) tma_store_2d(&epi.lo_map, out_lo, col0, row0);
-        bulk_commit();
-      }
-    }
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
   } else {
     // Epilogue warps 2..9: TMEM lane quarter = warp % 4 (the hardware's access rule), column
     // half = (warp - 2) / 4. After the final commit the stage ring is idle, so each warp
@@ -416,6 +353,251 @@ __global__ void __launch_bounds__(kThreads)
   if (warp == 1) {
     fence_after_sync();
     tmem_dealloc(tmem, BN);
+  }
+  if (threadIdx.x == 0 && s_fail && sh.err) atomicExch(sh.err, s_fail);
+}
+
+// ---- persistent kernel with store epilogues ------------------------------------------------
+// One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (N tile
+// fastest, so the CTAs running at the same time share the A row block through L2). The
+// accumulator is double-buffered in TMEM (2 x BN columns): the MMA warp fills buffer i % 2
+// while the epilogue warps drain the other, so a tile's epilogue overlaps the next tile's
+// main loop. The stage ring runs on across tiles; the epilogue has its own 64 KB of shared
+// memory (8 KB per warp, kEpiWarpBytes). Barriers: full/empty per stage (TMA -> MMA ->
+// TMA), acc_full per buffer (MMA commit -> epilogue), acc_empty per buffer (the eight
+// epilogue warps -> MMA, after their last tcgen05.ld of the buffer), and one input barrier
+// per epilogue warp for the dX pre-activation tile. Every wait is bounded; a role that
+// gives up records the error and leaves its loop, and the others then run out of work or
+// out of time.
+template <int BN, bool X3>
+struct PCfg {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = (kABytes + kBBytes) * (X3 ? 2 : 1);
+  static constexpr int kEpiBytes = kEpiWarps * kEpiWarpBytes;
+  static constexpr int kFit = (224 * 1024 - kEpiBytes - 2048) / kStageBytes;
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kSmem = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 256;
+  static_assert(kStages >= 2, "stage ring too small");
+  static_assert(kTmemCols <= 512, "TMEM has 512 columns");
+};
+
+template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+    umma_persistent_kernel(const __grid_constant__ Operands ops, GemmShape sh,
+                           const __grid_constant__ Epi epi) {
+  using C = PCfg<BN, X3>;
+  static_assert(Epi::kTma, "persistent kernel runs store epilogues");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* epi_smem = smem + C::kStages * C::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* epi_in = acc_empty + 2;         // [kEpiWarps]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_in + kEpiWarps);
+  __shared__ int s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int M = sh.M;
+  if (sh.m_count) M = min(M, *sh.m_count);
+  const int ntn = ceil_div(sh.N, BN);
+  const int tiles = ceil_div(M, BM) * ntn;
+  const int nk = ceil_div(sh.K, BK);
+  if ((int)blockIdx.x >= tiles) return;  // whole CTA leaves before any barrier or TMEM use
+
+  if (threadIdx.x == 0) {
+    s_fail = 0;
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&epi_in[w], 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::kTmemCols);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  auto failed = [&]() { return *(volatile int*)&s_fail != 0; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;  // K blocks issued so far (across tiles)
+      for (int t = blockIdx.x; t < tiles && !failed(); t += gridDim.x) {
+        const int m0 = (t / ntn) * BM, n0 = (t % ntn) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % C::kStages;
+          if (g >= C::kStages && !mbar_wait_bounded(&empty[s], ((g / C::kStages) - 1) & 1)) {
+            atomicExch(&s_fail, kErrTimeoutEmpty);
+            break;
+          }
+          uint8_t* sa = smem + s * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          const int k0 = kb * BK;
+#pragma unroll
+          for (int part = 0; part < (X3 ? 2 : 1); ++part) {
+            uint8_t* pa = part ? sb + C::kBBytes : sa;
+            uint8_t* pb = part ? sb + C::kBBytes + C::kABytes : sb;
+            const CUtensorMap* ma = part ? &ops.a_lo : &ops.a;
+            const CUtensorMap* mb = part ? &ops.b_lo : &ops.b;
+            if (A_MN) {
+              tma_load_2d(pa, ma, m0, k0, &full[s]);
+              tma_load_2d(pa + 8192, ma, m0 + 64, k0, &full[s]);
+            } else {
+              tma_load_2d(pa, ma, k0, m0, &full[s]);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(pb + j * 8192, mb, n0 + 64 * j, k0, &full[s]);
+            } else {
+              tma_load_2d(pb, mb, k0, n0, &full[s]);
+            }
+          }
+        }
+      }
+      // Let every copy this CTA issued land before the CTA may leave.
+      for (int i = max(0, g - C::kStages); i < g; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) atomicExch(&s_fail, kErrTimeoutFull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc<BN, A_MN, B_MN>();
+      int g = 0, i = 0;
+      for (int t = blockIdx.x; t < tiles && !failed(); t += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait_bounded(&acc_empty[b], ((i >> 1) - 1) & 1)) {
+          atomicExch(&s_fail, kErrTimeoutAcc);
+          break;
+        }
+        fence_after_sync();
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int s = g % C::kStages;
+          if (!mbar_wait_bounded(&full[s], (g / C::kStages) & 1)) {
+            atomicExch(&s_fail, kErrTimeoutFull);
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint32_t sa = smem_u32(smem + s * C::kStageBytes);
+          const uint32_t sb = sa + C::kABytes;
+          const uint32_t sa_lo = sb + C::kBBytes;
+          const uint32_t sb_lo = sa_lo + C::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ah = operand_desc<A_MN>(sa, k), bh = operand_desc<B_MN>(sb, k);
+            const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+            if (X3) {
+              mma_bf16(acc, operand_desc<A_MN>(sa_lo, k), bh, idesc, accumulate);
+              mma_bf16(acc, ah, operand_desc<B_MN>(sb_lo, k), idesc, 1u);
+              mma_bf16(acc, ah, bh, idesc, 1u);
+            } else {
+              mma_bf16(acc, ah, bh, idesc, accumulate);
+            }
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[b]);
+      }
+    }
+  } else {
+    // Epilogue warps 2..9: lane quarter q = warp % 4 (rows q*32 .. q*32+31, thread = row),
+    // column half = (warp - 2) / 4, 32 columns at a time; outputs staged swizzled in the
+    // warp's 8 KB and sent out by TMA stores. Rows at or past the live row count are
+    // written as zeros.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* wbuf = epi_smem + (warp - 2) * kEpiWarpBytes;
+    uint64_t* ibar = &epi_in[warp - 2];
+    uint8_t* in_f32 = wbuf;
+    uint8_t* out_f32 = wbuf + (Epi::kIn ? 4096 : 0);
+    uint8_t* out_hi = wbuf + 4096;
+    uint8_t* out_lo = wbuf + 6144;
+    const bool load_in = Epi::kIn && epi.uses_in();
+    constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
+    const int c_begin = half * kHalf, c_end = min(BN, (half + 1) * kHalf);
+    int loads = 0;        // input tiles loaded by this warp (parity of ibar)
+    bool pending = false;  // stores committed from this warp's staging buffers
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles && !failed(); t += gridDim.x, ++i) {
+      const int b = i & 1;
+      const int m0 = (t / ntn) * BM, n0 = (t % ntn) * BN;
+      const bool ok = mbar_wait_bounded(&acc_full[b], (i >> 1) & 1);
+      if (!ok) {
+        if (lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
+        break;
+      }
+      fence_after_sync();
+      const int row0 = m0 + q * 32;
+      const bool live = row0 + lane < M;
+      bool released = false;
+      for (int c = c_begin; c < c_end; c += 32) {
+        const int col0 = n0 + c;
+        const bool last = c + 32 >= c_end || col0 + 32 >= sh.N;
+        if (col0 >= sh.N) break;
+        if (load_in && lane == 0) {
+          mbar_arrive_expect_tx(ibar, 32 * 32 * 4);
+          tma_load_2d(in_f32, &epi.in_map, col0, row0, ibar);
+        }
+        float v[32];
+        tmem_ld32(tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+        if (last) {
+          // the accumulator buffer is free for the MMA warp once every warp has read it
+          fence_before_sync();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
+          released = true;
+        }
+        if (load_in) {
+          const bool got = mbar_wait_bounded(ibar, loads & 1);
+          ++loads;
+          if (!got) {
+            if (lane == 0) atomicExch(&s_fail, kErrTimeoutEpiIn);
+            mbar_wait_bounded(ibar, (loads - 1) & 1);  // let the copy land before leaving
+            break;
+          }
+        }
+        if (pending) {
+          if (lane == 0) bulk_wait_read_all();  // earlier stores have read the staging tiles
+          __syncwarp();
+        }
+        epi.stage(v, in_f32, out_f32, out_hi, out_lo, lane, col0, live, sh.N);
+        fence_proxy_async_smem();  // generic-proxy smem writes before the async proxy reads
+        __syncwarp();
+        if (lane == 0) {
+          if (epi.has_f32) tma_store_2d(&epi.f32_map, out_f32, col0, row0);
+          if (epi.has_hi) tma_store_2d(&epi.hi_map, out_hi, col0, row0);
+          if (epi.has_lo) tma_store_2d(&epi.lo_map, out_lo, col0, row0);
+          bulk_commit();
+        }
+        pending = true;
+      }
+      if (!released) {
+        fence_before_sync();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after_sync();
+    tmem_dealloc(tmem, C::kTmemCols);
   }
   if (threadIdx.x == 0 && s_fail && sh.err) atomicExch(sh.err, s_fail);
 }
@@ -598,17 +780,29 @@ int encode_tile_map(CUtensorMap* map, const void* base, bool f32, uint64_t inner
 template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
 int launch_gemm(const Operands& ops, const GemmShape& sh, const Epi& epi, int splits,
                 cudaStream_t stream) {
-  using C = Cfg<BN, X3, Epi::kDeep>;
   if (sh.M <= 0 || sh.N <= 0) return BT_OK;
   static bool configured = false;  // per template instance (attribute is per function)
-  if (!configured) {
-    BT_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<BN, A_MN, B_MN, X3, Epi>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    configured = true;
+  if constexpr (Epi::kTma) {
+    using C = PCfg<BN, X3>;
+    auto kernel = umma_persistent_kernel<BN, A_MN, B_MN, X3, Epi>;
+    if (!configured) {
+      BT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+      configured = true;
+    }
+    const int tiles = ceil_div(sh.M, BM) * ceil_div(sh.N, BN);
+    kernel<<<min(tiles, kNumSMs), kThreads, C::kSmem, stream>>>(ops, sh, epi);
+    BT_LAUNCH_CHECK("umma_persistent_kernel");
+  } else {
+    using C = Cfg<BN, X3, Epi::kDeep>;
+    auto kernel = umma_gemm_kernel<BN, A_MN, B_MN, X3, Epi>;
+    if (!configured) {
+      BT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+      configured = true;
+    }
+    dim3 grid(ceil_div(sh.M, BM), ceil_div(sh.N, BN), max(1, splits));
+    kernel<<<grid, kThreads, C::kSmem, stream>>>(ops, sh, epi);
+    BT_LAUNCH_CHECK("umma_gemm_kernel");
   }
-  dim3 grid(ceil_div(sh.M, BM), ceil_div(sh.N, BN), max(1, splits));
-  umma_gemm_kernel<BN, A_MN, B_MN, X3, Epi><<<grid, kThreads, C::kSmem, stream>>>(ops, sh, epi);
-  BT_LAUNCH_CHECK("umma_gemm_kernel");
   return BT_OK;
 }
 

@@ -769,6 +769,8 @@ extern "C" int bt_learner_create(const bt_learner_config* cfg, bt_learner** out)
 
 extern "C" void bt_learner_destroy(bt_learner* L) {
   if (!L) return;
+  if (L->graph) cudaGraphExecDestroy(L->graph);  // before the communicator it may use
+  if (L->cap_stream) cudaStreamDestroy(L->cap_stream);
   if (L->comm) comm_destroy(L->comm);
   for (cudaEvent_t e : L->prof.pool) cudaEventDestroy(e);
   for (cudaEvent_t e : L->fork_events) cudaEventDestroy(e);
@@ -841,14 +843,12 @@ extern "C" int bt_learner_get_state(bt_learner* L, float* params, float* mu, flo
   return BT_OK;
 }
 
-extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int32_t* perm,
-                                 float* stats, void* stream) {
-  BT_CHECK_ARG(L && perm, "bt_learner_update: null argument");
-  BT_TRY(check_batch(L, batch));
-  if (L->recurrent) return recurrent_update(L, batch, perm, stats, (cudaStream_t)stream);
+namespace {
+
+// The body of one PPO.update (non-recurrent), enqueued on s (and side streams joined back).
+int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float* stats,
+                cudaStream_t s) {
   const int world = std::max(1, L->cfg.world_size);
-  BT_CHECK_ARG(world == 1 || L->comm, "world_size %d needs bt_learner_comm_init", world);
-  cudaStream_t s = (cudaStream_t)stream;
   const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
   const int64_t Bg = L->B * world;
   BT_TRY(bootstrap_and_gae(L, batch, s));
@@ -881,6 +881,101 @@ extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int
   BT_K(L, kProfMisc, s, launch_increment(L->count_d, E * M, s));
   if (L->comm) BT_TRY(comm_allreduce_f64(L->comm, L->stat_sums, (size_t)E * M * kNumStatSums, s));
   if (stats) BT_K(L, kProfStats, s, launch_stat_finalize(L->stat_sums, E * M, 1.0f / (float)L->mb, stats, s));
+  return BT_OK;
+}
+
+void batch_key(const bt_batch* b, bool stats, const void* (&key)[10]) {
+  const void* k[10] = {b->obs,      b->bootstrap_obs, b->action, b->reward,
+                       b->terminated, b->truncated,   b->log_prob, b->value,
+                       stats ? (const void*)1 : nullptr, nullptr};
+  for (int i = 0; i < 10; ++i) key[i] = k[i];
+}
+
+bool same_key(const void* const (&a)[10], const void* const (&b)[10]) {
+  for (int i = 0; i < 10; ++i)
+    if (a[i] != b[i]) return false;
+  return true;
+}
+
+// Captures update_body into L->graph (updating the existing executable graph in place when
+// the topology allows it). The capture enqueues nothing: the launches it counted are
+// recorded as the graph's and removed from the live count.
+int capture_update(bt_learner* L, const bt_batch* batch, bool stats) {
+  const int64_t n0 = L->prof.launches;
+  if (!L->cap_stream) BT_CUDA(cudaStreamCreateWithFlags(&L->cap_stream, cudaStreamNonBlocking));
+  const cudaStream_t cs = L->cap_stream;
+  BT_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  const int rc = update_body(L, batch, L->perm_d, stats ? L->stats_d : nullptr, cs);
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(cs, &g);
+  L->graph_launches = L->prof.launches - n0;
+  L->prof.launches = n0;
+  if (rc != BT_OK || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    if (rc != BT_OK) return rc;
+    set_error("bt_learner_update: stream capture failed: %s", cudaGetErrorString(e));
+    return BT_ERR_CUDA;
+  }
+  if (L->graph) {
+    cudaGraphExecUpdateResultInfo info;
+    if (cudaGraphExecUpdate(L->graph, g, &info) != cudaSuccess) {
+      cudaGetLastError();
+      cudaGraphExecDestroy(L->graph);
+      L->graph = nullptr;
+    }
+  }
+  cudaError_t ie = cudaSuccess;
+  if (!L->graph) ie = cudaGraphInstantiate(&L->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) {
+    L->graph = nullptr;
+    set_error("bt_learner_update: graph instantiation failed: %s", cudaGetErrorString(ie));
+    return BT_ERR_CUDA;
+  }
+  return BT_OK;
+}
+
+}  // namespace
+
+extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int32_t* perm,
+                                 float* stats, void* stream) {
+  BT_CHECK_ARG(L && perm, "bt_learner_update: null argument");
+  BT_TRY(check_batch(L, batch));
+  if (L->recurrent) return recurrent_update(L, batch, perm, stats, (cudaStream_t)stream);
+  const int world = std::max(1, L->cfg.world_size);
+  BT_CHECK_ARG(world == 1 || L->comm, "world_size %d needs bt_learner_comm_init", world);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!L->graphs_on || L->prof.on) return update_body(L, batch, perm, stats, s);
+  const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
+  const size_t perm_bytes = (size_t)E * L->B * world * sizeof(int32_t);
+  if (!L->perm_d) {
+    BT_TRY(dalloc(L, &L->perm_d, perm_bytes / sizeof(int32_t)));
+    BT_TRY(dalloc(L, &L->stats_d, (size_t)E * M * 8));
+  }
+  BT_CUDA(cudaMemcpyAsync(L->perm_d, perm, perm_bytes, cudaMemcpyDeviceToDevice, s));
+  const void* key[10];
+  batch_key(batch, stats != nullptr, key);
+  if (L->graph && same_key(key, L->graph_key)) {
+    BT_CUDA(cudaGraphLaunch(L->graph, s));
+    L->prof.launches += L->graph_launches;
+  } else if (same_key(key, L->seen_key)) {
+    BT_TRY(capture_update(L, batch, stats != nullptr));
+    for (int i = 0; i < 10; ++i) L->graph_key[i] = key[i];
+    BT_CUDA(cudaGraphLaunch(L->graph, s));
+    L->prof.launches += L->graph_launches;
+  } else {
+    for (int i = 0; i < 10; ++i) L->seen_key[i] = key[i];
+    BT_TRY(update_body(L, batch, L->perm_d, stats ? L->stats_d : nullptr, s));
+  }
+  if (stats)
+    BT_CUDA(cudaMemcpyAsync(stats, L->stats_d, (size_t)E * M * 8 * sizeof(float),
+                            cudaMemcpyDeviceToDevice, s));
+  return BT_OK;
+}
+
+extern "C" int bt_learner_use_graphs(bt_learner* L, int32_t enable) {
+  BT_CHECK_ARG(L, "null learner");
+  L->graphs_on = enable != 0;
   return BT_OK;
 }
 

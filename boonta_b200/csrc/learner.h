@@ -178,6 +178,18 @@ struct bt_learner {
   // caller's stream through events, so the call keeps the caller's stream order.
   cudaStream_t side[4] = {nullptr, nullptr, nullptr, nullptr};
   std::vector<cudaEvent_t> fork_events;
+  // CUDA-graph replay of bt_learner_update: the first call with a given set of batch
+  // pointers runs eagerly, the second captures the update into a graph, later calls with
+  // the same pointers replay it. Permutations and statistics pass through the stable
+  // buffers perm_d / stats_d so that they do not change the captured arguments.
+  bool graphs_on = true;
+  cudaStream_t cap_stream = nullptr;  // captures run here (the caller's may be the legacy stream)
+  cudaGraphExec_t graph = nullptr;
+  int64_t graph_launches = 0;  // kernels and collectives in the graph
+  const void* graph_key[10] = {};
+  const void* seen_key[10] = {};
+  int32_t* perm_d = nullptr;
+  float* stats_d = nullptr;
   size_t next_event = 0;
 };
 

@@ -177,6 +177,10 @@ class Learner:
         _lib.check(_lib.lib().bt_learner_update(self._h, C.byref(b), _ptr(perm), _ptr(st), _stream()))
         return st
 
+    def use_graphs(self, enable: bool = True):
+        """Replay updates as a captured CUDA graph (the default) or enqueue them eagerly."""
+        _lib.check(_lib.lib().bt_learner_use_graphs(self._h, int(enable)))
+
     def targets(self):
         n = self.num_steps * self.num_envs
         adv = torch.empty(n, dtype=torch.float32, device=self.device)

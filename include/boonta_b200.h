@@ -175,6 +175,13 @@ BT_API int bt_learner_get_state(bt_learner* learner, float* params, float* mu, f
 BT_API int bt_learner_update(bt_learner* learner, const bt_batch* batch, const int32_t* permutations,
                       float* stats, void* stream);
 
+/* CUDA-graph replay of bt_learner_update (on by default; no counterpart in the reference,
+ * where XLA compiles the update into one program). The first update with a given set of
+ * batch pointers runs eagerly, the second is captured into a CUDA graph, and later updates
+ * with the same batch pointers replay it (the permutations and statistics are copied through
+ * internal buffers, so they may change between calls). While profiling, updates run eagerly. */
+BT_API int bt_learner_use_graphs(bt_learner* learner, int32_t enable);
+
 /* Targets of the last update: advantages/returns [T, N], bootstrap values [N]. */
 BT_API int bt_learner_targets(bt_learner* learner, float* advantages, float* returns,
                        float* bootstrap, void* stream);
