@@ -16,7 +16,8 @@ def __getattr__(name):
         from . import learner
 
         return getattr(learner, name)
-    if name in ("PPO", "PPOState"):
+    if name in ("PPO", "PPOState", "RecurrentPPO", "RecurrentPPOState", "RecurrentPPOConfig",
+                "Timestep", "Transition", "AdamState", "generalized_advantage_estimator"):
         from . import ppo
 
         return getattr(ppo, name)
