@@ -1,17 +1,28 @@
-// K5/K6/K7/K13: fused policy/value heads, PPO loss, loss gradient and logged statistics.
+// K5/K6/K7/K13: fused policy/value heads, PPO loss, loss gradient, head weight gradient
+// and logged statistics.
 //
-// One kernel per minibatch computes, for every live row of the minibatch:
-//   actor head  out = f_pi [W_pi; b_pi]     (logits, or the gaussian mean)
-//   critic head v   = f_v  [W_v; b_v]
-//   the clipped-surrogate / clipped-value / entropy loss of
-//   boonta/algorithms/ppo.py:77-121 and its gradient dL/d(out), dL/dv (with JAX's
-//   balanced tie rule for min/max/clip, ppo.py:95-114), dL/d f_pi and dL/d f_v through
-//   the head kernels, multiplied by the derivative of the tower's last activation,
-//   and the per-block partial sums behind the eight logged statistics (ppo.py:167-179).
-// Rows are processed in tiles of 32 staged in shared memory with the head kernels
-// (transposed, row stride = 1 mod 32 so that the dot products are bank-conflict free).
-// Per-block partial sums (statistics in double, the gaussian scale gradient in float)
-// are written to scratch and summed later in a fixed order, so results are
+// For every live row of a minibatch the kernel computes
+//   actor head  out = act(f_pi) [W_pi; b_pi]    (logits, or the gaussian mean)
+//   critic head v   = act(f_v)  [w_v; b_v]
+//   the clipped-surrogate / clipped-value / entropy loss of boonta/algorithms/ppo.py:77-121
+//   and its gradient dL/d(out), dL/dv (JAX's balanced tie rule for min/max/clip,
+//   ppo.py:95-114), dL/d f through the head kernels times the derivative of the tower's
+//   last activation, the per-block partial sums behind the eight logged statistics
+//   (ppo.py:167-179) and, when the head is small enough to keep its gradient in registers,
+//   the head weight gradients [f, 1]^T dL/d(out) and [f, 1]^T dL/dv as per-block partials.
+//
+// Work unit: a tile of 32 rows, 256 threads (8 warps), grid-stride over the tiles.
+//   1. the tile's pre-activations are loaded (float4, coalesced) and act(f) staged in
+//      shared memory, row stride F + 4 (16-byte rows, conflict-free float4 access);
+//   2. head outputs: warp w sums the feature slices w, w + 8, ... (4 features each) of row
+//      `lane` against the head kernel columns (shared memory, [j][k], broadcast float4
+//      reads) for all A + 1 outputs at once; the eight warp partials are added in order;
+//   3. loss: eight threads per row, thread `sub` owning outputs j = sub, sub + 8, ...;
+//      softmax / gaussian terms reduced over the eight with shuffles;
+//   4. dL/d f for the tile (same float4 mapping as 1, the pre-activation re-read for the
+//      activation derivative), stored as fp32 or bf16 (hi/lo);
+//   5. (fused head dW) thread k accumulates sum_r f[r][k] dL/d(out)[r][j] over its tiles.
+// Statistics are summed in double; all partial sums have a fixed order, so results are
 // deterministic for a fixed grid.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -20,17 +31,83 @@ namespace bt {
 
 constexpr int kHeadThreads = 256;
 constexpr int kHeadWarps = kHeadThreads / 32;
-constexpr int kMaxChunks = 4;  // float4 chunks per lane: feature widths up to 512
+constexpr int kTileRows = 32;
 constexpr float kLog2Pi = 1.8378770664093453f;
 
-// Shared memory: transposed head kernels wT[j][k] (actor rows j < A, then the critic row),
-// the biases, per-warp head outputs / output gradients, gaussian constants, reductions.
-size_t heads_smem_bytes(int F_pi, int F_v, int A, bool /*shared*/) {
-  size_t floats = (size_t)A * F_pi + F_v + (A + 1);  // wT, wTv, biases
-  floats += 2 * (size_t)kHeadWarps * (A + 1);         // out / dout per warp
-  floats += 3 * (size_t)A;                            // sigma, 1/sigma, log sigma
-  floats += (size_t)kHeadWarps * A;                   // dscale reduction
-  return floats * 4 + (size_t)kHeadWarps * kNumStatSums * 8 + 64;
+// Shared-memory layout of the heads kernel, in floats (every region 16-byte aligned).
+struct HeadsLayout {
+  int F, Fv, A, JP;
+  bool shared;
+  int ldf, ldv;
+  size_t f, fv, wj, wv, bias, red, vred, d, sig, isig, lsig, total;
+};
+
+// Padded output count JP of the kernel instance that serves A actions (A + 1 outputs):
+// 4, 8, 12 or 16 with the fused head weight gradient, 16, 32, 48 or 64 without.
+__host__ __device__ inline int heads_inst_jp(int A, bool fuse) {
+  const int n = A + 1;
+  if (fuse) return n <= 4 ? 4 : n <= 8 ? 8 : n <= 12 ? 12 : 16;
+  return n <= 16 ? 16 : n <= 32 ? 32 : n <= 48 ? 48 : 64;
+}
+
+__host__ __device__ inline HeadsLayout heads_layout(int F, int Fv, int A, bool shared, int JP) {
+  HeadsLayout L{};
+  L.F = F;
+  L.Fv = Fv;
+  L.A = A;
+  L.JP = JP;
+  L.shared = shared;
+  L.ldf = F + 4;
+  L.ldv = Fv + 4;
+  size_t o = 0;
+  auto take = [&](size_t n) {
+    const size_t at = o;
+    o += (n + 3) / 4 * 4;
+    return at;
+  };
+  L.f = take((size_t)kTileRows * L.ldf);
+  L.fv = take(shared ? 0 : (size_t)kTileRows * L.ldv);
+  L.wj = take((size_t)L.JP * F);
+  L.wv = take(shared ? 0 : Fv);
+  L.bias = take(L.JP);
+  // phase-2 partials; after the last tile the same space holds the final reductions
+  // (32 x 12 doubles of statistics and 32 x JP floats of gaussian scale gradient)
+  const size_t red_a = (size_t)kHeadWarps * kTileRows * L.JP;
+  const size_t red_b = (size_t)kTileRows * kNumStatSums * 2 + (size_t)kTileRows * L.JP;
+  L.red = take(red_a > red_b ? red_a : red_b);
+  L.vred = take(shared ? 0 : (size_t)kHeadWarps * kTileRows);
+  L.d = take((size_t)kTileRows * L.JP);
+  L.sig = take(L.JP);
+  L.isig = take(L.JP);
+  L.lsig = take(L.JP);
+  L.total = o;
+  return L;
+}
+
+bool heads_fuse_dw(int F_pi, int F_v, int A, bool /*shared*/) {
+  return A + 1 <= 16 && F_pi <= kHeadThreads && F_v <= kHeadThreads;
+}
+
+static size_t heads_smem_for(int F_pi, int F_v, int A, bool shared, bool fuse) {
+  return heads_layout(F_pi, F_v, A, shared, heads_inst_jp(A, fuse)).total * sizeof(float);
+}
+
+size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared) {
+  return heads_smem_for(F_pi, F_v, A, shared, heads_fuse_dw(F_pi, F_v, A, shared));
+}
+
+// Sum / max over the eight threads of a row group (lanes differing in bits 0..2).
+__device__ __forceinline__ float group8_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  return v;
+}
+__device__ __forceinline__ float group8_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  return v;
 }
 
 template <int A>
@@ -38,301 +115,420 @@ __device__ __forceinline__ float4 act4(float4 z) {
   return make_float4(act_fwd<A>(z.x), act_fwd<A>(z.y), act_fwd<A>(z.z), act_fwd<A>(z.w));
 }
 
-// f = act(pre) for all of a lane's chunks, the activation resolved once.
-__device__ __forceinline__ void act_row(const float4 (&z)[kMaxChunks], int act,
-                                        float4 (&f)[kMaxChunks]) {
-  with_act(act, [&](auto tag) {
-#pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) f[i] = act4<decltype(tag)::value>(z[i]);
-  });
-}
+// Stage act(pre) of the tile's rows [row0, row0 + 32) into f_s (rows past `live` as 0).
+// Each thread handles float4 chunks c = tid + 256 i; the loads of a batch of eight chunks
+// are all issued before any is used, so their latencies overlap.
+constexpr int kBatch = 8;
 
-__device__ __forceinline__ void load_row(const float* src, int F, int lane, float4 (&v)[kMaxChunks]) {
+template <int ACT>
+__device__ __forceinline__ void stage_features(const float* pre, int F, int ld, int row0,
+                                               int live, float* f_s) {
+  const int q4 = F / 4, total = kTileRows * q4;
+  {
+    for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
+      float4 z[kBatch];
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int q = lane + 32 * i;
-    v[i] = (4 * q < F) ? __ldg(reinterpret_cast<const float4*>(src) + q) : make_float4(0, 0, 0, 0);
-  }
-}
-
-__device__ __forceinline__ float dot_row(const float4 (&f)[kMaxChunks], const float* w, int F,
-                                         int lane) {
-  float acc = 0.f;
+      for (int i = 0; i < kBatch; ++i) {
+        const int c = c0 + i * kHeadThreads;
+        const int r = c / q4, q = c - r * q4;
+        z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < total && row0 + r < live)
+          z[i] = __ldg(reinterpret_cast<const float4*>(pre + (size_t)(row0 + r) * F) + q);
+      }
 #pragma unroll
-  for (int i = 0; i < kMaxChunks; ++i) {
-    const int q = lane + 32 * i;
-    if (4 * q < F) {
-      const float4 ww = reinterpret_cast<const float4*>(w)[q];
-      acc = fmaf(f[i].x, ww.x, acc);
-      acc = fmaf(f[i].y, ww.y, acc);
-      acc = fmaf(f[i].z, ww.z, acc);
-      acc = fmaf(f[i].w, ww.w, acc);
+      for (int i = 0; i < kBatch; ++i) {
+        const int c = c0 + i * kHeadThreads;
+        const int r = c / q4, q = c - r * q4;
+        if (c < total)
+          *reinterpret_cast<float4*>(f_s + r * ld + 4 * q) = act4<ACT>(z[i]);
+      }
     }
   }
-  return warp_sum(acc);
 }
 
-// dL/d f for the lane's chunks, times the tower's last activation derivative, stored as
-// fp32 or bf16 (hi/lo) at row `row`.
-__device__ __forceinline__ void store_df(float4 g, const float4& pre, int act, size_t base, int q,
-                                         float* df, __nv_bfloat16* dfb, __nv_bfloat16* dfb_lo) {
-  with_act(act, [&](auto tag) {
-    constexpr int A = decltype(tag)::value;
-    g.x *= act_dz<A>(pre.x);
-    g.y *= act_dz<A>(pre.y);
-    g.z *= act_dz<A>(pre.z);
-    g.w *= act_dz<A>(pre.w);
-  });
-  const size_t i = base + 4 * (size_t)q;
-  if (dfb) {
-    store_bf16(dfb, dfb_lo, i, g.x);
-    store_bf16(dfb, dfb_lo, i + 1, g.y);
-    store_bf16(dfb, dfb_lo, i + 2, g.z);
-    store_bf16(dfb, dfb_lo, i + 3, g.w);
-  } else {
-    *reinterpret_cast<float4*>(df + i) = g;
+// dL/d pre of the tile: g = (sum_j d[r][j] w[j][k]) * act'(pre), for the actor tower
+// (JP outputs through wj_s) or the critic tower (output jcol through wv_s). Batches of
+// eight chunks as in stage_features (pre-activations loaded first).
+template <int JP, int Act>
+__device__ __forceinline__ void store_feature_grad(const float* pre, int F, int row0,
+                                                   int live, int rows_cap, const float* d_s,
+                                                   const float* w_s, int nj, int jcol,
+                                                   float* df, __nv_bfloat16* dfb,
+                                                   __nv_bfloat16* dfb_lo) {
+  const int q4 = F / 4, total = kTileRows * q4;
+  {
+    for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
+      float4 z[kBatch];
+      if constexpr (Act != BT_ACT_NONE) {
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          const int c = c0 + i * kHeadThreads;
+          const int r = c / q4, q = c - r * q4;
+          z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (c < total && row0 + r < live)
+            z[i] = __ldg(reinterpret_cast<const float4*>(pre + (size_t)(row0 + r) * F) + q);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const int c = c0 + i * kHeadThreads;
+        const int r = c / q4, q = c - r * q4;
+        const int row = row0 + r;
+        if (c >= total || row >= rows_cap) continue;
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (nj > 1) {
+#pragma unroll 4
+          for (int j = 0; j < JP; ++j) {
+            const float dj = d_s[r * JP + j];
+            const float4 w = *reinterpret_cast<const float4*>(w_s + (size_t)j * F + 4 * q);
+            g.x = fmaf(dj, w.x, g.x);
+            g.y = fmaf(dj, w.y, g.y);
+            g.z = fmaf(dj, w.z, g.z);
+            g.w = fmaf(dj, w.w, g.w);
+          }
+        } else {
+          const float dj = d_s[r * JP + jcol];
+          const float4 w = *reinterpret_cast<const float4*>(w_s + 4 * q);
+          g = make_float4(dj * w.x, dj * w.y, dj * w.z, dj * w.w);
+        }
+        if constexpr (Act != BT_ACT_NONE) {
+          g.x *= act_dz<Act>(z[i].x);
+          g.y *= act_dz<Act>(z[i].y);
+          g.z *= act_dz<Act>(z[i].z);
+          g.w *= act_dz<Act>(z[i].w);
+        }
+        const size_t e = (size_t)row * F + 4 * q;
+        if (dfb) {
+          store_bf16x4(dfb, dfb_lo, e, g);
+        } else {
+          *reinterpret_cast<float4*>(df + e) = g;
+        }
+      }
+    }
   }
 }
 
-// One warp per row (grid-stride over the minibatch rows). All loads of a row — the
-// features of both towers and the pre-activations behind the activation derivative — are
-// issued together as float4s before any arithmetic.
-__global__ void __launch_bounds__(kHeadThreads) heads_loss_kernel(HeadsParams p) {
+template <int JP, bool FUSE, int ACT>
+__global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams p) {
+  constexpr int JJ = (JP + 7) / 8;  // outputs per thread in the loss phase
   extern __shared__ __align__(16) float sm[];
-  const int A = p.A;
+  const int F = p.F_pi, Fv = p.F_v, A = p.A;
   const bool shared = (p.f_v == p.f_pi);
-  const int F = p.F_pi, Fv = p.F_v;
-  float* wT = sm;                          // [A][F]
-  float* wTv = wT + (size_t)A * F;         // [Fv]
-  float* bias = wTv + Fv;                  // [A + 1] (actor biases, critic bias)
-  float* out_s = bias + (A + 1);           // [warps][A + 1]
-  float* dout_s = out_s + kHeadWarps * (A + 1);
-  float* sig_s = dout_s + kHeadWarps * (A + 1);
-  float* isig_s = sig_s + A;
-  float* lsig_s = isig_s + A;
-  float* red_s = lsig_s + A;               // [warps][A]
-  double* stat_s = reinterpret_cast<double*>(
-      (reinterpret_cast<uintptr_t>(red_s + kHeadWarps * A) + 7) & ~uintptr_t(7));
+  const HeadsLayout Lo = heads_layout(F, Fv, A, shared, JP);
+  float* f_s = sm + Lo.f;
+  float* fv_s = sm + Lo.fv;
+  float* wj_s = sm + Lo.wj;
+  float* wv_s = sm + Lo.wv;
+  float* bias_s = sm + Lo.bias;
+  float* red_s = sm + Lo.red;
+  float* vred_s = sm + Lo.vred;
+  float* d_s = sm + Lo.d;
+  float* isig_s = sm + Lo.isig;
+  float* lsig_s = sm + Lo.lsig;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int live = live_rows(p.count, p.rows);
+  const int tiles = ceil_div(live, kTileRows);
 
-  for (int i = tid; i < F * A; i += kHeadThreads) {
-    const int k = i / A, j = i - k * A;
-    wT[(size_t)j * F + k] = p.w_pi[i];
+  // head kernels as columns wj[j][k] (j < A actor outputs, j = A the value when the torso
+  // is shared, the rest zero), biases, gaussian constants
+  for (int i = tid; i < JP * F; i += kHeadThreads) {
+    const int j = i / F, k = i - j * F;
+    float w = 0.f;
+    if (j < A) w = p.w_pi[(size_t)k * A + j];
+    else if (j == A && shared) w = p.w_v[k];
+    wj_s[i] = w;
   }
-  for (int k = tid; k < Fv; k += kHeadThreads) wTv[k] = p.w_v[k];
-  for (int j = tid; j < A; j += kHeadThreads) bias[j] = p.w_pi[(size_t)F * A + j];
-  if (tid == 0) bias[A] = p.w_v[Fv];
+  if (!shared)
+    for (int k = tid; k < Fv; k += kHeadThreads) wv_s[k] = p.w_v[k];
+  for (int j = tid; j < JP; j += kHeadThreads)
+    bias_s[j] = j < A ? p.w_pi[(size_t)F * A + j] : (j == A ? p.w_v[Fv] : 0.f);
   if (p.head == BT_HEAD_GAUSSIAN) {
     for (int j = tid; j < A; j += kHeadThreads) {
-      const float s = p.scale[j];
-      const float sig = (fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)))) + 1e-3f;  // softplus + 1e-3
-      sig_s[j] = sig;
+      const float sc = p.scale[j];
+      const float sig = (fmaxf(sc, 0.f) + log1pf(expf(-fabsf(sc)))) + 1e-3f;  // softplus + 1e-3
       isig_s[j] = 1.f / sig;
       lsig_s[j] = logf(sig);
     }
   }
   __syncthreads();
 
+  // loss-phase identity: row r of the tile, output group sub
+  const int r = tid >> 3, sub = tid & 7;
   double st[kNumStatSums];
 #pragma unroll
   for (int s = 0; s < kNumStatSums; ++s) st[s] = 0.0;
-  float dscale_acc[2] = {0.f, 0.f};  // lanes own j = lane, lane + 32
-  float* o = out_s + warp * (A + 1);
-  float* d = dout_s + warp * (A + 1);
+  float dsc[JJ];
+#pragma unroll
+  for (int jj = 0; jj < JJ; ++jj) dsc[jj] = 0.f;
+  // fused head dW: thread k of the features
+  float accw[FUSE ? JP : 1];
+#pragma unroll
+  for (int j = 0; j < (FUSE ? JP : 1); ++j) accw[j] = 0.f;
+  float accv = 0.f, accb = 0.f;
 
-  for (int row = blockIdx.x * kHeadWarps + warp; row < live; row += gridDim.x * kHeadWarps) {
-    const int flat = p.idx ? p.idx[row] : row;
-    // the towers' pre-activations; the head input is act(pre), recomputed here
-    float4 f[kMaxChunks], fv[kMaxChunks], zp[kMaxChunks], zv[kMaxChunks];
-    load_row(p.f_pi + (size_t)row * F, F, lane, zp);
-    if (!shared) load_row(p.f_v + (size_t)row * Fv, Fv, lane, zv);
-    act_row(zp, p.act_pi, f);
-    if (!shared) act_row(zv, p.act_v, fv);
-    const float lp_old = p.lp_old[flat];
-    const float adv = p.adv[flat];
-    const float ret = p.ret[flat];
-    const float v_old = p.v_old[flat];
-    int action = 0;
-    if (p.head == BT_HEAD_CATEGORICAL) action = reinterpret_cast<const int*>(p.action)[flat];
-    float act_j[2] = {0.f, 0.f};
-    if (p.head == BT_HEAD_GAUSSIAN) {
-      const float* av = reinterpret_cast<const float*>(p.action) + (size_t)flat * A;
-      if (lane < A) act_j[0] = av[lane];
-      if (lane + 32 < A) act_j[1] = av[lane + 32];
-    }
-    // Head outputs.
-    for (int j = 0; j < A; ++j) {
-      const float t = dot_row(f, wT + (size_t)j * F, F, lane);
-      if (lane == 0) o[j] = t + bias[j];
-    }
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int row0 = tile * kTileRows;
+    // 1. features
+    stage_features<ACT>(p.f_pi, F, Lo.ldf, row0, live, f_s);
+    if (!shared) stage_features<ACT>(p.f_v, Fv, Lo.ldv, row0, live, fv_s);
+    __syncthreads();
+
+    // 2. head outputs: warp partials over interleaved 4-feature slices
     {
-      const float t = shared ? dot_row(f, wTv, F, lane) : dot_row(fv, wTv, Fv, lane);
-      if (lane == 0) o[A] = t + bias[A];
-    }
-    __syncwarp();
-    const float value = o[A];
-    float lp, ent;
-    float pj[2] = {0.f, 0.f}, lpj[2] = {0.f, 0.f}, zj[2] = {0.f, 0.f};
-    if (p.head == BT_HEAD_CATEGORICAL) {
-      float mx = -INFINITY;
-      for (int j = lane; j < A; j += 32) mx = fmaxf(mx, o[j]);
-      mx = warp_max(mx);
-      float se = 0.f;
-      for (int j = lane; j < A; j += 32) se += expf(o[j] - mx);
-      se = warp_sum(se);
-      const float lse = logf(se);
-      float h = 0.f;
+      float acc[JP];
 #pragma unroll
-      for (int qq = 0; qq < 2; ++qq) {
-        const int j = lane + 32 * qq;
-        if (j < A) {
-          lpj[qq] = (o[j] - mx) - lse;
-          pj[qq] = expf(lpj[qq]);
-          h -= pj[qq] * lpj[qq];
+      for (int j = 0; j < JP; ++j) acc[j] = 0.f;
+      const float* frow = f_s + lane * Lo.ldf;
+      for (int sl = warp; sl < F / 4; sl += kHeadWarps) {
+        const float4 x = *reinterpret_cast<const float4*>(frow + 4 * sl);
+#pragma unroll
+        for (int j = 0; j < JP; ++j) {
+          const float4 w = *reinterpret_cast<const float4*>(wj_s + (size_t)j * F + 4 * sl);
+          acc[j] = fmaf(x.x, w.x, acc[j]);
+          acc[j] = fmaf(x.y, w.y, acc[j]);
+          acc[j] = fmaf(x.z, w.z, acc[j]);
+          acc[j] = fmaf(x.w, w.w, acc[j]);
         }
       }
-      ent = warp_sum(h);
-      lp = (o[action] - mx) - lse;
-    } else {
-      float acc = 0.f, e = 0.f;
+      float* rp = red_s + (size_t)(warp * kTileRows + lane) * JP;
 #pragma unroll
-      for (int qq = 0; qq < 2; ++qq) {
-        const int j = lane + 32 * qq;
-        if (j < A) {
-          zj[qq] = (act_j[qq] - o[j]) * isig_s[j];
-          acc += -0.5f * zj[qq] * zj[qq] - lsig_s[j] - 0.5f * kLog2Pi;
-          e += 0.5f + 0.5f * kLog2Pi + lsig_s[j];
+      for (int j = 0; j < JP; j += 4)
+        *reinterpret_cast<float4*>(rp + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      if (!shared) {
+        float v = 0.f;
+        const float* vrow = fv_s + lane * Lo.ldv;
+        for (int sl = warp; sl < Fv / 4; sl += kHeadWarps) {
+          const float4 x = *reinterpret_cast<const float4*>(vrow + 4 * sl);
+          const float4 w = *reinterpret_cast<const float4*>(wv_s + 4 * sl);
+          v = fmaf(x.x, w.x, v);
+          v = fmaf(x.y, w.y, v);
+          v = fmaf(x.z, w.z, v);
+          v = fmaf(x.w, w.w, v);
         }
+        vred_s[warp * kTileRows + lane] = v;
       }
-      lp = warp_sum(acc);
-      ent = warp_sum(e);
     }
-    // Surrogate (ppo.py:90-103), with JAX's balanced tie rule for min/max/clip.
-    const float eps = p.clip;
-    const float ratio = expf(lp - lp_old);
-    const float lo = 1.f - eps, hi = 1.f + eps;
-    const float u = fmaxf(ratio, lo);
-    const float du = (ratio == u) ? ((lo == u) ? 0.5f : 1.f) : 0.f;
-    const float clipped = fminf(u, hi);
-    const float dm = (u == clipped) ? ((hi == clipped) ? 0.5f : 1.f) : 0.f;
-    const float s1 = ratio * adv, s2 = clipped * adv;
-    const float mn = fminf(s1, s2);
-    const float t1 = (s1 == mn) ? ((s2 == mn) ? 0.5f : 1.f) : 0.f;
-    const float t2 = (s2 == mn) ? ((s1 == mn) ? 0.5f : 1.f) : 0.f;
-    const float g_lp = -((t1 * adv + t2 * adv * (dm * du)) * ratio) * p.inv_mb;
-    const float g_ent = -p.ent_coef * p.inv_mb;
-    // Value loss (ppo.py:105-115).
-    const float c1 = 0.5f * ((value - ret) * (value - ret));
-    float crit, dcrit;
-    if (p.clip_value) {
-      const float dv = value - v_old;
-      const float uu = fmaxf(dv, -eps);
-      const float duu = (dv == uu) ? ((-eps == uu) ? 0.5f : 1.f) : 0.f;
-      const float cl = fminf(uu, eps);
-      const float dcl = (uu == cl) ? ((eps == cl) ? 0.5f : 1.f) : 0.f;
-      const float vc = v_old + cl;
-      const float c2 = 0.5f * ((vc - ret) * (vc - ret));
-      crit = fmaxf(c1, c2);
-      const float w1 = (c1 == crit) ? ((c2 == crit) ? 0.5f : 1.f) : 0.f;
-      const float w2 = (c2 == crit) ? ((c1 == crit) ? 0.5f : 1.f) : 0.f;
-      dcrit = w1 * (value - ret) + w2 * (vc - ret) * (dcl * duu);
-    } else {
-      crit = c1;
-      dcrit = value - ret;
-    }
-    const float d_value = p.vf_coef * p.inv_mb * dcrit;
+    __syncthreads();
+
+    // 3. loss and output gradients, eight threads per row
+    {
+      const int row = row0 + r;
+      const bool on = row < live;
+      float o[JJ];
 #pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-      const int j = lane + 32 * qq;
-      if (j < A) {
-        float g;
-        if (p.head == BT_HEAD_CATEGORICAL) {
-          g = g_lp * (((j == action) ? 1.f : 0.f) - pj[qq]) + g_ent * (-pj[qq] * (lpj[qq] + ent));
-        } else {
-          g = g_lp * (zj[qq] * isig_s[j]);
-          dscale_acc[qq] += g_lp * ((zj[qq] * zj[qq] - 1.f) * isig_s[j]) + g_ent * isig_s[j];
+      for (int jj = 0; jj < JJ; ++jj) {
+        const int j = sub + 8 * jj;
+        float t = 0.f;
+        if (j < JP) {
+          t = bias_s[j];
+          for (int w = 0; w < kHeadWarps; ++w) t += red_s[(size_t)(w * kTileRows + r) * JP + j];
         }
-        d[j] = g;
-        p.d_out[(size_t)row * A + j] = g;
+        o[jj] = t;
       }
-    }
-    if (lane == 0) {
-      d[A] = d_value;
-      p.d_val[row] = d_value;
-      st[0] += (double)mn;
-      st[1] += (double)ent;
-      st[2] += (double)(lp_old - lp);
-      st[3] += (fabsf(ratio - 1.f) > eps) ? 1.0 : 0.0;
-      st[4] += (double)adv;
-      st[5] += (double)crit;
-      const double res = (double)ret - (double)value;
-      st[6] += res;
-      st[7] += res * res;
-      st[8] += (double)ret;
-      st[9] += (double)ret * (double)ret;
-      st[10] += (double)value;
-      st[11] += 1.0;
-    }
-    __syncwarp();
-    // dL/d f = d_out W_pi^T (+ d_value w_v^T when shared), times act'.
-#pragma unroll
-    for (int i = 0; i < kMaxChunks; ++i) {
-      const int q = lane + 32 * i;
-      if (4 * q >= F) continue;
-      float4 g = make_float4(0, 0, 0, 0);
-      for (int j = 0; j < A; ++j) {
-        const float dj = d[j];
-        const float4 w = reinterpret_cast<const float4*>(wT + (size_t)j * F)[q];
-        g.x = fmaf(dj, w.x, g.x);
-        g.y = fmaf(dj, w.y, g.y);
-        g.z = fmaf(dj, w.z, g.z);
-        g.w = fmaf(dj, w.w, g.w);
-      }
+      float value = bias_s[A];
       if (shared) {
-        const float4 w = reinterpret_cast<const float4*>(wTv)[q];
-        g.x = fmaf(d[A], w.x, g.x);
-        g.y = fmaf(d[A], w.y, g.y);
-        g.z = fmaf(d[A], w.z, g.z);
-        g.w = fmaf(d[A], w.w, g.w);
+        for (int w = 0; w < kHeadWarps; ++w) value += red_s[(size_t)(w * kTileRows + r) * JP + A];
+      } else {
+        for (int w = 0; w < kHeadWarps; ++w) value += vred_s[w * kTileRows + r];
       }
-      store_df(g, zp[i], p.act_pi, (size_t)row * F, q, p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
-    }
-    if (!shared) {
+      const int flat = on ? (p.idx ? p.idx[row] : row) : 0;
+      const float lp_old = on ? p.lp_old[flat] : 0.f;
+      const float adv = on ? p.adv[flat] : 0.f;
+      const float ret = on ? p.ret[flat] : 0.f;
+      const float v_old = on ? p.v_old[flat] : 0.f;
+      float lp, ent;
+      float pj[JJ], lpj[JJ], zj[JJ];
 #pragma unroll
-      for (int i = 0; i < kMaxChunks; ++i) {
-        const int q = lane + 32 * i;
-        if (4 * q >= Fv) continue;
-        const float4 w = reinterpret_cast<const float4*>(wTv)[q];
-        const float4 g = make_float4(d[A] * w.x, d[A] * w.y, d[A] * w.z, d[A] * w.w);
-        store_df(g, zv[i], p.act_v, (size_t)row * Fv, q, p.d_fv, p.d_fv_b, p.d_fv_b_lo);
+      for (int jj = 0; jj < JJ; ++jj) pj[jj] = lpj[jj] = zj[jj] = 0.f;
+      int action = 0;
+      if (p.head == BT_HEAD_CATEGORICAL) {
+        if (on) action = reinterpret_cast<const int*>(p.action)[flat];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int jj = 0; jj < JJ; ++jj)
+          if (sub + 8 * jj < A) mx = fmaxf(mx, o[jj]);
+        mx = group8_max(mx);
+        float se = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < JJ; ++jj)
+          if (sub + 8 * jj < A) se += expf(o[jj] - mx);
+        se = group8_sum(se);
+        const float lse = logf(se);
+        float h = 0.f, mine = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < JJ; ++jj) {
+          const int j = sub + 8 * jj;
+          if (j < A) {
+            lpj[jj] = (o[jj] - mx) - lse;
+            pj[jj] = expf(lpj[jj]);
+            h -= pj[jj] * lpj[jj];
+            if (j == action) mine = lpj[jj];
+          }
+        }
+        ent = group8_sum(h);
+        lp = group8_sum(mine);  // one thread holds the action's log-prob, the rest 0
+      } else {
+        const float* av = reinterpret_cast<const float*>(p.action) + (size_t)flat * A;
+        float acc = 0.f, e = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < JJ; ++jj) {
+          const int j = sub + 8 * jj;
+          if (j < A) {
+            const float a = on ? av[j] : 0.f;
+            zj[jj] = (a - o[jj]) * isig_s[j];
+            acc += -0.5f * zj[jj] * zj[jj] - lsig_s[j] - 0.5f * kLog2Pi;
+            e += 0.5f + 0.5f * kLog2Pi + lsig_s[j];
+          }
+        }
+        lp = group8_sum(acc);
+        ent = group8_sum(e);
+      }
+      // Surrogate (ppo.py:90-103), with JAX's balanced tie rule for min/max/clip.
+      const float eps = p.clip;
+      const float ratio = expf(lp - lp_old);
+      const float lo = 1.f - eps, hi = 1.f + eps;
+      const float u = fmaxf(ratio, lo);
+      const float du = (ratio == u) ? ((lo == u) ? 0.5f : 1.f) : 0.f;
+      const float clipped = fminf(u, hi);
+      const float dm = (u == clipped) ? ((hi == clipped) ? 0.5f : 1.f) : 0.f;
+      const float s1 = ratio * adv, s2 = clipped * adv;
+      const float mn = fminf(s1, s2);
+      const float t1 = (s1 == mn) ? ((s2 == mn) ? 0.5f : 1.f) : 0.f;
+      const float t2 = (s2 == mn) ? ((s1 == mn) ? 0.5f : 1.f) : 0.f;
+      const float g_lp = -((t1 * adv + t2 * adv * (dm * du)) * ratio) * p.inv_mb;
+      const float g_ent = -p.ent_coef * p.inv_mb;
+      // Value loss (ppo.py:105-115).
+      const float c1 = 0.5f * ((value - ret) * (value - ret));
+      float crit, dcrit;
+      if (p.clip_value) {
+        const float dv = value - v_old;
+        const float uu = fmaxf(dv, -eps);
+        const float duu = (dv == uu) ? ((-eps == uu) ? 0.5f : 1.f) : 0.f;
+        const float cl = fminf(uu, eps);
+        const float dcl = (uu == cl) ? ((eps == cl) ? 0.5f : 1.f) : 0.f;
+        const float vc = v_old + cl;
+        const float c2 = 0.5f * ((vc - ret) * (vc - ret));
+        crit = fmaxf(c1, c2);
+        const float w1 = (c1 == crit) ? ((c2 == crit) ? 0.5f : 1.f) : 0.f;
+        const float w2 = (c2 == crit) ? ((c1 == crit) ? 0.5f : 1.f) : 0.f;
+        dcrit = w1 * (value - ret) + w2 * (vc - ret) * (dcl * duu);
+      } else {
+        crit = c1;
+        dcrit = value - ret;
+      }
+      const float d_value = on ? p.vf_coef * p.inv_mb * dcrit : 0.f;
+#pragma unroll
+      for (int jj = 0; jj < JJ; ++jj) {
+        const int j = sub + 8 * jj;
+        if (j >= JP) continue;
+        float g = 0.f;
+        if (j < A && on) {
+          if (p.head == BT_HEAD_CATEGORICAL) {
+            g = g_lp * (((j == action) ? 1.f : 0.f) - pj[jj]) +
+                g_ent * (-pj[jj] * (lpj[jj] + ent));
+          } else {
+            g = g_lp * (zj[jj] * isig_s[j]);
+            dsc[jj] += g_lp * ((zj[jj] * zj[jj] - 1.f) * isig_s[j]) + g_ent * isig_s[j];
+          }
+          if (p.d_out) p.d_out[(size_t)row * A + j] = g;
+        }
+        d_s[r * JP + j] = (j == A) ? d_value : g;
+      }
+      if (sub == 0 && on) {
+        if (p.d_val) p.d_val[row] = d_value;
+        st[0] += (double)mn;
+        st[1] += (double)ent;
+        st[2] += (double)(lp_old - lp);
+        st[3] += (fabsf(ratio - 1.f) > eps) ? 1.0 : 0.0;
+        st[4] += (double)adv;
+        st[5] += (double)crit;
+        const double res = (double)ret - (double)value;
+        st[6] += res;
+        st[7] += res * res;
+        st[8] += (double)ret;
+        st[9] += (double)ret * (double)ret;
+        st[10] += (double)value;
+        st[11] += 1.0;
       }
     }
-    __syncwarp();
+    __syncthreads();
+
+    // 4. dL/d pre for the towers
+    store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, wj_s, JP, 0, p.d_fpi,
+                           p.d_fpi_b, p.d_fpi_b_lo);
+    if (!shared)
+      store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, wv_s, 1, A, p.d_fv,
+                             p.d_fv_b, p.d_fv_b_lo);
+    // 5. head weight gradients
+    if constexpr (FUSE) {
+      if (tid < F) {
+        for (int rr = 0; rr < kTileRows; ++rr) {
+          const float fk = f_s[rr * Lo.ldf + tid];
+#pragma unroll
+          for (int j = 0; j < JP; j += 4) {
+            const float4 dd = *reinterpret_cast<const float4*>(d_s + rr * JP + j);
+            accw[j] = fmaf(fk, dd.x, accw[j]);
+            accw[j + 1] = fmaf(fk, dd.y, accw[j + 1]);
+            accw[j + 2] = fmaf(fk, dd.z, accw[j + 2]);
+            accw[j + 3] = fmaf(fk, dd.w, accw[j + 3]);
+          }
+        }
+      }
+      if (!shared && tid < Fv)
+        for (int rr = 0; rr < kTileRows; ++rr) accv = fmaf(fv_s[rr * Lo.ldv + tid], d_s[rr * JP + A], accv);
+      if (tid < JP)
+        for (int rr = 0; rr < kTileRows; ++rr) accb += d_s[rr * JP + tid];
+    }
+    __syncthreads();
   }
 
-  // Block partial sums in a fixed order: warps' lane 0 -> shared -> thread 0.
-  if (lane == 0) {
-    for (int s = 0; s < kNumStatSums; ++s) stat_s[warp * kNumStatSums + s] = st[s];
+  if constexpr (FUSE) {
+    float* pp = p.dw_pi_partials + (size_t)blockIdx.x * (F + 1) * A;
+    if (tid < F) {
+#pragma unroll
+      for (int j = 0; j < JP; ++j)
+        if (j < A) pp[(size_t)tid * A + j] = accw[j];
+    }
+    if (tid < A) pp[(size_t)F * A + tid] = accb;
+    float* pv = p.dw_v_partials + (size_t)blockIdx.x * (Fv + 1);
+    if (shared) {
+      if (tid < F) {
+#pragma unroll
+        for (int j = 0; j < JP; ++j)
+          if (j == A) pv[tid] = accw[j];
+      }
+    } else if (tid < Fv) {
+      pv[tid] = accv;
+    }
+    if (tid == A) pv[Fv] = accb;
+  }
+
+  // Block partial sums in a fixed order: row slots -> thread 0..11 (statistics), row slots
+  // -> thread j (gaussian scale gradient).
+  double* st_s = reinterpret_cast<double*>(red_s);
+  float* ds_s = red_s + kTileRows * kNumStatSums * 2;
+  if (sub == 0) {
+#pragma unroll
+    for (int s = 0; s < kNumStatSums; ++s) st_s[r * kNumStatSums + s] = st[s];
   }
   if (p.head == BT_HEAD_GAUSSIAN) {
 #pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-      const int j = lane + 32 * qq;
-      if (j < A) red_s[warp * A + j] = dscale_acc[qq];
+    for (int jj = 0; jj < JJ; ++jj) {
+      const int j = sub + 8 * jj;
+      if (j < A) ds_s[r * JP + j] = dsc[jj];
     }
   }
   __syncthreads();
   if (tid < kNumStatSums) {
     double s = 0.0;
-    for (int w = 0; w < kHeadWarps; ++w) s += stat_s[w * kNumStatSums + tid];
+    for (int rr = 0; rr < kTileRows; ++rr) s += st_s[rr * kNumStatSums + tid];
     p.stat_partials[(size_t)blockIdx.x * kNumStatSums + tid] = s;
   }
   if (p.head == BT_HEAD_GAUSSIAN && p.dscale_partials) {
     for (int j = tid; j < A; j += kHeadThreads) {
       float s = 0.f;
-      for (int w = 0; w < kHeadWarps; ++w) s += red_s[w * A + j];
+      for (int rr = 0; rr < kTileRows; ++rr) s += ds_s[rr * JP + j];
       const float sc = p.scale[j];
       const float sgm = 1.f / (1.f + expf(-sc));  // d softplus / d scale
       p.dscale_partials[(size_t)blockIdx.x * A + j] = s * sgm;
@@ -340,26 +536,55 @@ __global__ void __launch_bounds__(kHeadThreads) heads_loss_kernel(HeadsParams p)
   }
 }
 
-int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
-  const bool shared = p.f_v == p.f_pi;
-  const size_t smem = heads_smem_bytes(p.F_pi, p.F_v, p.A, shared);
-  BT_CHECK_ARG(p.A <= 64, "heads: action_dim %d > 64 is not supported", p.A);
-  BT_CHECK_ARG(p.F_pi % 4 == 0 && p.F_v % 4 == 0 && p.F_pi <= 4 * 32 * kMaxChunks &&
-                   p.F_v <= 4 * 32 * kMaxChunks,
-               "heads: feature widths %d / %d must be multiples of 4 and at most %d", p.F_pi,
-               p.F_v, 4 * 32 * kMaxChunks);
-  BT_CHECK_ARG(smem <= 227 * 1024, "heads: feature width too large for shared memory");
-  if (smem > 48 * 1024) {
-    static size_t configured = 0;
-    if (smem > configured) {
-      BT_CUDA(cudaFuncSetAttribute(heads_loss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
-      configured = smem;
-    }
+template <int JP, bool FUSE, int ACT>
+int launch_heads_inst(const HeadsParams& p, int blocks, size_t smem, cudaStream_t stream) {
+  auto kernel = heads_loss_kernel<JP, FUSE, ACT>;
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    BT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured = smem;
   }
-  heads_loss_kernel<<<blocks, kHeadThreads, smem, stream>>>(p);
+  kernel<<<blocks, kHeadThreads, smem, stream>>>(p);
   BT_LAUNCH_CHECK("heads_loss_kernel");
   return BT_OK;
+}
+
+// The activation of the towers' last layers is a template parameter (one instance per
+// activation keeps each kernel's code small); both towers must end in the same one.
+template <int JP, bool FUSE>
+int launch_heads_jp(const HeadsParams& p, int blocks, size_t smem, cudaStream_t stream) {
+  switch (p.act_pi) {
+    case BT_ACT_TANH: return launch_heads_inst<JP, FUSE, BT_ACT_TANH>(p, blocks, smem, stream);
+    case BT_ACT_RELU: return launch_heads_inst<JP, FUSE, BT_ACT_RELU>(p, blocks, smem, stream);
+    case BT_ACT_SILU: return launch_heads_inst<JP, FUSE, BT_ACT_SILU>(p, blocks, smem, stream);
+    default: return launch_heads_inst<JP, FUSE, BT_ACT_NONE>(p, blocks, smem, stream);
+  }
+}
+
+int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
+  const bool shared = p.f_v == p.f_pi;
+  const bool fuse = p.dw_pi_partials != nullptr;
+  const size_t smem = heads_smem_for(p.F_pi, p.F_v, p.A, shared, fuse);
+  BT_CHECK_ARG(p.A >= 1 && p.A <= 63, "heads: action_dim %d outside [1, 63]", p.A);
+  BT_CHECK_ARG(p.F_pi % 4 == 0 && p.F_v % 4 == 0, "heads: feature widths %d / %d must be "
+               "multiples of 4", p.F_pi, p.F_v);
+  BT_CHECK_ARG(shared || p.act_pi == p.act_v, "heads: actor and critic towers must end in the "
+               "same activation (%d / %d)", p.act_pi, p.act_v);
+  BT_CHECK_ARG(smem <= 227 * 1024, "heads: feature width too large for shared memory");
+  const int jp = heads_inst_jp(p.A, fuse);  // the instance below; its layout uses this JP
+  if (fuse) {
+    BT_CHECK_ARG(heads_fuse_dw(p.F_pi, p.F_v, p.A, shared) && p.dw_v_partials,
+                 "heads: fused head weight gradient needs A + 1 <= 16 and widths <= %d",
+                 kHeadThreads);
+    if (jp <= 4) return launch_heads_jp<4, true>(p, blocks, smem, stream);
+    if (jp <= 8) return launch_heads_jp<8, true>(p, blocks, smem, stream);
+    if (jp <= 12) return launch_heads_jp<12, true>(p, blocks, smem, stream);
+    return launch_heads_jp<16, true>(p, blocks, smem, stream);
+  }
+  if (jp <= 16) return launch_heads_jp<16, false>(p, blocks, smem, stream);
+  if (jp <= 32) return launch_heads_jp<32, false>(p, blocks, smem, stream);
+  if (jp <= 48) return launch_heads_jp<48, false>(p, blocks, smem, stream);
+  return launch_heads_jp<64, false>(p, blocks, smem, stream);
 }
 
 // Head outputs only (bootstrap values, act): one warp per row; the head input is act(f).

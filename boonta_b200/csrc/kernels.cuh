@@ -46,10 +46,16 @@ struct HeadsParams {
   int act_v;
   double* stat_partials;   // [gridDim.x][kNumStatSums]
   float* dscale_partials;  // [gridDim.x][A] (gaussian)
+  // nullable: fused head weight gradients, per block [gridDim.x][(F_pi + 1) * A] and
+  // [gridDim.x][F_v + 1] (allowed when heads_fuse_dw holds)
+  float* dw_pi_partials;
+  float* dw_v_partials;
 };
 
 int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream);
 size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared);
+// Whether the heads kernel can accumulate the head weight gradients itself (small heads).
+bool heads_fuse_dw(int F_pi, int F_v, int A, bool shared);
 int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
                          const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
                          float* value, cudaStream_t stream);
@@ -77,6 +83,27 @@ __device__ __forceinline__ void store_bf16(__nv_bfloat16* hi, __nv_bfloat16* lo,
   const __nv_bfloat16 h = __float2bfloat16_rn(x);
   hi[i] = h;
   if (lo) lo[i] = __float2bfloat16_rn(x - __bfloat162float(h));
+}
+// Four consecutive values (index i a multiple of 4, 8-byte aligned) as bf16, hi and (when
+// `lo` is set) the remainders, with paired conversions and 8-byte stores.
+__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i,
+                                             float4 g) {
+  const __nv_bfloat162 h01 = __floats2bfloat162_rn(g.x, g.y);
+  const __nv_bfloat162 h23 = __floats2bfloat162_rn(g.z, g.w);
+  uint2 hv;
+  hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+  hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+  *reinterpret_cast<uint2*>(hi + i) = hv;
+  if (lo) {
+    const __nv_bfloat162 l01 =
+        __floats2bfloat162_rn(g.x - __low2float(h01), g.y - __high2float(h01));
+    const __nv_bfloat162 l23 =
+        __floats2bfloat162_rn(g.z - __low2float(h23), g.w - __high2float(h23));
+    uint2 lv;
+    lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+    lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+    *reinterpret_cast<uint2*>(lo + i) = lv;
+  }
 }
 int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
                        __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,

@@ -288,20 +288,31 @@ int allocate(bt_learner* L) {
   const int A = L->A;
   BT_TRY(dalloc(L, &L->d_out, (size_t)R * A));
   BT_TRY(dalloc(L, &L->d_val, R));
-  // skinny head dW: up to 8 blocks of 128 threads per SM (enough loads in flight), at
-  // least 128 rows per split (fewer partials for the reduction to read)
-  L->head_pi_splits = std::max(1, std::min(ceil_div(L->rows_cap, 128),
-                                           8 * kNumSMs / ceil_div(L->F_pi + 1, 128)));
-  L->head_v_splits = std::max(1, std::min(ceil_div(L->rows_cap, 128),
-                                          8 * kNumSMs / ceil_div(L->F_v + 1, 128)));
+  // heads kernel: tiles of 32 rows, up to two blocks per SM (shared memory allowing), the
+  // tiles spread evenly over the blocks
+  {
+    const size_t hs = heads_smem_bytes(L->F_pi, L->F_v, A, L->shared);
+    const int per_sm = std::max<int>(1, std::min<int>(2, (int)((226 * 1024) / (hs + 1024))));
+    const int tiles = ceil_div(L->rows_cap, 32);
+    const int rounds = ceil_div(tiles, kNumSMs * per_sm);
+    L->heads_blocks = ceil_div(tiles, rounds);
+  }
+  L->heads_fused_dw = heads_fuse_dw(L->F_pi, L->F_v, A, L->shared);
+  if (L->heads_fused_dw) {
+    // the heads kernel accumulates the head weight gradients, one partial per block
+    L->head_pi_splits = L->head_v_splits = L->heads_blocks;
+  } else {
+    // skinny head dW: up to 8 blocks of 128 threads per SM (enough loads in flight), at
+    // least 128 rows per split (fewer partials for the reduction to read)
+    L->head_pi_splits = std::max(1, std::min(ceil_div(L->rows_cap, 128),
+                                             8 * kNumSMs / ceil_div(L->F_pi + 1, 128)));
+    L->head_v_splits = std::max(1, std::min(ceil_div(L->rows_cap, 128),
+                                            8 * kNumSMs / ceil_div(L->F_v + 1, 128)));
+  }
   BT_TRY(dalloc(L, &L->head_pi_part, (size_t)L->head_pi_splits * (L->F_pi + 1) * A));
   BT_TRY(dalloc(L, &L->head_v_part, (size_t)L->head_v_splits * (L->F_v + 1)));
   L->segs_h.push_back({L->head_pi_part, L->head_pi_splits, (L->F_pi + 1) * A,
                        (int64_t)(L->F_pi + 1) * A, L->head_pi_off});
-  {
-    const size_t hs = heads_smem_bytes(L->F_pi, L->F_v, A, L->shared);
-    L->heads_blocks = kNumSMs * std::max<int>(1, std::min<int>(4, (int)((200 * 1024) / hs)));
-  }
   BT_TRY(dalloc(L, &L->stat_part, (size_t)L->heads_blocks * kNumStatSums));
   if (c.network.head == BT_HEAD_GAUSSIAN) {
     BT_TRY(dalloc(L, &L->dscale_part, (size_t)L->heads_blocks * A));
@@ -636,17 +647,24 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   hp.act_v = last_v.act;
   hp.stat_partials = L->stat_part;
   hp.dscale_partials = L->dscale_part;
+  if (L->heads_fused_dw) {
+    hp.dw_pi_partials = L->head_pi_part;
+    hp.dw_v_partials = L->head_v_part;
+  }
   BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
   BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
-  // head weight gradients: [F + 1, A] = [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value,
-  // on a side stream next to the towers' backward
+  // head weight gradients when not fused: [F + 1, A] = [f, 1]^T d_out and
+  // [F + 1, 1] = [f, 1]^T d_value, on a side stream next to the towers' backward
   cudaStream_t sh = side_stream(L, 3, s);
   BT_TRY(stream_dep(L, s, sh));
-  BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out, L->A,
-                                            rows, in.count, L->head_pi_splits, L->head_pi_part,
-                                            sh));
-  BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_v.pre(), L->F_v, last_v.act, L->d_val, 1, rows,
-                                            in.count, L->head_v_splits, L->head_v_part, sh));
+  if (!L->heads_fused_dw) {
+    BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out,
+                                              L->A, rows, in.count, L->head_pi_splits,
+                                              L->head_pi_part, sh));
+    BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_v.pre(), L->F_v, last_v.act, L->d_val, 1,
+                                              rows, in.count, L->head_v_splits,
+                                              L->head_v_part, sh));
+  }
   if (in.count) {
     // padded minibatch (multi-GPU): the tensor-core dW GEMMs read whole 64-row blocks, so the
     // dz rows past the live count must be zero

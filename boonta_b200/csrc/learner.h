@@ -153,6 +153,7 @@ struct bt_learner {
   float* dscale_part = nullptr;
   double* stat_part = nullptr;
   int heads_blocks = 0;
+  bool heads_fused_dw = false;  // the heads kernel writes the head weight-gradient partials
   // targets
   float* adv = nullptr;
   float* ret = nullptr;

@@ -268,13 +268,19 @@ int recurrent_heads(bt_learner* L, LayerPlan& g, const MinibatchInputs& in, cons
   hp.act_v = BT_ACT_NONE;
   hp.stat_partials = L->stat_part;
   hp.dscale_partials = L->dscale_part;
+  if (L->heads_fused_dw) {
+    hp.dw_pi_partials = L->head_pi_part;
+    hp.dw_v_partials = L->head_v_part;
+  }
   BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
   BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
-  BT_K(L, kProfHeadDw, s, launch_skinny_dw(g.h, L->F_pi, BT_ACT_NONE, L->d_out, L->A,
-                                           L->rows_cap, rows_live, L->head_pi_splits,
-                                           L->head_pi_part, s));
-  BT_K(L, kProfHeadDw, s, launch_skinny_dw(g.h, L->F_v, BT_ACT_NONE, L->d_val, 1, L->rows_cap,
-                                           rows_live, L->head_v_splits, L->head_v_part, s));
+  if (!L->heads_fused_dw) {
+    BT_K(L, kProfHeadDw, s, launch_skinny_dw(g.h, L->F_pi, BT_ACT_NONE, L->d_out, L->A,
+                                             L->rows_cap, rows_live, L->head_pi_splits,
+                                             L->head_pi_part, s));
+    BT_K(L, kProfHeadDw, s, launch_skinny_dw(g.h, L->F_v, BT_ACT_NONE, L->d_val, 1, L->rows_cap,
+                                             rows_live, L->head_v_splits, L->head_v_part, s));
+  }
   return BT_OK;
 }
 
