@@ -183,6 +183,15 @@ def device_rollout(w, seed: int, device):
     r["terminated"] = (torch.rand((t, n), generator=g, device=device) < w.done_p).to(torch.uint8)
     r["truncated"] = torch.zeros((t, n), dtype=torch.uint8, device=device)
     r["value"] = torch.randn((t, n), generator=g, device=device)
+    if w.network.recurrent:
+        # first.done (reset before step t), the carry entering step 0 and step T-1
+        h = w.network.torso[-1].features
+        fd = torch.zeros((t, n), dtype=torch.uint8, device=device)
+        fd[0] = (torch.rand(n, generator=g, device=device) < w.done_p).to(torch.uint8)
+        fd[1:] = r["terminated"][:-1] | r["truncated"][:-1]
+        r["first_done"] = fd
+        r["carry"] = w.hidden_std * torch.randn((n, h), generator=g, device=device)
+        r["last_carry"] = w.hidden_std * torch.randn((n, h), generator=g, device=device)
     return {k: v.contiguous() for k, v in r.items()}
 
 
@@ -191,7 +200,8 @@ def device_perms(w, world: int, count: int, seed: int, device):
 
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    size = w.batch_size * world
+    # recurrent networks permute environments (env-minibatches), the others samples
+    size = (w.num_envs if w.network.recurrent else w.batch_size) * world
     return [torch.stack([torch.randperm(size, generator=g, device=device, dtype=torch.int32)
                          for _ in range(w.ppo.update_epochs)]) for _ in range(count)]
 
@@ -251,6 +261,10 @@ class ClockSampler:
 def cpu_baseline(w, budget_s: float = 15.0) -> dict:
     from oracle import optim
     from oracle import ppo as oppo
+    from oracle import recurrent as orec
+
+    # the recurrent learner step (env-minibatches, GRU) for recurrent networks
+    step = orec.update if w.network.recurrent else oppo.update
 
     threads = len(os.sched_getaffinity(0))
     rng_w = w
@@ -262,16 +276,16 @@ def cpu_baseline(w, budget_s: float = 15.0) -> dict:
     perms = configs.permutations(rng_w)
     # GAE + bootstrap alone
     t0 = time.perf_counter()
-    oppo.update(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
-                max_minibatches=0)
+    step(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
+         max_minibatches=0)
     t_gae = time.perf_counter() - t0
     # minibatch steps until the budget is used (at least one)
     mb_ratio = w.minibatch_size / rng_w.minibatch_size
     done, t_mb = 0, 0.0
     while done < w.ppo.update_epochs * w.ppo.num_minibatches:
         t0 = time.perf_counter()
-        oppo.update(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
-                    max_minibatches=done + 1)
+        step(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
+             max_minibatches=done + 1)
         t_mb = time.perf_counter() - t0 - t_gae
         done += 1
         if t_mb * 1 > budget_s / 4 or t_mb > budget_s / (done + 1):

@@ -7,8 +7,6 @@
 //   ARows     A(m, k) = src[row(m) * ld + k]           activations, or obs rows gathered
 //                                                     through the minibatch indices
 //   ACols     A(m, k) = src[row(k) * ld + m]           transposed activations (dW GEMMs)
-//   AIm2col   3x3 SAME patches of an NHWC image       (conv forward)
-//   AIm2colT  transposed patches                      (conv dW)
 //   BRows     B(k, n) = src[k * ld + n]                kernel [K+1, N] (bias row last)
 //   BCols     B(k, n) = src[n * ld + k]                kernel^T (dX GEMMs)
 // A "ones" column (forward) or row (dW) at index K_in makes the bias part of the GEMM:
@@ -53,37 +51,6 @@ struct ACols {  // m contiguous: A(m, k) = src[row(k) * ld + m]
       return src[(size_t)r * ld + m];
     }
     return m == kin ? 1.f : 0.f;
-  }
-};
-
-// Conv 3x3 SAME, stride 1, NHWC rows of H*W*C floats: m = row * H*W + pixel,
-// k = (dy * 3 + dx) * C + c; k == 9C is the bias column.
-struct AIm2col {
-  static constexpr bool kMContig = false;
-  const float* src;
-  const int* idx;
-  int H, W, C;
-  __device__ __forceinline__ float load(int m, int k, int M, int /*K*/) const {
-    if (m >= M) return 0.f;
-    const int kin = 9 * C;
-    if (k >= kin) return k == kin ? 1.f : 0.f;
-    const int hw = H * W;
-    const int row = m / hw, pix = m - row * hw;
-    const int y = pix / W, x = pix - y * W;
-    const int tap = k / C, c = k - tap * C;
-    const int yy = y + tap / 3 - 1, xx = x + tap % 3 - 1;
-    if (yy < 0 || yy >= H || xx < 0 || xx >= W) return 0.f;
-    const int r = idx ? idx[row] : row;
-    return src[(size_t)r * hw * C + (yy * W + xx) * C + c];
-  }
-};
-
-struct AIm2colT {  // A(m, k) = patch value with m the (tap, c) index and k the pixel row
-  static constexpr bool kMContig = false;
-  AIm2col inner;
-  __device__ __forceinline__ float load(int m, int k, int M, int K) const {
-    if (k >= K || m >= M) return 0.f;
-    return inner.load(k, m, K, M);
   }
 };
 

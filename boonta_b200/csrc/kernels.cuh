@@ -60,6 +60,15 @@ int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, con
                          const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
                          float* value, cudaStream_t stream);
 
+// Conv 3x3 SAME stride 1 on NHWC rows (conv.cu): forward z = conv + bias, h = act(z)
+// ([rows, H*W*Cout]); weight gradient as per-block partials [blocks][(9C + 1) * Cout].
+int launch_conv_forward(const float* obs, const int* idx, int rows, const int* count, int H,
+                        int W, int C, int Cout, const float* w, int act, float* z, float* h,
+                        __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb, cudaStream_t s);
+int launch_conv_dw(const float* obs, const int* idx, int rows, const int* count, int H, int W,
+                   int C, int Cout, const float* dz, int blocks, float* out, cudaStream_t s);
+int conv_dw_blocks(int rows);
+
 // LayerNorm (flax, epsilon 1e-6, fast variance) fused with the following activation.
 int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act,
                       float* y, float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb,

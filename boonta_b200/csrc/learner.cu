@@ -102,9 +102,10 @@ int build_layout(bt_learner* L) {
       lp.kind = l.kind;
       lp.act = l.activation;
       lp.ln = l.layernorm ? 1 : 0;
+      // Dense layers take the precision's tensor-core path; a Conv3x3 (always the first
+      // layer) stays on its fp32 kernels and hands bf16 operands to the tensor-core layer
+      // after it.
       lp.tc = L->cfg.precision != BT_PREC_FP32 && l.kind == BT_LAYER_DENSE;
-      BT_CHECK_ARG(!(L->cfg.precision != BT_PREC_FP32 && l.kind == BT_LAYER_CONV3X3),
-                   "Conv3x3 layers run in fp32 only (precision %d requested)", L->cfg.precision);
       std::string p = std::string(names[t]) + "/" + std::to_string(i);
       if (l.kind == BT_LAYER_GRU) {
         const int H = l.features;
@@ -261,7 +262,7 @@ int allocate(bt_learner* L) {
       }
       // dW GEMM: [kin + 1, ncol] over K = rows (dense) or rows * H*W (conv)
       const int dm = lp.kin + 1, dn = lp.ncol;
-      const int dk = lp.kind == BT_LAYER_CONV3X3 ? L->rows_cap * lp.H * lp.W : L->rows_cap;
+      const int dk = L->rows_cap;
       if (lp.tc) {
         // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1]. These GEMMs run on a side
         // stream next to the dX chain, so they need not fill the GPU: at most one wave of
@@ -273,6 +274,8 @@ int allocate(bt_learner* L) {
         int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 32));
         lp.dw_kbps = ceil_div(nkb, splits);
         lp.dw_splits = ceil_div(nkb, lp.dw_kbps);
+      } else if (lp.kind == BT_LAYER_CONV3X3) {
+        lp.dw_splits = conv_dw_blocks(L->rows_cap);  // one partial per conv dW block
       } else {
         lp.dw_splits = pick_splits(dm, dn, dk);
       }
@@ -349,9 +352,11 @@ int allocate(bt_learner* L) {
 
 // ---- tensor-core (bf16) operand buffers and TMA tensor maps -------------------------------
 int allocate_tensor_core(bt_learner* L) {
-  L->tc_any = false;
-  for (int t = 0; t < L->ntowers; ++t)
+  L->tc_any = L->tc_first = false;
+  for (int t = 0; t < L->ntowers; ++t) {
     for (LayerPlan& lp : L->towers[t].layers) L->tc_any |= lp.tc;
+    L->tc_first |= !L->towers[t].layers.empty() && L->towers[t].layers[0].tc;
+  }
   if (!L->tc_any) return BT_OK;
   L->x3 = L->cfg.precision == BT_PREC_BF16X3;
   const int R = L->act_rows;
@@ -383,10 +388,24 @@ int allocate_tensor_core(bt_learner* L) {
         lp.xin_lo = L->xg_lo;
         lp.ldx = L->ldx0;
       } else {
-        BT_CHECK_ARG(layers[i - 1].tc, "a tensor-core layer must follow a tensor-core layer");
-        lp.xin_b = layers[i - 1].hb;
-        lp.xin_lo = layers[i - 1].hb_lo;
-        lp.ldx = layers[i - 1].ldh;
+        LayerPlan& prev = layers[i - 1];
+        BT_CHECK_ARG(prev.tc || prev.kind == BT_LAYER_CONV3X3,
+                     "a tensor-core layer must follow a tensor-core or Conv3x3 layer");
+        if (!prev.tc) {
+          // the conv writes its output as the bf16 operand of this layer, and this layer's
+          // dX epilogue writes the conv's dL/dz in fp32 (maps for both)
+          prev.out_b = true;
+          prev.ldh = ru8(prev.kout + 1);
+          BT_TRY(pair(&prev.hb, &prev.hb_lo, (size_t)R * prev.ldh));
+          BT_TRY(launch_ones_column(prev.hb, R, prev.kout, prev.ldh, 1.f, 0));
+          const uint64_t f32_ld = (uint64_t)prev.kout * 4;
+          BT_TRY(umma::encode_tile_map(&prev.map_pre, prev.pre(), true, prev.kout, R, f32_ld, 128));
+          BT_TRY(umma::encode_tile_map(&prev.map_dpre, prev.d_pre, true, prev.kout, R, f32_ld,
+                                       128));
+        }
+        lp.xin_b = prev.hb;
+        lp.xin_lo = prev.hb_lo;
+        lp.ldx = prev.ldh;
       }
       const int mtiles = ceil_div(L->rows_cap, umma::BM);
       lp.fwd_bn = (!L->x3 && lp.kout % 256 == 0 && mtiles * (lp.kout / 256) >= kNumSMs) ? 256 : 128;
@@ -446,7 +465,7 @@ int allocate_tensor_core(bt_learner* L) {
 // minibatch gathered into L->xg (gather_obs).
 int gather_obs(bt_learner* L, const float* obs, const int* idx, int rows, const int* count,
                cudaStream_t s) {
-  if (!L->tc_any) return BT_OK;
+  if (!L->tc_first) return BT_OK;
   BT_K(L, kProfMisc, s, launch_gather_bf16(obs, idx, rows, L->cfg.network.obs_dim, L->ldx0, L->xg,
                                            L->xg_lo, count, s));
   return BT_OK;
@@ -490,11 +509,11 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
                                                  lp.rstd, count, s));
       }
     } else if (lp.kind == BT_LAYER_CONV3X3) {
-      AIm2col a{in, gather, lp.H, lp.W, lp.C};
-      BRows b{w, lp.ncol, lp.kin + 1};
-      EpiForward ep{lp.z, lp.h, lp.ncol, lp.act};
-      BT_K(L, kProfGemmFwd, s, launch_gemm_simt(a, b, ep, rows * lp.H * lp.W, lp.ncol, lp.kin + 1, 1, s, count,
-                              nullptr, lp.H * lp.W));
+      BT_K(L, kProfGemmFwd, s, launch_conv_forward(in, gather, rows, count, lp.H, lp.W, lp.C,
+                                                   lp.ncol, w, lp.act, lp.z,
+                                                   lp.out_b ? nullptr : lp.h,
+                                                   lp.out_b ? lp.hb : nullptr, lp.hb_lo,
+                                                   lp.ldh, s));
     } else {
       ARows a{in, gather, in_ld, lp.kin};
       BRows b{w, lp.ncol, lp.kin + 1};
@@ -556,9 +575,10 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
         epx.hi_map = prev.map_dzb;
         epx.lo_map = prev.map_dzb_lo;
         epx.act = prev.act;
-        epx.has_f32 = prev.ln;
-        epx.has_hi = !prev.ln;
-        epx.has_lo = !prev.ln && L->x3;
+        // fp32 dL/dz for a LayerNorm or non-tensor-core (conv) previous layer
+        epx.has_f32 = prev.ln || !prev.tc;
+        epx.has_hi = !epx.has_f32;
+        epx.has_lo = epx.has_hi && L->x3;
         if (L->x3) {
           BT_K(L, kProfGemmDx, s, umma::launch_gemm<64, false, false, true>(lp.dx_ops, shx, epx, 1, s));
         } else {
@@ -569,11 +589,8 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
     }
     EpiPartial ep{lp.dw_part, dn, (size_t)dm * dn};
     if (lp.kind == BT_LAYER_CONV3X3) {
-      AIm2colT a{AIm2col{obs, idx, lp.H, lp.W, lp.C}};
-      const int K = rows * lp.H * lp.W;
-      BRows b{lp.d_z, lp.ncol, K};
-      BT_K(L, kProfGemmDw, sw, launch_gemm_simt(a, b, ep, dm, dn, K, lp.dw_splits, sw, nullptr, count,
-                              lp.H * lp.W));
+      BT_K(L, kProfGemmDw, sw, launch_conv_dw(obs, idx, rows, count, lp.H, lp.W, lp.C, lp.ncol,
+                                              lp.d_z, lp.dw_splits, lp.dw_part, sw));
     } else {
       const float* in = i == 0 ? obs : tp.layers[i - 1].h;
       const int* gather = i == 0 ? idx : nullptr;

@@ -37,6 +37,7 @@ struct LayerPlan {
   int ln_blocks = 0;
   // tensor-core (bf16) path
   bool tc = false;
+  bool out_b = false;  // (conv) also writes its output as the bf16 operand hb/hb_lo
   __nv_bfloat16* xin_b = nullptr;  // bf16 input operand [rows, ldx], ones column at kin
   int ldx = 0;
   __nv_bfloat16* hb = nullptr;  // bf16 output [rows, ldh], ones column at kout
@@ -117,6 +118,7 @@ struct bt_learner {
   int* mb_count_d = nullptr;  // live rows for bt_learner_loss_grads
   // tensor-core path
   bool tc_any = false;
+  bool tc_first = false;  // some tower starts with a tensor-core layer (reads L->xg)
   bool x3 = false;                    // split-bf16 (BT_PREC_BF16X3) operands
   __nv_bfloat16* params_b = nullptr;  // bf16 shadow of params (written by every Adam step)
   __nv_bfloat16* params_b_lo = nullptr;

@@ -47,13 +47,16 @@ def small(name: str, t: int, n: int, epochs: int, minibatches: int, **kw):
 CASES = {
     "c1": lambda: configs.c1(),  # full size: CPU-runnable reference case
     "c2": lambda: small("c2", 8, 256, 2, 4, precision="fp32"),
-    "c3": lambda: small("c3", 4, 64, 2, 2),
+    "c3": lambda: small("c3", 4, 64, 2, 2, precision="fp32"),
     "c5": lambda: small("c5", 4, 64, 2, 2, precision="fp32"),
     # bf16 tensor-core GEMMs, checked against the oracle's bf16-operand arithmetic
     "c2_bf16": lambda: small("c2", 8, 256, 2, 4, precision="bf16"),
     "c5_bf16": lambda: small("c5", 4, 128, 2, 2, precision="bf16"),
     # split-bf16 tensor-core GEMMs, checked against the plain fp32 oracle
     "c2_bf16x3": lambda: small("c2", 8, 256, 2, 4, precision="bf16x3"),
+    # fp32 conv kernels handing bf16 operands to a tensor-core dense layer
+    "c3_bf16x3": lambda: small("c3", 4, 64, 2, 2, precision="bf16x3"),
+    "c3_bf16": lambda: small("c3", 4, 64, 2, 2, precision="bf16"),
 }
 
 
