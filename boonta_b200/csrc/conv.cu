@@ -7,13 +7,14 @@
 // a zero halo (kConvRows images per step, [image][channel][(H + 2) * (W + 2)]), so every
 // patch value is a plain shared-memory read and a warp reading one tap of consecutive
 // pixels touches consecutive words:
-//   forward: one thread per output pixel computes all NC output channels (the weights
-//            [9C + 1][NC] are broadcast float4 reads), z and h stored as float4s;
-//   dW:      lane k of a warp pair owns patch element k (k = (dy * 3 + dx) * C + ci, and
-//            k = 9C the bias "1"), accumulating sum_pixels patch[k] * dz[c] for all NC
-//            channels in registers; the four warp pairs take interleaved images and are
-//            added in order at the end, one [9C + 1][Cout] partial per block (reduced by
-//            the split-K reduction in a fixed order).
+//   forward: one thread per output pixel and group of images computes all NC output
+//            channels of that pixel in those images (the weights [9C + 1][NC] are
+//            broadcast float4 reads), z and h stored as float4s;
+//   dW:      thread t owns patch element k = t % (9C + 1) (k = (dy * 3 + dx) * C + ci,
+//            and k = 9C the bias "1") in image phase t / (9C + 1), accumulating
+//            sum_pixels patch[k] * dz[c] for all NC channels in registers; the phases
+//            (interleaved images) are added in order at the end, one [9C + 1][Cout]
+//            partial per block (reduced by the split-K reduction in a fixed order).
 // Weight layout: the [9C + 1, Cout] kernel+bias block of the flat parameters (row k as
 // above, bias row last), as flax's HWIO kernel flattened.
 #include "common.cuh"
@@ -50,14 +51,19 @@ __device__ __forceinline__ void stage_images(const float* obs, const int* idx, i
   }
 }
 
+// Forward: thread (pixel p, image group) computes all NC channels of pixel p for IPT
+// images of the staged step at once, so each weight row read (broadcast float4s) feeds
+// IPT x NC FMAs.
 template <int NC, int ACT>
 __global__ void __launch_bounds__(kConvThreads) conv_forward_kernel(
     const float* obs, const int* idx, int rows, const int* count, ConvGeom g, const float* w,
     float* z, float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb) {
+  constexpr int IPT = NC <= 16 ? 4 : 2;  // images per thread
+  constexpr int kGroups = kConvRows / IPT;
   extern __shared__ __align__(16) float sm[];
   float* x_s = sm;
   float* w_s = x_s + kConvRows * g.img();  // [9C + 1][NC], channels past Cout zero
-  const int kin = 9 * g.C, hw = g.hw(), wp = g.W + 2;
+  const int kin = 9 * g.C, hw = g.hw(), wp = g.W + 2, plane = (g.H + 2) * wp;
   for (int i = threadIdx.x; i < (kin + 1) * NC; i += kConvThreads) {
     const int k = i / NC, c = i - k * NC;
     w_s[i] = c < g.Cout ? w[(size_t)k * g.Cout + c] : 0.f;
@@ -68,16 +74,18 @@ __global__ void __launch_bounds__(kConvThreads) conv_forward_kernel(
   for (int r0 = blockIdx.x * kConvRows; r0 < live; r0 += gridDim.x * kConvRows) {
     stage_images(obs, idx, r0, live, g, x_s);
     __syncthreads();
-    for (int t = threadIdx.x; t < kConvRows * hw; t += kConvThreads) {
-      const int rr = t / hw, pix = t - rr * hw;
-      const int row = r0 + rr;
-      if (row >= live) continue;
+    for (int task = threadIdx.x; task < kGroups * hw; task += kConvThreads) {
+      const int grp = task / hw, pix = task - grp * hw;
       const int y = pix / g.W, x = pix - y * g.W;
-      float acc[NC];
+      const int i0 = grp * IPT;
+      float acc[IPT][NC];
 #pragma unroll
-      for (int c = 0; c < NC; ++c) acc[c] = w_s[kin * NC + c];
-      const float* xb = x_s + rr * g.img() + y * wp + x;
-      const int plane = (g.H + 2) * wp;
+      for (int c = 0; c < NC; ++c) {
+        const float b = w_s[kin * NC + c];
+#pragma unroll
+        for (int m = 0; m < IPT; ++m) acc[m][c] = b;
+      }
+      const float* xb = x_s + i0 * g.img() + y * wp + x;
 #pragma unroll
       for (int dy = 0; dy < 3; ++dy)
 #pragma unroll
@@ -85,37 +93,48 @@ __global__ void __launch_bounds__(kConvThreads) conv_forward_kernel(
           const float* xp = xb + dy * wp + dx;
           const float* wr = w_s + ((dy * 3 + dx) * g.C) * NC;
           for (int ci = 0; ci < g.C; ++ci) {
-            const float v = xp[ci * plane];
+            float v[IPT];
+#pragma unroll
+            for (int m = 0; m < IPT; ++m) v[m] = xp[m * g.img() + ci * plane];
 #pragma unroll
             for (int c = 0; c < NC; c += 4) {
               const float4 ww = *reinterpret_cast<const float4*>(wr + ci * NC + c);
-              acc[c] = fmaf(v, ww.x, acc[c]);
-              acc[c + 1] = fmaf(v, ww.y, acc[c + 1]);
-              acc[c + 2] = fmaf(v, ww.z, acc[c + 2]);
-              acc[c + 3] = fmaf(v, ww.w, acc[c + 3]);
+#pragma unroll
+              for (int m = 0; m < IPT; ++m) {
+                acc[m][c] = fmaf(v[m], ww.x, acc[m][c]);
+                acc[m][c + 1] = fmaf(v[m], ww.y, acc[m][c + 1]);
+                acc[m][c + 2] = fmaf(v[m], ww.z, acc[m][c + 2]);
+                acc[m][c + 3] = fmaf(v[m], ww.w, acc[m][c + 3]);
+              }
             }
           }
         }
-      const size_t o = ((size_t)row * hw + pix) * g.Cout;
-      if (g.Cout == NC) {
 #pragma unroll
-        for (int c = 0; c < NC; c += 4) {
-          *reinterpret_cast<float4*>(z + o + c) =
-              make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
-          const float4 hv = make_float4(act_fwd<ACT>(acc[c]), act_fwd<ACT>(acc[c + 1]),
-                                        act_fwd<ACT>(acc[c + 2]), act_fwd<ACT>(acc[c + 3]));
-          if (h) *reinterpret_cast<float4*>(h + o + c) = hv;
-          if (hb) store_bf16x4(hb, hb_lo, (size_t)row * ldhb + (size_t)pix * g.Cout + c, hv);
-        }
-      } else {
+      for (int m = 0; m < IPT; ++m) {
+        const int row = r0 + i0 + m;
+        if (row >= live) break;
+        const size_t o = ((size_t)row * hw + pix) * g.Cout;
+        if (g.Cout == NC) {
 #pragma unroll
-        for (int c = 0; c < NC; ++c)
-          if (c < g.Cout) {
-            z[o + c] = acc[c];
-            const float hv = act_fwd<ACT>(acc[c]);
-            if (h) h[o + c] = hv;
-            if (hb) store_bf16(hb, hb_lo, (size_t)row * ldhb + (size_t)pix * g.Cout + c, hv);
+          for (int c = 0; c < NC; c += 4) {
+            *reinterpret_cast<float4*>(z + o + c) =
+                make_float4(acc[m][c], acc[m][c + 1], acc[m][c + 2], acc[m][c + 3]);
+            const float4 hv =
+                make_float4(act_fwd<ACT>(acc[m][c]), act_fwd<ACT>(acc[m][c + 1]),
+                            act_fwd<ACT>(acc[m][c + 2]), act_fwd<ACT>(acc[m][c + 3]));
+            if (h) *reinterpret_cast<float4*>(h + o + c) = hv;
+            if (hb) store_bf16x4(hb, hb_lo, (size_t)row * ldhb + (size_t)pix * g.Cout + c, hv);
           }
+        } else {
+#pragma unroll
+          for (int c = 0; c < NC; ++c)
+            if (c < g.Cout) {
+              z[o + c] = acc[m][c];
+              const float hv = act_fwd<ACT>(acc[m][c]);
+              if (h) h[o + c] = hv;
+              if (hb) store_bf16(hb, hb_lo, (size_t)row * ldhb + (size_t)pix * g.Cout + c, hv);
+            }
+        }
       }
     }
     __syncthreads();
@@ -130,12 +149,11 @@ __global__ void __launch_bounds__(kConvThreads) conv_dw_kernel(
   float* x_s = sm;
   float* dz_s = x_s + kConvRows * g.img();  // [kConvRows * hw][NC]
   const int kin = 9 * g.C, hw = g.hw(), wp = g.W + 2;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkw = (kin + 1 + 31) / 32;                  // warps covering the patch elements
-  const int groups = (kConvThreads / 32) / nkw;         // pixel phases
-  const int kslot = (warp % nkw) * 32 + lane;
-  const int phase = warp / nkw;
-  const bool active = phase < groups && kslot <= kin;
+  // thread t: patch element kslot = t % (9C + 1) in image phase t / (9C + 1)
+  const int groups = kConvThreads / (kin + 1);  // image phases
+  const int kslot = threadIdx.x % (kin + 1);
+  const int phase = threadIdx.x / (kin + 1);
+  const bool active = phase < groups;
   int koff = 0;  // offset of patch element kslot relative to the pixel's top-left tap
   if (kslot < kin) {
     const int tap = kslot / g.C, ci = kslot - tap * g.C;
@@ -186,19 +204,19 @@ __global__ void __launch_bounds__(kConvThreads) conv_dw_kernel(
     __syncthreads();
   }
   // phases added in order: phase p's sums to shared memory, then phase 0's threads
-  float* red = sm;  // [groups][nkw * 32][NC] (reuses the image buffers)
-  if (phase < groups) {
+  float* red = sm;  // [groups][9C + 1][NC] (reuses the image buffers)
+  if (active) {
 #pragma unroll
-    for (int c = 0; c < NC; ++c) red[((size_t)phase * nkw * 32 + kslot) * NC + c] = acc[c];
+    for (int c = 0; c < NC; ++c) red[((size_t)phase * (kin + 1) + kslot) * NC + c] = acc[c];
   }
   __syncthreads();
-  if (phase == 0 && kslot <= kin) {
+  if (phase == 0) {
     float* o = out + (size_t)blockIdx.x * (kin + 1) * g.Cout + (size_t)kslot * g.Cout;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       if (c >= g.Cout) break;
       float s = 0.f;
-      for (int p = 0; p < groups; ++p) s += red[((size_t)p * nkw * 32 + kslot) * NC + c];
+      for (int p = 0; p < groups; ++p) s += red[((size_t)p * (kin + 1) + kslot) * NC + c];
       o[c] = s;
     }
   }
@@ -213,8 +231,7 @@ size_t conv_fwd_smem(const ConvGeom& g, int nc) {
 size_t conv_dw_smem(const ConvGeom& g, int nc) {
   const size_t stage =
       (size_t)kConvRows * (g.H + 2) * (g.W + 2) * g.C + (size_t)kConvRows * g.H * g.W * nc;
-  const int nkw = (9 * g.C + 1 + 31) / 32;
-  const size_t red = (size_t)((kConvThreads / 32) / nkw) * nkw * 32 * nc;
+  const size_t red = (size_t)(kConvThreads / (9 * g.C + 1)) * (9 * g.C + 1) * nc;
   return std::max(stage, red) * 4;
 }
 
