@@ -36,7 +36,8 @@ EXPORTS = (
     "bt_learner_loss_grads", "bt_learner_act", "bt_sample_categorical", "bt_nccl_unique_id",
     "bt_learner_comm_init", "bt_learner_profile", "bt_learner_profile_read",
     "bt_learner_launch_count", "bt_gemm_bf16", "bt_gemm_bf16x3", "bt_clip_adam",
-    "bt_clip_adam_noalloc", "bt_learner_use_graphs",
+    "bt_clip_adam_noalloc", "bt_learner_use_graphs", "bt_learner_check",
+    "bt_selftest_bounded_wait",
 )
 
 
@@ -120,6 +121,8 @@ def lib() -> C.CDLL:
         "bt_learner_get_state": (C.c_int, [vp, vp, vp, vp, C.POINTER(i32), vp]),
         "bt_learner_update": (C.c_int, [vp, C.POINTER(Batch), vp, vp, vp]),
         "bt_learner_use_graphs": (C.c_int, [vp, i32]),
+        "bt_learner_check": (C.c_int, [vp, vp]),
+        "bt_selftest_bounded_wait": (C.c_int, [i32, vp]),
         "bt_learner_targets": (C.c_int, [vp, vp, vp, vp, vp]),
         "bt_learner_loss_grads": (C.c_int, [vp, C.POINTER(Batch), vp, vp, vp, i32, vp, vp, vp]),
         "bt_learner_act": (C.c_int, [vp, vp, i32, vp, f32, vp, vp, vp, vp]),

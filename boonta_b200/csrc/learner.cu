@@ -878,6 +878,27 @@ extern "C" int bt_learner_get_state(bt_learner* L, float* params, float* mu, flo
   return BT_OK;
 }
 
+extern "C" int bt_learner_check(bt_learner* L, void* stream) {
+  BT_CHECK_ARG(L, "null learner");
+  BT_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  int code = 0;
+  BT_CUDA(cudaMemcpy(&code, L->err_d, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code == 0) return BT_OK;
+  BT_CUDA(cudaMemset(L->err_d, 0, sizeof(int)));
+  if (code == 2) {
+    set_error("a rank's share of a global minibatch exceeded the learner's capacity");
+    return BT_ERR_CAPACITY;
+  }
+  const char* what = code == umma::kErrTimeoutFull    ? "a stage of TMA loads never arrived"
+                     : code == umma::kErrTimeoutEmpty ? "a stage was never released by the MMAs"
+                     : code == umma::kErrTimeoutAcc   ? "an accumulator was never committed or released"
+                     : code == umma::kErrTimeoutEpiIn ? "an epilogue input tile never arrived"
+                                                      : "unknown";
+  set_error("a bounded wait in a tensor-core GEMM gave up (code %d: %s); its results are invalid",
+            code, what);
+  return BT_ERR_TIMEOUT;
+}
+
 namespace {
 
 // The body of one PPO.update (non-recurrent), enqueued on s (and side streams joined back).

@@ -177,6 +177,10 @@ class Learner:
         _lib.check(_lib.lib().bt_learner_update(self._h, C.byref(b), _ptr(perm), _ptr(st), _stream()))
         return st
 
+    def check(self):
+        """Synchronise and raise if a kernel of an earlier call recorded a failure."""
+        _lib.check(_lib.lib().bt_learner_check(self._h, _stream()))
+
     def use_graphs(self, enable: bool = True):
         """Replay updates as a captured CUDA graph (the default) or enqueue them eagerly."""
         _lib.check(_lib.lib().bt_learner_use_graphs(self._h, int(enable)))

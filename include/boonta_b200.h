@@ -175,6 +175,18 @@ BT_API int bt_learner_get_state(bt_learner* learner, float* params, float* mu, f
 BT_API int bt_learner_update(bt_learner* learner, const bt_batch* batch, const int32_t* permutations,
                       float* stats, void* stream);
 
+/* Synchronises `stream` and reports a failure that kernels of earlier calls recorded on the
+ * device (a bounded wait that gave up: BT_ERR_TIMEOUT; a rank's minibatch share beyond
+ * capacity: BT_ERR_CAPACITY), clearing it. Updates only enqueue work, so their device-side
+ * failures surface here (no counterpart in the reference, where XLA reports them). */
+BT_API int bt_learner_check(bt_learner* learner, void* stream);
+
+/* Self-test of the bounded waits every waiting kernel uses: one thread waits on an mbarrier
+ * that nothing arrives at, for limit_us microseconds (at most 2 s), then gives up and records
+ * the failure; returns BT_ERR_TIMEOUT when it did (the expected result) with the context still
+ * usable. No counterpart in the reference. */
+BT_API int bt_selftest_bounded_wait(int32_t limit_us, void* stream);
+
 /* CUDA-graph replay of bt_learner_update (on by default; no counterpart in the reference,
  * where XLA compiles the update into one program). The first update with a given set of
  * batch pointers runs eagerly, the second is captured into a CUDA graph, and later updates
