@@ -264,14 +264,12 @@ int allocate(bt_learner* L) {
       const int dm = lp.kin + 1, dn = lp.ncol;
       const int dk = L->rows_cap;
       if (lp.tc) {
-        // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1]. These GEMMs run on a side
-        // stream next to the dX chain, so they need not fill the GPU: at most one wave of
-        // CTAs and at least 32 K blocks (2048 rows) per split keep the split-K partials
-        // (written and re-read by the reduction) small.
+        // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1], split over K (the rows) to
+        // fill one wave of CTAs with at least 16 K blocks (1024 rows) per split.
         const int bn = c.precision == BT_PREC_BF16X3 ? 64 : 128;
         const int tiles = ceil_div(lp.kout, 128) * ceil_div(lp.kin + 1, bn);
         const int nkb = ceil_div(L->rows_cap, 64);
-        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 32));
+        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 16));
         lp.dw_kbps = ceil_div(nkb, splits);
         lp.dw_splits = ceil_div(nkb, lp.dw_kbps);
       } else if (lp.kind == BT_LAYER_CONV3X3) {
