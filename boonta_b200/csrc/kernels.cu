@@ -316,21 +316,46 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
   const float bc1 = __fsub_rn(1.f, powf(p.b1, (float)count));
   const float bc2 = __fsub_rn(1.f, powf(p.b2, (float)count));
   const float omb1 = __fsub_rn(1.f, p.b1), omb2 = __fsub_rn(1.f, p.b2);
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += stride) {
-    float g = p.grads[i];
+  auto step = [&](float g, float& prm, float& m, float& v) {
     if (clip) g = __fmul_rn(__fdiv_rn(g, g_norm), p.max_norm);
-    const float m = __fadd_rn(__fmul_rn(omb1, g), __fmul_rn(p.b1, p.mu[i]));
-    const float v = __fadd_rn(__fmul_rn(omb2, __fmul_rn(g, g)), __fmul_rn(p.b2, p.nu[i]));
+    m = __fadd_rn(__fmul_rn(omb1, g), __fmul_rn(p.b1, m));
+    v = __fadd_rn(__fmul_rn(omb2, __fmul_rn(g, g)), __fmul_rn(p.b2, v));
     const float mh = __fdiv_rn(m, bc1);
     const float vh = __fdiv_rn(v, bc2);
     const float den = __fadd_rn(__fsqrt_rn(__fadd_rn(vh, p.eps_root)), p.eps);
     const float u = __fmul_rn(-p.lr, __fdiv_rn(mh, den));
-    const float np_ = __fadd_rn(p.params[i], u);
-    p.params[i] = np_;
+    prm = __fadd_rn(prm, u);
+  };
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // four elements per thread and step as float4s (all loads before any store) when every
+  // buffer allows it, the remainder past the last multiple of 4 one by one
+  const uintptr_t a16 = (uintptr_t)p.params | (uintptr_t)p.mu | (uintptr_t)p.nu |
+                        (uintptr_t)p.grads;
+  const uintptr_t a8 = (uintptr_t)p.shadow | (uintptr_t)p.shadow_lo;
+  const bool vec = (a16 & 15) == 0 && (a8 & 7) == 0;
+  const int64_t n4 = vec ? p.n / 4 : 0;
+  for (int64_t q = first; q < n4; q += stride) {
+    const float4 g = __ldg(reinterpret_cast<const float4*>(p.grads) + q);
+    float4 prm = reinterpret_cast<const float4*>(p.params)[q];
+    float4 m = reinterpret_cast<const float4*>(p.mu)[q];
+    float4 v = reinterpret_cast<const float4*>(p.nu)[q];
+    step(g.x, prm.x, m.x, v.x);
+    step(g.y, prm.y, m.y, v.y);
+    step(g.z, prm.z, m.z, v.z);
+    step(g.w, prm.w, m.w, v.w);
+    reinterpret_cast<float4*>(p.params)[q] = prm;
+    reinterpret_cast<float4*>(p.mu)[q] = m;
+    reinterpret_cast<float4*>(p.nu)[q] = v;
+    if (p.shadow) store_bf16x4(p.shadow, p.shadow_lo, 4 * q, prm);
+  }
+  for (int64_t i = 4 * n4 + first; i < p.n; i += stride) {
+    float prm = p.params[i], m = p.mu[i], v = p.nu[i];
+    step(p.grads[i], prm, m, v);
+    p.params[i] = prm;
     p.mu[i] = m;
     p.nu[i] = v;
-    if (p.shadow) store_bf16(p.shadow, p.shadow_lo, i, np_);
+    if (p.shadow) store_bf16(p.shadow, p.shadow_lo, i, prm);
   }
 }
 
@@ -625,7 +650,17 @@ __global__ void gather_bf16_kernel(const float* obs, const int* idx, int rows, i
   const int lane = threadIdx.x & 31;
   if (row >= live_rows(count, rows)) return;
   const float* src = obs + (size_t)(idx ? idx[row] : row) * d;
-  for (int k = lane; k < ld; k += 32) {
+  int k0 = 0;
+  if ((d & 3) == 0 && (ld & 3) == 0) {
+    // float4 loads and 8-byte bf16 stores, four chunks in flight per lane
+    const int q4 = d / 4;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll 4
+    for (int q = lane; q < q4; q += 32)
+      store_bf16x4(out, out_lo, (size_t)row * ld + 4 * q, __ldg(s4 + q));
+    k0 = d;
+  }
+  for (int k = k0 + lane; k < ld; k += 32) {
     const float v = k < d ? src[k] : (k == d ? 1.f : 0.f);
     store_bf16(out, out_lo, (size_t)row * ld + k, v);
   }
