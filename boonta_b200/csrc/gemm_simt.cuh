@@ -216,6 +216,97 @@ __global__ void __launch_bounds__(kGemmThreads)
   }
 }
 
+// Small-output variant for the recurrent per-step products (M = environments of a
+// minibatch, N and K a few hundred): BM x 32 tiles, K in steps of 32 with the next step's
+// operands loaded into registers while the current one is multiplied (one shared-memory
+// buffer per step, two barriers), 128 threads each computing (BM / 16) x 4 outputs, so a
+// 256 x 256 product still spreads over 64-128 CTAs. Same loader / epilogue interface, no
+// split-K, live rows through m_count.
+template <int BM, class AL, class BL, class EP>
+__global__ void __launch_bounds__(128)
+    gemm_simt_small_kernel(AL a, BL b, EP ep, int M, int N, int K, const int* m_count) {
+  constexpr int BN = 32, BK = 32, RM = BM / 16;
+  constexpr int NA = BM * BK / 128, NB = BN * BK / 128;  // elements per thread per step
+  __shared__ float As[BK][BM + 1];
+  __shared__ float Bs[BK][BN + 1];
+  if (m_count) M = min(M, *m_count);
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  if (m0 >= M) return;
+  const int tid = threadIdx.x;
+  const int tm = tid >> 3, tn = tid & 7;  // rows tm*RM .. +RM-1, columns tn*4 .. +3
+  float acc[RM][4];
+#pragma unroll
+  for (int i = 0; i < RM; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  float ra[NA], rb[NB];
+  auto load = [&](int k0) {  // consecutive threads on consecutive k (or n when contiguous)
+#pragma unroll
+    for (int u = 0; u < NA; ++u) {
+      const int e = tid + 128 * u, mm = e / BK, kk = e % BK;
+      ra[u] = (k0 + kk < K) ? a.load(m0 + mm, k0 + kk, M, K) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+      const int e = tid + 128 * u;
+      const int kk = BL::kNContig ? e / BN : e % BK, nn = BL::kNContig ? e % BN : e / BK;
+      rb[u] = (k0 + kk < K) ? b.load(k0 + kk, n0 + nn, N) : 0.f;
+    }
+  };
+  load(0);
+  for (int k0 = 0; k0 < K; k0 += BK) {
+#pragma unroll
+    for (int u = 0; u < NA; ++u) {
+      const int e = tid + 128 * u;
+      As[e % BK][e / BK] = ra[u];
+    }
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+      const int e = tid + 128 * u;
+      if (BL::kNContig) {
+        Bs[e / BN][e % BN] = rb[u];
+      } else {
+        Bs[e % BK][e / BK] = rb[u];
+      }
+    }
+    __syncthreads();
+    if (k0 + BK < K) load(k0 + BK);  // in flight during the products below
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float av[RM], bv[4];
+#pragma unroll
+      for (int i = 0; i < RM; ++i) av[i] = As[kk][tm * RM + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tn * 4 + j];
+#pragma unroll
+      for (int i = 0; i < RM; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < RM; ++i) {
+    const int m = m0 + tm * RM + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tn * 4 + j;
+      if (n < N) ep.store(m, n, acc[i][j], 0);
+    }
+  }
+}
+
+template <int BM, class AL, class BL, class EP>
+int launch_gemm_simt_small(const AL& a, const BL& b, const EP& ep, int M, int N, int K,
+                           cudaStream_t stream, const int* m_count = nullptr) {
+  if (M <= 0 || N <= 0) return BT_OK;
+  dim3 grid(ceil_div(M, BM), ceil_div(N, 32));
+  gemm_simt_small_kernel<BM, AL, BL, EP><<<grid, 128, 0, stream>>>(a, b, ep, M, N, K, m_count);
+  BT_LAUNCH_CHECK("gemm_simt_small_kernel");
+  return BT_OK;
+}
+
 template <class AL, class BL, class EP>
 int launch_gemm_simt(const AL& a, const BL& b, const EP& ep, int M, int N, int K, int splits,
                      cudaStream_t stream, const int* m_count = nullptr,

@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F,
                                                         const float* d, int n, int rows,
                                                         const int* count, int rows_per_split,
                                                         float* out) {
-  __shared__ float ds[64][NMAX];
+  __shared__ __align__(16) float ds[64][NMAX];
   const int k = blockIdx.x * 128 + threadIdx.x;
   const int live = live_rows(count, rows);
   const int r0 = blockIdx.y * rows_per_split;
@@ -590,9 +590,21 @@ __global__ void __launch_bounds__(128) skinny_dw_kernel(const float* f, int F,
         if (k < F) fk[u] = act_fwd<ACT>(fk[u]);
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < 8; ++u) {
+        if constexpr (NMAX % 4 == 0) {
 #pragma unroll
-        for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(fk[u], ds[r8 + u][j], acc[j]);
+          for (int j = 0; j < NMAX; j += 4) {  // broadcast float4 reads of the row's d
+            const float4 dd = *reinterpret_cast<const float4*>(&ds[r8 + u][j]);
+            acc[j] = fmaf(fk[u], dd.x, acc[j]);
+            acc[j + 1] = fmaf(fk[u], dd.y, acc[j + 1]);
+            acc[j + 2] = fmaf(fk[u], dd.z, acc[j + 2]);
+            acc[j + 3] = fmaf(fk[u], dd.w, acc[j + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(fk[u], ds[r8 + u][j], acc[j]);
+        }
+      }
     }
   }
   if (k <= F) {

@@ -938,17 +938,27 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
   return BT_OK;
 }
 
-void batch_key(const bt_batch* b, bool stats, const void* (&key)[10]) {
-  const void* k[10] = {b->obs,      b->bootstrap_obs, b->action, b->reward,
-                       b->terminated, b->truncated,   b->log_prob, b->value,
-                       stats ? (const void*)1 : nullptr, nullptr};
-  for (int i = 0; i < 10; ++i) key[i] = k[i];
+constexpr int kKey = 12;
+
+void batch_key(const bt_batch* b, bool stats, const void* (&key)[kKey]) {
+  const void* k[kKey] = {b->obs,        b->bootstrap_obs, b->action,     b->reward,
+                         b->terminated, b->truncated,     b->log_prob,   b->value,
+                         b->first_done, b->carry,         b->last_carry,
+                         stats ? (const void*)1 : nullptr};
+  for (int i = 0; i < kKey; ++i) key[i] = k[i];
 }
 
-bool same_key(const void* const (&a)[10], const void* const (&b)[10]) {
-  for (int i = 0; i < 10; ++i)
+bool same_key(const void* const (&a)[kKey], const void* const (&b)[kKey]) {
+  for (int i = 0; i < kKey; ++i)
     if (a[i] != b[i]) return false;
   return true;
+}
+
+// One full update, recurrent or not, enqueued on s.
+int run_update(bt_learner* L, const bt_batch* batch, const int32_t* perm, float* stats,
+               cudaStream_t s) {
+  if (L->recurrent) return recurrent_update(L, batch, perm, stats, s);
+  return update_body(L, batch, perm, stats, s);
 }
 
 // Captures update_body into L->graph (updating the existing executable graph in place when
@@ -959,7 +969,7 @@ int capture_update(bt_learner* L, const bt_batch* batch, bool stats) {
   if (!L->cap_stream) BT_CUDA(cudaStreamCreateWithFlags(&L->cap_stream, cudaStreamNonBlocking));
   const cudaStream_t cs = L->cap_stream;
   BT_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-  const int rc = update_body(L, batch, L->perm_d, stats ? L->stats_d : nullptr, cs);
+  const int rc = run_update(L, batch, L->perm_d, stats ? L->stats_d : nullptr, cs);
   cudaGraph_t g = nullptr;
   const cudaError_t e = cudaStreamEndCapture(cs, &g);
   L->graph_launches = L->prof.launches - n0;
@@ -995,31 +1005,32 @@ extern "C" int bt_learner_update(bt_learner* L, const bt_batch* batch, const int
                                  float* stats, void* stream) {
   BT_CHECK_ARG(L && perm, "bt_learner_update: null argument");
   BT_TRY(check_batch(L, batch));
-  if (L->recurrent) return recurrent_update(L, batch, perm, stats, (cudaStream_t)stream);
   const int world = std::max(1, L->cfg.world_size);
   BT_CHECK_ARG(world == 1 || L->comm, "world_size %d needs bt_learner_comm_init", world);
   cudaStream_t s = (cudaStream_t)stream;
-  if (!L->graphs_on || L->prof.on) return update_body(L, batch, perm, stats, s);
+  if (!L->graphs_on || L->prof.on) return run_update(L, batch, perm, stats, s);
   const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
-  const size_t perm_bytes = (size_t)E * L->B * world * sizeof(int32_t);
+  // permutations: [E, T*N*world] samples, or [E, N*world] environments (recurrent)
+  const size_t perm_bytes =
+      (size_t)E * (L->recurrent ? (int64_t)L->N : L->B) * world * sizeof(int32_t);
   if (!L->perm_d) {
     BT_TRY(dalloc(L, &L->perm_d, perm_bytes / sizeof(int32_t)));
     BT_TRY(dalloc(L, &L->stats_d, (size_t)E * M * 8));
   }
   BT_CUDA(cudaMemcpyAsync(L->perm_d, perm, perm_bytes, cudaMemcpyDeviceToDevice, s));
-  const void* key[10];
+  const void* key[kKey];
   batch_key(batch, stats != nullptr, key);
   if (L->graph && same_key(key, L->graph_key)) {
     BT_CUDA(cudaGraphLaunch(L->graph, s));
     L->prof.launches += L->graph_launches;
   } else if (same_key(key, L->seen_key)) {
     BT_TRY(capture_update(L, batch, stats != nullptr));
-    for (int i = 0; i < 10; ++i) L->graph_key[i] = key[i];
+    for (int i = 0; i < kKey; ++i) L->graph_key[i] = key[i];
     BT_CUDA(cudaGraphLaunch(L->graph, s));
     L->prof.launches += L->graph_launches;
   } else {
-    for (int i = 0; i < 10; ++i) L->seen_key[i] = key[i];
-    BT_TRY(update_body(L, batch, L->perm_d, stats ? L->stats_d : nullptr, s));
+    for (int i = 0; i < kKey; ++i) L->seen_key[i] = key[i];
+    BT_TRY(run_update(L, batch, L->perm_d, stats ? L->stats_d : nullptr, s));
   }
   if (stats)
     BT_CUDA(cudaMemcpyAsync(stats, L->stats_d, (size_t)E * M * 8 * sizeof(float),

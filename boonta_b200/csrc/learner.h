@@ -189,8 +189,8 @@ struct bt_learner {
   cudaStream_t cap_stream = nullptr;  // captures run here (the caller's may be the legacy stream)
   cudaGraphExec_t graph = nullptr;
   int64_t graph_launches = 0;  // kernels and collectives in the graph
-  const void* graph_key[10] = {};
-  const void* seen_key[10] = {};
+  const void* graph_key[12] = {};
+  const void* seen_key[12] = {};
   int32_t* perm_d = nullptr;
   float* stats_d = nullptr;
   size_t next_event = 0;

@@ -175,7 +175,7 @@ int gru_forward(bt_learner* L, LayerPlan& g, const float* x, const float* carry,
     ARows a{g.hin + (size_t)t * H, nullptr, T * H, H};
     BRows b{L->params + g.wh_off, 3 * H, H};
     EpiForward ep{g.hp, nullptr, 3 * H, BT_ACT_NONE};
-    BT_K(L, kProfGemmFwd, s, launch_gemm_simt(a, b, ep, envs, 3 * H, H, 1, s, env_count, nullptr));
+    BT_K(L, kProfGemmFwd, s, launch_gemm_simt_small<32>(a, b, ep, envs, 3 * H, H, s, env_count));
     BT_K(L, kProfMisc, s, launch_elementwise(gru_fwd_step_kernel, (int64_t)envs * H, s, t, T, H,
                                              envs, env_count, (const float*)g.xp,
                                              (const float*)g.hp,
@@ -200,7 +200,7 @@ int gru_backward(bt_learner* L, LayerPlan& g, LayerPlan& prev, const int* env_co
       ARows a{g.dhp + (size_t)t * 3 * H, nullptr, T * 3 * H, 3 * H};
       BCols b{L->params + g.wh_off, 3 * H, 3 * H};
       EpiCarry ep{g.dh_carry, g.dh_direct, L->rnn_reset, T, t, H};
-      BT_K(L, kProfGemmDx, s, launch_gemm_simt(a, b, ep, envs, H, 3 * H, 1, s, env_count, nullptr));
+      BT_K(L, kProfGemmDx, s, launch_gemm_simt_small<16>(a, b, ep, envs, H, 3 * H, s, env_count));
     }
   }
   // weight gradients over all live rows

@@ -31,14 +31,23 @@ def _run(w, graphs: bool, steps: int):
             np.stack(stats), lrn.launch_count())
 
 
-@pytest.mark.parametrize("precision", ["fp32", "bf16x3"])
-def test_graph_replay_matches_eager_updates(precision):
-    w = configs.make("c2", precision=precision).scaled(num_steps=8, num_envs=256,
-                                                       num_minibatches=4, update_epochs=2)
+CASES = {
+    "c2_fp32": lambda: configs.make("c2", precision="fp32").scaled(
+        num_steps=8, num_envs=256, num_minibatches=4, update_epochs=2),
+    "c2_bf16x3": lambda: configs.make("c2", precision="bf16x3").scaled(
+        num_steps=8, num_envs=256, num_minibatches=4, update_epochs=2),
+    "c4_gru": lambda: configs.make("c4").scaled(num_steps=8, num_envs=32, num_minibatches=2,
+                                                update_epochs=2),
+}
+
+
+@pytest.mark.parametrize("name", list(CASES))
+def test_graph_replay_matches_eager_updates(name):
+    w = CASES[name]()
     eager = _run(w, graphs=False, steps=4)
     graph = _run(w, graphs=True, steps=4)  # eager, capture + replay, replay, replay
     for a, b in zip(eager[:3], graph[:3]):
         np.testing.assert_array_equal(a, b)
-    assert eager[3] == graph[3] == 4 * 2 * 4
+    assert eager[3] == graph[3] == 4 * w.ppo.update_epochs * w.ppo.num_minibatches
     np.testing.assert_array_equal(eager[4], graph[4])
     assert eager[5] == graph[5]  # replays count the graph's kernels as launches
