@@ -205,6 +205,8 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();  // the operands and live counts come from earlier kernels
   int M = sh.M, K = sh.K;
   if (sh.m_count) M = min(M, *sh.m_count);
   if (sh.k_count) K = min(K, *sh.k_count);
@@ -402,13 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int M = sh.M;
-  if (sh.m_count) M = min(M, *sh.m_count);
-  const int ntn = ceil_div(sh.N, BN);
-  const int tiles = ceil_div(M, BM) * ntn;
-  const int nk = ceil_div(sh.K, BK);
-  if ((int)blockIdx.x >= tiles) return;  // whole CTA leaves before any barrier or TMEM use
-
+  pdl_trigger();
   if (threadIdx.x == 0) {
     s_fail = 0;
     for (int s = 0; s < C::kStages; ++s) {
@@ -428,6 +424,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   auto failed = [&]() { return *(volatile int*)&s_fail != 0; };
+  // The prologue above overlaps the previous kernel's tail; everything below reads its
+  // outputs. A CTA without tiles runs no loop and frees its TMEM at the end.
+  pdl_wait();
+  int M = sh.M;
+  if (sh.m_count) M = min(M, *sh.m_count);
+  const int ntn = ceil_div(sh.N, BN);
+  const int tiles = ceil_div(M, BM) * ntn;
+  const int nk = ceil_div(sh.K, BK);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -790,8 +794,8 @@ int launch_gemm(const Operands& ops, const GemmShape& sh, const Epi& epi, int sp
       configured = true;
     }
     const int tiles = ceil_div(sh.M, BM) * ceil_div(sh.N, BN);
-    kernel<<<min(tiles, kNumSMs), kThreads, C::kSmem, stream>>>(ops, sh, epi);
-    BT_LAUNCH_CHECK("umma_persistent_kernel");
+    BT_CUDA(launch_pdl(kernel, dim3(min(tiles, kNumSMs)), dim3(kThreads), C::kSmem, stream, ops,
+                       sh, epi));
   } else {
     using C = Cfg<BN, X3, Epi::kDeep>;
     auto kernel = umma_gemm_kernel<BN, A_MN, B_MN, X3, Epi>;
@@ -800,8 +804,7 @@ int launch_gemm(const Operands& ops, const GemmShape& sh, const Epi& epi, int sp
       configured = true;
     }
     dim3 grid(ceil_div(sh.M, BM), ceil_div(sh.N, BN), max(1, splits));
-    kernel<<<grid, kThreads, C::kSmem, stream>>>(ops, sh, epi);
-    BT_LAUNCH_CHECK("umma_gemm_kernel");
+    BT_CUDA(launch_pdl(kernel, grid, dim3(kThreads), C::kSmem, stream, ops, sh, epi));
   }
   return BT_OK;
 }

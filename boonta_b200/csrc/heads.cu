@@ -227,6 +227,8 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
   float* lsig_s = sm + Lo.lsig;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();
+  pdl_wait();  // parameters, features and targets come from earlier kernels
   const int live = live_rows(p.count, p.rows);
   const int tiles = ceil_div(live, kTileRows);
 
@@ -544,8 +546,7 @@ int launch_heads_inst(const HeadsParams& p, int blocks, size_t smem, cudaStream_
     BT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     configured = smem;
   }
-  kernel<<<blocks, kHeadThreads, smem, stream>>>(p);
-  BT_LAUNCH_CHECK("heads_loss_kernel");
+  BT_CUDA(launch_pdl(kernel, dim3(blocks), dim3(kHeadThreads), smem, stream, p));
   return BT_OK;
 }
 

@@ -188,6 +188,8 @@ __global__ void __launch_bounds__(256, 4) reduce_segments_kernel(const Segment* 
                                                               float* grads,
                                                               double* norm_partials) {
   __shared__ double sh[8];
+  pdl_trigger();
+  pdl_wait();
   const ReduceChunk ch = chunks[blockIdx.x];
   const Segment sg = segs[ch.seg];
   double sq = 0.0;
@@ -275,8 +277,8 @@ __global__ void __launch_bounds__(256, 4) reduce_segments_kernel(const Segment* 
 int launch_reduce_segments(const Segment* segs, const ReduceChunk* chunks, int num_chunks,
                            float* grads, double* norm_partials, cudaStream_t stream) {
   if (num_chunks <= 0) return BT_OK;
-  reduce_segments_kernel<<<num_chunks, 256, 0, stream>>>(segs, chunks, grads, norm_partials);
-  BT_LAUNCH_CHECK("reduce_segments_kernel");
+  BT_CUDA(launch_pdl(reduce_segments_kernel, dim3(num_chunks), dim3(256), 0, stream, segs,
+                     chunks, grads, norm_partials));
   return BT_OK;
 }
 
@@ -304,6 +306,8 @@ int launch_sumsq(const float* g, int64_t n, double* norm_partials, cudaStream_t 
 __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
   __shared__ double sh[8];
   __shared__ float s_norm;
+  pdl_trigger();
+  pdl_wait();
   double part = 0.0;
   for (int i = threadIdx.x; i < p.num_norm_partials; i += blockDim.x) part += p.norm_partials[i];
   // fixed-order block sum: thread-strided partial sums, then warps in order
@@ -360,8 +364,7 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
 }
 
 int launch_adam(const AdamParams& p, cudaStream_t stream) {
-  adam_kernel<<<2 * kNumSMs, 256, 0, stream>>>(p);
-  BT_LAUNCH_CHECK("adam_kernel");
+  BT_CUDA(launch_pdl(adam_kernel, dim3(2 * kNumSMs), dim3(256), 0, stream, p));
   return BT_OK;
 }
 
@@ -660,6 +663,8 @@ __global__ void gather_bf16_kernel(const float* obs, const int* idx, int rows, i
                                    __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (row >= live_rows(count, rows)) return;
   const float* src = obs + (size_t)(idx ? idx[row] : row) * d;
   int k0 = 0;
@@ -682,9 +687,8 @@ int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld
                        __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
                        cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
-  gather_bf16_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(obs, idx, rows, d, ld, out,
-                                                                   out_lo, count);
-  BT_LAUNCH_CHECK("gather_bf16_kernel");
+  BT_CUDA(launch_pdl(gather_bf16_kernel, dim3(ceil_div(rows * 32, 256)), dim3(256), 0, stream,
+                     obs, idx, rows, d, ld, out, out_lo, count));
   return BT_OK;
 }
 
