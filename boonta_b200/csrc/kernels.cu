@@ -21,6 +21,8 @@ __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int
                                   int ldhb, float* mean_out, float* rstd_out, const int* count) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (row >= live_rows(count, rows)) return;
   const float* zr = z + (size_t)row * n;
   float s = 0.f, s2 = 0.f;
@@ -53,10 +55,8 @@ int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, 
                       float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb, float* mean,
                       float* rstd, const int* count, cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
-  ln_forward_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(z, scale_bias, rows, n, act, y,
-                                                                  h, hb, hb_lo, ldhb, mean, rstd,
-                                                                  count);
-  BT_LAUNCH_CHECK("ln_forward_kernel");
+  BT_CUDA(launch_pdl(ln_forward_kernel, dim3(ceil_div(rows * 32, 256)), dim3(256), 0, stream, z,
+                     scale_bias, rows, n, act, y, h, hb, hb_lo, ldhb, mean, rstd, count));
   return BT_OK;
 }
 
@@ -398,6 +398,8 @@ int launch_increment(int* count, int by, cudaStream_t stream) {
 // ---- statistics --------------------------------------------------------------------------
 // One warp per statistic: lanes stride over the block partials, then a fixed shuffle tree.
 __global__ void stat_reduce_kernel(const double* partials, int blocks, double* out) {
+  pdl_trigger();
+  pdl_wait();
   const int s = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (s >= kNumStatSums) return;
   double t = 0.0;
@@ -407,8 +409,8 @@ __global__ void stat_reduce_kernel(const double* partials, int blocks, double* o
 }
 
 int launch_stat_reduce(const double* partials, int blocks, double* out, cudaStream_t stream) {
-  stat_reduce_kernel<<<1, 32 * kNumStatSums, 0, stream>>>(partials, blocks, out);
-  BT_LAUNCH_CHECK("stat_reduce_kernel");
+  BT_CUDA(launch_pdl(stat_reduce_kernel, dim3(1), dim3(32 * kNumStatSums), 0, stream, partials,
+                     blocks, out));
   return BT_OK;
 }
 

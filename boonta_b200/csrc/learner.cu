@@ -266,7 +266,7 @@ int allocate(bt_learner* L) {
       if (lp.tc) {
         // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1], split over K (the rows) to
         // fill one wave of CTAs with at least 16 K blocks (1024 rows) per split.
-        const int bn = c.precision == BT_PREC_BF16X3 ? 64 : 128;
+        const int bn = 128;
         const int tiles = ceil_div(lp.kout, 128) * ceil_div(lp.kin + 1, bn);
         const int nkb = ceil_div(L->rows_cap, 64);
         int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 16));
@@ -559,7 +559,7 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
       umma::GemmShape sh{lp.kout, lp.kin + 1, rows, lp.dw_kbps, nullptr, count, L->err_d};
       umma::EpiDwT ep{lp.dw_part, lp.kout, (size_t)dm * dn, lp.kin + 1};
       if (L->x3) {
-        BT_K(L, kProfGemmDw, sw, umma::launch_gemm<64, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
+        BT_K(L, kProfGemmDw, sw, umma::launch_gemm<128, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
       } else {
         BT_K(L, kProfGemmDw, sw, umma::launch_gemm<128, true, true, false>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
       }
