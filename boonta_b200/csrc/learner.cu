@@ -421,8 +421,7 @@ int allocate_tensor_core(bt_learner* L) {
         BT_TRY(umma::encode_map(fa, xin, lp.kin, R, (uint64_t)lp.ldx * 2, 64, 128));
         BT_TRY(umma::encode_map(fb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64, 64));
         BT_TRY(umma::encode_map(xa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 128));
-        BT_TRY(umma::encode_map(xb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64,
-                                L->x3 ? 64 : 128));
+        BT_TRY(umma::encode_map(xb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64, 128));
         BT_TRY(umma::encode_map(wa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 64));
         BT_TRY(umma::encode_map(wb, xin, lp.kin + 1, R, (uint64_t)lp.ldx * 2, 64, 64));
       }
@@ -494,7 +493,7 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       ep.has_hi = !lp.ln && !last;
       ep.has_lo = ep.has_hi && L->x3;
       if (L->x3) {
-        BT_K(L, kProfGemmFwd, s, umma::launch_gemm<64, false, true, true>(lp.fwd_ops, sh, ep, 1, s));
+        BT_K(L, kProfGemmFwd, s, umma::launch_gemm<128, false, true, true>(lp.fwd_ops, sh, ep, 1, s));
       } else if (lp.fwd_bn == 256) {
         BT_K(L, kProfGemmFwd, s, umma::launch_gemm<256, false, true, false>(lp.fwd_ops, sh, ep, 1, s));
       } else {
@@ -578,7 +577,7 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
         epx.has_hi = !epx.has_f32;
         epx.has_lo = epx.has_hi && L->x3;
         if (L->x3) {
-          BT_K(L, kProfGemmDx, s, umma::launch_gemm<64, false, false, true>(lp.dx_ops, shx, epx, 1, s));
+          BT_K(L, kProfGemmDx, s, umma::launch_gemm<128, false, false, true>(lp.dx_ops, shx, epx, 1, s));
         } else {
           BT_K(L, kProfGemmDx, s, umma::launch_gemm<128, false, false, false>(lp.dx_ops, shx, epx, 1, s));
         }
