@@ -149,6 +149,58 @@ def gae_bytes(w) -> float:
     return 18.0 * w.batch_size + 4.0 * w.num_envs
 
 
+def gae_bandwidth(w, device, rounds: int = 4) -> dict:
+    """HBM bandwidth of the GAE kernel alone on the workload's [T, N] shape, through the public
+    bt_gae entry point: back-to-back launches cycling over enough independent copies of the
+    inputs and outputs that their total (> 160 MB) exceeds L2, so every launch reads and writes
+    HBM; CUDA events around `rounds` passes over the copies, after one untimed pass."""
+    import ctypes
+
+    import torch
+
+    from boonta_b200 import _lib
+
+    lib = _lib.lib()
+    t, n = w.num_steps, w.num_envs
+    per = gae_bytes(w)
+    copies = min(64, max(2, int(np.ceil(160e6 / per))))
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    bufs = []
+    for _ in range(copies):
+        bufs.append((torch.randn((t, n), generator=g, device=device),
+                     (torch.rand((t, n), generator=g, device=device) < w.done_p).to(torch.uint8),
+                     torch.zeros((t, n), dtype=torch.uint8, device=device),
+                     torch.randn((t, n), generator=g, device=device),
+                     torch.randn((n,), generator=g, device=device),
+                     torch.empty((t, n), device=device), torch.empty((t, n), device=device)))
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+
+    def one(b):
+        _lib.check(lib.bt_gae(*(x.data_ptr() for x in b[:5]), None, None, t, n,
+                              float(w.ppo.gamma), float(w.ppo.gae_lambda), b[5].data_ptr(),
+                              b[6].data_ptr(), sp))
+
+    for b in bufs:
+        one(b)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(rounds):
+        for b in bufs:
+            one(b)
+    e.record(stream)
+    torch.cuda.synchronize()
+    us = s.elapsed_time(e) * 1000.0 / (rounds * copies)
+    gbs = per / (us * 1e-6) / 1e9
+    pk, pk_kind = peaks()
+    del bufs
+    return {"gbs": gbs, "us_per_launch": us, "bytes_per_launch": per, "launches": rounds * copies,
+            "frac": gbs / pk["hbm_gbs"], "peak": pk["hbm_gbs"], "peaks": pk_kind,
+            "note": f"{copies} input/output copies cycled (> L2), back-to-back launches"}
+
+
 # ---- synthetic inputs on the device ----------------------------------------------------------
 def device_rollout(w, seed: int, device):
     import torch
@@ -445,11 +497,14 @@ def main():
 
     pk, pk_kind = peaks()
     roof = roofline(w, prof, pk, pk_kind)
+    # GAE inside the update (one event-bracketed launch per update, so launch latency is
+    # included) and alone, back to back on inputs larger than L2 (the bandwidth figure)
+    gae_in_update = None
     if "gae" in prof:
         g_ms, g_n = prof["gae"]
-        gae_gbs = gae_bytes(w) / (g_ms / 1000.0 / g_n) / 1e9
-    else:
-        gae_gbs = None
+        gae_in_update = gae_bytes(w) / (g_ms / 1000.0 / g_n) / 1e9
+    gae_bw = gae_bandwidth(w, device)
+    gae_bw["in_update_gbs"] = gae_in_update
 
     line = {
         "metric": "ppo_learner_env_steps_per_sec", "value": value, "unit": "env-steps/s",
@@ -464,7 +519,8 @@ def main():
                    f"{w.batch_size * w.network.obs_dim * 4 / 1e6:.0f} MB per GPU)",
                    "description": w.description},
         "roofline": roof,
-        "gae_hbm_gbs": gae_gbs,
+        "gae_hbm_gbs": gae_bw["gbs"],
+        "gae": gae_bw,
         "kernel_ms_per_step": {k: v[0] for k, v in sorted(prof.items())},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),

@@ -14,12 +14,11 @@
 // and rounded once, as the reference does with its Python-float hyperparameters.
 //
 // Data layout: [T, N] row-major, so for a fixed t consecutive envs are consecutive in
-// memory. The fast kernel gives each warp 32 env columns: one elected lane arms an
-// mbarrier, the warp's lanes issue one bulk (TMA engine) copy per (t, array) row slice
-// into shared memory — every load of the block is in flight at once — and after the
-// barrier each lane scans its column from shared memory and writes A and R for all t with
-// 128-byte coalesced stores. The HBM roofline bounds it: 18 bytes per env-step (reward 4,
-// terminated 1, truncated 1, value 4 read; advantage 4, return 4 written) + 4 per env.
+// memory. The fast kernel (gae_tile_kernel below) stages a block's env columns in shared
+// memory with asynchronous 16-byte copies issued by all its threads and scans each column
+// in one thread, writing A and R with coalesced stores. The HBM roofline bounds it: 18
+// bytes per env-step (reward 4, terminated 1, truncated 1, value 4 read; advantage 4,
+// return 4 written) + 4 per env.
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -38,19 +37,28 @@ struct GaeParams {
   int T, N;
   float gamma;   // float32(gamma)
   float glam;    // float32(gamma * lambda), product formed in double
-  int* err;      // nullable error word (set to 1 when a bounded wait gives up)
+  int* err;      // nullable error word of the learner (no GAE kernel waits on anything)
 };
 
-__device__ __forceinline__ float gae_step(float r, float v, float next_v, float term_b,
-                                          float trunc_b, float rho, float c, float adv,
-                                          float gamma, float glam) {
+// The step splits into the part that does not depend on the carried advantage (delta and
+// the carry factor k) and the carry itself, advantage = delta + k * advantage.
+__device__ __forceinline__ void gae_delta(float r, float v, float next_v, float term_b,
+                                          float trunc_b, float rho, float c, float gamma,
+                                          float glam, float& delta_out, float& k_out) {
   const float term = __fsub_rn(1.f, term_b);
   const float trunc = __fsub_rn(1.f, trunc_b);
   float delta = __fmul_rn(__fmul_rn(gamma, term), next_v);
   delta = __fsub_rn(__fadd_rn(r, delta), v);
   delta = __fmul_rn(rho, delta);
-  delta = __fmul_rn(delta, trunc);
-  const float k = __fmul_rn(__fmul_rn(__fmul_rn(glam, c), term), trunc);
+  delta_out = __fmul_rn(delta, trunc);
+  k_out = __fmul_rn(__fmul_rn(__fmul_rn(glam, c), term), trunc);
+}
+
+__device__ __forceinline__ float gae_step(float r, float v, float next_v, float term_b,
+                                          float trunc_b, float rho, float c, float adv,
+                                          float gamma, float glam) {
+  float delta, k;
+  gae_delta(r, v, next_v, term_b, trunc_b, rho, c, gamma, glam, delta, k);
   return __fadd_rn(delta, __fmul_rn(k, adv));
 }
 
@@ -73,79 +81,171 @@ __global__ void gae_plain_kernel(GaeParams p) {
   }
 }
 
-constexpr int kGaeEnvs = 32;  // env columns per warp (block)
+// Tiled path: a block owns NE env columns (NE = 16 or 32) for all T. Every thread of the
+// block issues 16-byte asynchronous copies (cp.async, no registers held) of its share of
+// the block's reward/value/flag rows into shared memory, in four commit groups that cover
+// the time steps from the last one down (the order the scan consumes them); every byte of
+// the block is requested before the first wait. The block then waits group by group
+// (cp.async.wait_group + a block barrier) and warp 0 scans each quarter while the later
+// quarters are still arriving. One thread per column does the scan, so its arithmetic is
+// the sequential reference order. Requires N % NE == 0, 16-byte aligned arrays and
+// T * NE * 10 bytes of shared memory within kGaeMaxSmem.
+constexpr int kGaeGroups = 4;
+constexpr size_t kGaeMaxSmem = 200 * 1024;
+constexpr int kGaeBatch = 16;  // steps whose inputs are moved to registers at once
 
-// Bulk path: N % 32 == 0 (so every u8 row slice is 32 bytes, 16-byte aligned), rho/c
-// absent, T * 32 * 10 bytes of shared memory.
-__global__ void __launch_bounds__(32) gae_bulk_kernel(GaeParams p) {
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most `pending` of this thread's most recent commit groups are in flight.
+__device__ __forceinline__ void cp_async_wait_pending(int pending) {
+  switch (pending) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+  }
+}
+
+// kGaeBatch steps t = tb - 1 down to tb - kGaeBatch of one column, in three passes so that
+// only the carry (one multiply and one add per step) is serial: inputs to registers, the
+// carry-independent terms of every step, the carry, then the stores. (Loading first also
+// keeps the shared loads clear of the output stores, which go through generic pointers the
+// compiler must assume may alias shared memory.)
+template <int NE>
+__device__ __forceinline__ void gae_scan_batch(const GaeParams& p, const float* r_s,
+                                               const float* v_s, const uint8_t* term_s,
+                                               const uint8_t* trunc_s, int tb, int n0, int lane,
+                                               bool on, float& adv, float& next_v) {
+  float rr[kGaeBatch], vv[kGaeBatch], tm[kGaeBatch], tr[kGaeBatch];
+#pragma unroll
+  for (int k = 0; k < kGaeBatch; ++k) {
+    const int s = (tb - 1 - k) * NE + lane;
+    rr[k] = r_s[s];
+    vv[k] = v_s[s];
+    tm[k] = (float)term_s[s];
+    tr[k] = (float)trunc_s[s];
+  }
+  float dl[kGaeBatch], kk[kGaeBatch];
+#pragma unroll
+  for (int k = 0; k < kGaeBatch; ++k)
+    gae_delta(rr[k], vv[k], k == 0 ? next_v : vv[k - 1], tm[k], tr[k], 1.f, 1.f, p.gamma,
+              p.glam, dl[k], kk[k]);
+#pragma unroll
+  for (int k = 0; k < kGaeBatch; ++k) {
+    adv = __fadd_rn(dl[k], __fmul_rn(kk[k], adv));
+    rr[k] = adv;  // the step's advantage, in place of its reward
+  }
+  next_v = vv[kGaeBatch - 1];
+  if (on) {
+    float* pa = p.adv + (size_t)(tb - 1) * p.N + n0 + lane;
+    float* pr = p.ret + (size_t)(tb - 1) * p.N + n0 + lane;
+#pragma unroll
+    for (int k = 0; k < kGaeBatch; ++k) {
+      pa[-(ptrdiff_t)k * p.N] = rr[k];
+      pr[-(ptrdiff_t)k * p.N] = __fadd_rn(rr[k], vv[k]);
+    }
+  }
+}
+
+template <int NE>
+__global__ void __launch_bounds__(NE * 8) gae_tile_kernel(GaeParams p) {
+  constexpr int kThreads = NE * 8;
+  constexpr int kF = NE / 4, kB = NE / 16;    // 16-byte pieces per row: floats, flags
+  constexpr int kRow = 2 * kF + 2 * kB;
   extern __shared__ __align__(128) uint8_t smem[];
   const int T = p.T;
-  float* r_s = reinterpret_cast<float*>(smem);             // [T][32]
-  float* v_s = r_s + (size_t)T * kGaeEnvs;                 // [T][32]
-  uint8_t* term_s = reinterpret_cast<uint8_t*>(v_s + (size_t)T * kGaeEnvs);  // [T][32]
-  uint8_t* trunc_s = term_s + (size_t)T * kGaeEnvs;        // [T][32]
-  __shared__ __align__(8) uint64_t bar;
+  const int C = (T + kGaeGroups - 1) / kGaeGroups;  // steps per group
+  float* r_s = reinterpret_cast<float*>(smem);                 // [T][NE]
+  float* v_s = r_s + (size_t)T * NE;                           // [T][NE]
+  uint8_t* term_s = reinterpret_cast<uint8_t*>(v_s + (size_t)T * NE);  // [T][NE]
+  uint8_t* trunc_s = term_s + (size_t)T * NE;                  // [T][NE]
+  const int tid = threadIdx.x;
+  const int n0 = blockIdx.x * NE;
 
-  const int lane = threadIdx.x;
-  const int n0 = blockIdx.x * kGaeEnvs;
-  if (lane == 0) {
-    mbar_init(&bar, 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-  if (lane == 0) mbar_arrive_expect_tx(&bar, (uint32_t)T * kGaeEnvs * 10u);
-  __syncwarp();
-  for (int t = lane; t < T; t += 32) {
-    const size_t row = (size_t)t * p.N + n0;
-    bulk_g2s(r_s + (size_t)t * kGaeEnvs, p.reward + row, kGaeEnvs * 4, &bar);
-    bulk_g2s(v_s + (size_t)t * kGaeEnvs, p.value + row, kGaeEnvs * 4, &bar);
-    bulk_g2s(term_s + (size_t)t * kGaeEnvs, p.term + row, kGaeEnvs, &bar);
-    bulk_g2s(trunc_s + (size_t)t * kGaeEnvs, p.trunc + row, kGaeEnvs, &bar);
-  }
-  const float boot = p.bootstrap[n0 + lane];
-  if (!mbar_wait_bounded(&bar, 0)) {
-    // The copies did not land in time: report, poison this block's outputs, and leave
-    // without touching shared memory again.
-    if (lane == 0 && p.err) atomicExch(p.err, 1);
-    for (int t = 0; t < T; ++t) {
-      const size_t i = (size_t)t * p.N + n0 + lane;
-      p.adv[i] = __int_as_float(0x7fc00000);
-      p.ret[i] = __int_as_float(0x7fc00000);
+  for (int g = 0; g < kGaeGroups; ++g) {  // group g: t in [t_lo, t_hi), latest steps first
+    const int t_hi = max(T - g * C, 0);
+    const int t_lo = max(t_hi - C, 0);
+    const int pieces = (t_hi - t_lo) * kRow;
+    for (int i = tid; i < pieces; i += kThreads) {
+      const int t = t_lo + i / kRow;
+      int j = i - (t - t_lo) * kRow;
+      const size_t row = (size_t)t * p.N + n0;
+      const int s = t * NE;
+      if (j < kF) {
+        cp_async16(r_s + s + 4 * j, p.reward + row + 4 * j);
+      } else if ((j -= kF) < kF) {
+        cp_async16(v_s + s + 4 * j, p.value + row + 4 * j);
+      } else if ((j -= kF) < kB) {
+        cp_async16(term_s + s + 16 * j, p.term + row + 16 * j);
+      } else {
+        j -= kB;
+        cp_async16(trunc_s + s + 16 * j, p.trunc + row + 16 * j);
+      }
     }
-    return;
+    cp_async_commit();  // possibly empty; every thread commits the same four groups
   }
+
+  // Warp 0 scans, all 32 lanes together; with NE = 16, lanes 16..31 shadow lanes 0..15 and
+  // store nothing.
+  const bool scan = tid < 32;
+  const bool on = tid < NE;
+  const int lane = tid & (NE - 1);
   float adv = 0.f;
-  float next_v = boot;
-  for (int t = T - 1; t >= 0; --t) {
-    const int s = t * kGaeEnvs + lane;
-    const float v = v_s[s];
-    adv = gae_step(r_s[s], v, next_v, (float)term_s[s], (float)trunc_s[s], 1.f, 1.f, adv,
-                   p.gamma, p.glam);
-    const size_t i = (size_t)t * p.N + n0 + lane;
-    p.adv[i] = adv;
-    p.ret[i] = __fadd_rn(adv, v);
-    next_v = v;
+  float next_v = scan ? p.bootstrap[n0 + lane] : 0.f;
+  for (int g = 0; g < kGaeGroups; ++g) {
+    cp_async_wait_pending(kGaeGroups - 1 - g);
+    __syncthreads();  // every thread's copies of group g have landed
+    if (!scan) continue;
+    const int t_hi = max(T - g * C, 0);
+    const int t_lo = max(t_hi - C, 0);
+    int tb = t_hi;
+    for (; tb - kGaeBatch >= t_lo; tb -= kGaeBatch)
+      gae_scan_batch<NE>(p, r_s, v_s, term_s, trunc_s, tb, n0, lane, on, adv, next_v);
+    for (; tb > t_lo; --tb) {  // the remainder of a group, one step at a time
+      const int s = (tb - 1) * NE + lane;
+      const float v = v_s[s];
+      adv = gae_step(r_s[s], v, next_v, (float)term_s[s], (float)trunc_s[s], 1.f, 1.f, adv,
+                     p.gamma, p.glam);
+      if (on) {
+        const size_t i = (size_t)(tb - 1) * p.N + n0 + lane;
+        p.adv[i] = adv;
+        p.ret[i] = __fadd_rn(adv, v);
+      }
+      next_v = v;
+    }
   }
+}
+
+template <int NE>
+int launch_gae_tile(const GaeParams& p, cudaStream_t stream) {
+  const size_t smem = (size_t)p.T * NE * 10;
+  if (smem > 48 * 1024) {
+    BT_CUDA(cudaFuncSetAttribute(gae_tile_kernel<NE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+  }
+  gae_tile_kernel<NE><<<p.N / NE, NE * 8, smem, stream>>>(p);
+  BT_LAUNCH_CHECK("gae_tile_kernel");
+  return BT_OK;
 }
 
 int launch_gae(const GaeParams& p, cudaStream_t stream) {
   if (p.T == 0 || p.N == 0) return BT_OK;
-  const size_t smem = (size_t)p.T * kGaeEnvs * 10;
   const bool aligned =
-      (p.N % kGaeEnvs == 0) && ((uintptr_t)p.reward % 16 == 0) &&
-      ((uintptr_t)p.value % 16 == 0) && ((uintptr_t)p.term % 16 == 0) &&
-      ((uintptr_t)p.trunc % 16 == 0);
-  if (aligned && p.rho == nullptr && p.c == nullptr && smem <= 200 * 1024) {
-    if (smem > 48 * 1024) {
-      BT_CUDA(cudaFuncSetAttribute(gae_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
-    }
-    gae_bulk_kernel<<<p.N / kGaeEnvs, kGaeEnvs, smem, stream>>>(p);
-    BT_LAUNCH_CHECK("gae_bulk_kernel");
-  } else {
-    gae_plain_kernel<<<ceil_div(p.N, 128), 128, 0, stream>>>(p);
-    BT_LAUNCH_CHECK("gae_plain_kernel");
-  }
+      ((uintptr_t)p.reward % 16 == 0) && ((uintptr_t)p.value % 16 == 0) &&
+      ((uintptr_t)p.term % 16 == 0) && ((uintptr_t)p.trunc % 16 == 0);
+  const bool tiled = aligned && p.rho == nullptr && p.c == nullptr;
+  // 32 columns per block when that still gives about two blocks per SM, else 16.
+  if (tiled && p.N % 32 == 0 && p.N / 32 >= 2 * kNumSMs && (size_t)p.T * 320 <= kGaeMaxSmem)
+    return launch_gae_tile<32>(p, stream);
+  if (tiled && p.N % 16 == 0 && (size_t)p.T * 160 <= kGaeMaxSmem)
+    return launch_gae_tile<16>(p, stream);
+  gae_plain_kernel<<<ceil_div(p.N, 128), 128, 0, stream>>>(p);
+  BT_LAUNCH_CHECK("gae_plain_kernel");
   return BT_OK;
 }
 

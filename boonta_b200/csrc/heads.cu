@@ -115,6 +115,28 @@ __device__ __forceinline__ float4 act4(float4 z) {
   return make_float4(act_fwd<A>(z.x), act_fwd<A>(z.y), act_fwd<A>(z.z), act_fwd<A>(z.w));
 }
 
+// Chunk coordinates without integer division in the loops (a division costs several
+// special-function-unit instructions, the unit the activations already keep busy): chunk
+// c = tid + 256 i of a tile with q4 float4 columns per row sits at row r, column q, and the
+// next chunk of the same thread is 256 further on.
+struct ChunkWalk {
+  int r, q, dr, dq, q4;
+  __device__ __forceinline__ ChunkWalk(int q4_) : q4(q4_) {
+    dr = kHeadThreads / q4;
+    dq = kHeadThreads - dr * q4;
+    r = threadIdx.x / q4;
+    q = threadIdx.x - r * q4;
+  }
+  __device__ __forceinline__ void next() {
+    q += dq;
+    r += dr;
+    if (q >= q4) {
+      q -= q4;
+      ++r;
+    }
+  }
+};
+
 // Stage act(pre) of the tile's rows [row0, row0 + 32) into f_s (rows past `live` as 0).
 // Each thread handles float4 chunks c = tid + 256 i; the loads of a batch of eight chunks
 // are all issued before any is used, so their latencies overlap.
@@ -124,24 +146,24 @@ template <int ACT>
 __device__ __forceinline__ void stage_features(const float* pre, int F, int ld, int row0,
                                                int live, float* f_s) {
   const int q4 = F / 4, total = kTileRows * q4;
-  {
-    for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
-      float4 z[kBatch];
+  ChunkWalk w(q4);
+  for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
+    float4 z[kBatch];
+    ChunkWalk at = w;
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i) {
-        const int c = c0 + i * kHeadThreads;
-        const int r = c / q4, q = c - r * q4;
-        z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (c < total && row0 + r < live)
-          z[i] = __ldg(reinterpret_cast<const float4*>(pre + (size_t)(row0 + r) * F) + q);
-      }
+    for (int i = 0; i < kBatch; ++i) {
+      const int c = c0 + i * kHeadThreads;
+      z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < total && row0 + at.r < live)
+        z[i] = __ldg(reinterpret_cast<const float4*>(pre + (size_t)(row0 + at.r) * F) + at.q);
+      at.next();
+    }
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i) {
-        const int c = c0 + i * kHeadThreads;
-        const int r = c / q4, q = c - r * q4;
-        if (c < total)
-          *reinterpret_cast<float4*>(f_s + r * ld + 4 * q) = act4<ACT>(z[i]);
-      }
+    for (int i = 0; i < kBatch; ++i) {
+      const int c = c0 + i * kHeadThreads;
+      if (c < total)
+        *reinterpret_cast<float4*>(f_s + w.r * ld + 4 * w.q) = act4<ACT>(z[i]);
+      w.next();
     }
   }
 }
@@ -156,53 +178,54 @@ __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int 
                                                    float* df, __nv_bfloat16* dfb,
                                                    __nv_bfloat16* dfb_lo) {
   const int q4 = F / 4, total = kTileRows * q4;
-  {
-    for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
-      float4 z[kBatch];
-      if constexpr (Act != BT_ACT_NONE) {
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-          const int c = c0 + i * kHeadThreads;
-          const int r = c / q4, q = c - r * q4;
-          z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (c < total && row0 + r < live)
-            z[i] = __ldg(reinterpret_cast<const float4*>(pre + (size_t)(row0 + r) * F) + q);
-        }
-      }
+  ChunkWalk w(q4);
+  for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
+    float4 z[kBatch];
+    if constexpr (Act != BT_ACT_NONE) {
+      ChunkWalk at = w;
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) {
         const int c = c0 + i * kHeadThreads;
-        const int r = c / q4, q = c - r * q4;
-        const int row = row0 + r;
-        if (c >= total || row >= rows_cap) continue;
-        float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (nj > 1) {
+        z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < total && row0 + at.r < live)
+          z[i] = __ldg(reinterpret_cast<const float4*>(pre + (size_t)(row0 + at.r) * F) + at.q);
+        at.next();
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int c = c0 + i * kHeadThreads;
+      const int r = w.r, q = w.q;
+      w.next();
+      const int row = row0 + r;
+      if (c >= total || row >= rows_cap) continue;
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (nj > 1) {
 #pragma unroll 4
-          for (int j = 0; j < JP; ++j) {
-            const float dj = d_s[r * JP + j];
-            const float4 w = *reinterpret_cast<const float4*>(w_s + (size_t)j * F + 4 * q);
-            g.x = fmaf(dj, w.x, g.x);
-            g.y = fmaf(dj, w.y, g.y);
-            g.z = fmaf(dj, w.z, g.z);
-            g.w = fmaf(dj, w.w, g.w);
-          }
-        } else {
-          const float dj = d_s[r * JP + jcol];
-          const float4 w = *reinterpret_cast<const float4*>(w_s + 4 * q);
-          g = make_float4(dj * w.x, dj * w.y, dj * w.z, dj * w.w);
+        for (int j = 0; j < JP; ++j) {
+          const float dj = d_s[r * JP + j];
+          const float4 wv = *reinterpret_cast<const float4*>(w_s + (size_t)j * F + 4 * q);
+          g.x = fmaf(dj, wv.x, g.x);
+          g.y = fmaf(dj, wv.y, g.y);
+          g.z = fmaf(dj, wv.z, g.z);
+          g.w = fmaf(dj, wv.w, g.w);
         }
-        if constexpr (Act != BT_ACT_NONE) {
-          g.x *= act_dz<Act>(z[i].x);
-          g.y *= act_dz<Act>(z[i].y);
-          g.z *= act_dz<Act>(z[i].z);
-          g.w *= act_dz<Act>(z[i].w);
-        }
-        const size_t e = (size_t)row * F + 4 * q;
-        if (dfb) {
-          store_bf16x4(dfb, dfb_lo, e, g);
-        } else {
-          *reinterpret_cast<float4*>(df + e) = g;
-        }
+      } else {
+        const float dj = d_s[r * JP + jcol];
+        const float4 wv = *reinterpret_cast<const float4*>(w_s + 4 * q);
+        g = make_float4(dj * wv.x, dj * wv.y, dj * wv.z, dj * wv.w);
+      }
+      if constexpr (Act != BT_ACT_NONE) {
+        g.x *= act_dz<Act>(z[i].x);
+        g.y *= act_dz<Act>(z[i].y);
+        g.z *= act_dz<Act>(z[i].z);
+        g.w *= act_dz<Act>(z[i].w);
+      }
+      const size_t e = (size_t)row * F + 4 * q;
+      if (dfb) {
+        store_bf16x4(dfb, dfb_lo, e, g);
+      } else {
+        *reinterpret_cast<float4*>(df + e) = g;
       }
     }
   }
@@ -458,10 +481,10 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
 
     // 4. dL/d pre for the towers
     store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, wj_s, JP, 0, p.d_fpi,
-                           p.d_fpi_b, p.d_fpi_b_lo);
+                                p.d_fpi_b, p.d_fpi_b_lo);
     if (!shared)
       store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, wv_s, 1, A, p.d_fv,
-                             p.d_fv_b, p.d_fv_b_lo);
+                                  p.d_fv_b, p.d_fv_b_lo);
     // 5. head weight gradients
     if constexpr (FUSE) {
       if (tid < F) {

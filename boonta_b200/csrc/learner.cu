@@ -265,11 +265,11 @@ int allocate(bt_learner* L) {
       const int dk = L->rows_cap;
       if (lp.tc) {
         // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1], split over K (the rows) to
-        // fill one wave of CTAs with at least 16 K blocks (1024 rows) per split.
+        // fill one wave of CTAs with at least 8 K blocks (512 rows) per split.
         const int bn = 128;
         const int tiles = ceil_div(lp.kout, 128) * ceil_div(lp.kin + 1, bn);
         const int nkb = ceil_div(L->rows_cap, 64);
-        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 16));
+        int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 8));
         lp.dw_kbps = ceil_div(nkb, splits);
         lp.dw_splits = ceil_div(nkb, lp.dw_kbps);
       } else if (lp.kind == BT_LAYER_CONV3X3) {
@@ -885,6 +885,10 @@ extern "C" int bt_learner_check(bt_learner* L, void* stream) {
   if (code == 2) {
     set_error("a rank's share of a global minibatch exceeded the learner's capacity");
     return BT_ERR_CAPACITY;
+  }
+  if (code == 21) {  // kErrGruBarrier (gru_seq.cu)
+    set_error("a step barrier of the recurrent sequence kernels gave up; its results are invalid");
+    return BT_ERR_TIMEOUT;
   }
   const char* what = code == umma::kErrTimeoutFull    ? "a stage of TMA loads never arrived"
                      : code == umma::kErrTimeoutEmpty ? "a stage was never released by the MMAs"

@@ -66,6 +66,9 @@ struct LayerPlan {
   float* dhp = nullptr;   // dL/d hidden projections [rows, 3H]
   float* dh_direct = nullptr;  // dh * z of the current step [envs, H]
   float* dh_carry = nullptr;   // gradient flowing into the previous step's output [envs, H]
+  // one-launch sequence kernels (gru_seq.cu) usable for the minibatch / the tail sequence
+  bool seq_mb = false, seq_tail = false;
+  unsigned int* seq_bar = nullptr;  // their step-barrier counter
   float* wi_part = nullptr;    // split partials of d[W_i; b_i], dW_h, db_hn
   float* wh_part = nullptr;
   float* bhn_part = nullptr;

@@ -83,7 +83,8 @@ constexpr int kNoAllocMaxDevices = 64;
 __device__ __align__(256) double g_noalloc_scratch[kNoAllocChunks];
 
 // Device address of g_noalloc_scratch per device, looked up once with that device current
-// (host code cannot use the symbol itself as a device pointer).
+// (host code cannot use the symbol itself as a device pointer). The lookup happens in the
+// first call on each device, which should therefore come before any stream capture there.
 void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 std::mutex g_noalloc_mutex;
 

@@ -26,6 +26,30 @@ namespace bt {
 
 int comm_allreduce_f64(Comm* c, double* buf, size_t n, cudaStream_t stream);
 
+// gru_seq.cu
+struct GruSeqParams {
+  int T, H, envs;
+  const int* env_count;
+  const float* xp;
+  const float* wh;
+  const float* bhn;
+  const uint8_t* reset;
+  float* hin;
+  float* h;
+  float* gr;
+  float* gz;
+  float* gn;
+  float* ghn;
+  const float* dhs;
+  float* dxp;
+  float* dhp;
+  unsigned int* bar;
+  int* err;
+};
+int gru_seq_supported(int envs, int H, bool* ok);
+int launch_gru_seq_forward(const GruSeqParams& p, cudaStream_t s);
+int launch_gru_seq_backward(const GruSeqParams& p, cudaStream_t s);
+
 namespace {
 
 // Row metadata of an env minibatch: idx[e*T + t] = t*N + env[e]; reset flags from
@@ -157,6 +181,30 @@ int pick_splits_k(int M, int N, int K) {
 
 LayerPlan& gru_layer(bt_learner* L) { return L->towers[0].layers.back(); }
 
+GruSeqParams seq_params(bt_learner* L, LayerPlan& g, const int* env_count, int envs, int T) {
+  GruSeqParams q{};
+  q.T = T;
+  q.H = g.hidden;
+  q.envs = envs;
+  q.env_count = env_count;
+  q.xp = g.xp;
+  q.wh = L->params + g.wh_off;
+  q.bhn = L->params + g.bhn_off;
+  q.reset = L->rnn_reset;
+  q.hin = g.hin;
+  q.h = g.h;
+  q.gr = g.gr;
+  q.gz = g.gz;
+  q.gn = g.gn;
+  q.ghn = g.ghn;
+  q.dhs = g.d_pre;
+  q.dxp = g.dxp;
+  q.dhp = g.dhp;
+  q.bar = g.seq_bar;
+  q.err = L->err_d;
+  return q;
+}
+
 // Forward of the GRU over `envs` sequences of length T (rows e*T + t), input x [rows, kin].
 int gru_forward(bt_learner* L, LayerPlan& g, const float* x, const float* carry, const int* env,
                 const int* env_count, const int* rows_live, int envs, int T, cudaStream_t s) {
@@ -171,6 +219,11 @@ int gru_forward(bt_learner* L, LayerPlan& g, const float* x, const float* carry,
   BT_K(L, kProfMisc, s, launch_elementwise(gru_init_kernel, (int64_t)envs * H, s, carry, env,
                                            env_count, envs, T, H, (const uint8_t*)L->rnn_reset,
                                            g.hin));
+  if (envs == L->units_cap ? g.seq_mb : (envs == L->N && T == 2 && g.seq_tail)) {
+    // the whole recurrence in one launch
+    BT_K(L, kProfGemmFwd, s, launch_gru_seq_forward(seq_params(L, g, env_count, envs, T), s));
+    return BT_OK;
+  }
   for (int t = 0; t < T; ++t) {
     ARows a{g.hin + (size_t)t * H, nullptr, T * H, H};
     BRows b{L->params + g.wh_off, 3 * H, H};
@@ -186,9 +239,27 @@ int gru_forward(bt_learner* L, LayerPlan& g, const float* x, const float* carry,
   return BT_OK;
 }
 
+int gru_backward_steps(bt_learner* L, LayerPlan& g, const int* env_count, int envs, int T,
+                       cudaStream_t s);
+int gru_weight_grads(bt_learner* L, LayerPlan& g, LayerPlan& prev, const int* rows_live,
+                     int rows, cudaStream_t s);
+
 int gru_backward(bt_learner* L, LayerPlan& g, LayerPlan& prev, const int* env_count,
                  const int* rows_live, int envs, int T, cudaStream_t s) {
   const int H = g.hidden, rows = envs * T;
+  if (envs == L->units_cap && g.seq_mb) {
+    // backward through time in one launch
+    BT_K(L, kProfGemmDx, s, launch_gru_seq_backward(seq_params(L, g, env_count, envs, T), s));
+  } else {
+    BT_TRY(gru_backward_steps(L, g, env_count, envs, T, s));
+  }
+  BT_TRY(gru_weight_grads(L, g, prev, rows_live, rows, s));
+  return BT_OK;
+}
+
+int gru_backward_steps(bt_learner* L, LayerPlan& g, const int* env_count, int envs, int T,
+                       cudaStream_t s) {
+  const int H = g.hidden;
   for (int t = T - 1; t >= 0; --t) {
     BT_K(L, kProfMisc, s, launch_elementwise(gru_bwd_step_kernel, (int64_t)envs * H, s, t, T, H,
                                              envs, env_count, (const float*)g.d_pre,
@@ -203,6 +274,12 @@ int gru_backward(bt_learner* L, LayerPlan& g, LayerPlan& prev, const int* env_co
       BT_K(L, kProfGemmDx, s, launch_gemm_simt_small<16>(a, b, ep, envs, H, 3 * H, s, env_count));
     }
   }
+  return BT_OK;
+}
+
+int gru_weight_grads(bt_learner* L, LayerPlan& g, LayerPlan& prev, const int* rows_live,
+                     int rows, cudaStream_t s) {
+  const int H = g.hidden;
   // weight gradients over all live rows
   {
     ACols a{prev.h, nullptr, g.kin, g.kin};  // [x, 1]^T dxp -> [W_i; b_i]
@@ -317,6 +394,10 @@ int allocate_gru(bt_learner* L, LayerPlan& g) {
                        (int64_t)(g.kin + 1) * 3 * H, g.wi_off});
   L->segs_h.push_back({g.wh_part, g.wh_splits, H * 3 * H, (int64_t)H * 3 * H, g.wh_off});
   L->segs_h.push_back({g.bhn_part, g.bhn_splits, H, (int64_t)H, g.bhn_off});
+  // one-launch sequence kernels where every CTA of their grid fits on the GPU at once
+  BT_TRY(gru_seq_supported(E, H, &g.seq_mb));
+  BT_TRY(gru_seq_supported(L->N, H, &g.seq_tail));
+  BT_TRY(dalloc(L, &g.seq_bar, 1));
   // row metadata
   BT_TRY(dalloc(L, &L->rnn_idx, R));
   BT_TRY(dalloc(L, &L->rnn_reset, R));

@@ -265,7 +265,8 @@ BT_API int bt_clip_adam(float* params, float* mu, float* nu, const float* grads,
  * FFI custom call, which runs after XLA has reserved most of the GPU for its own pool.
  * Scratch is a fixed 128 KB array compiled into the library (resident on every GPU that
  * loads it until exit), so n is limited to 134,217,728 elements; larger n is rejected with
- * BT_ERR_INVALID. The first call on a device looks the array's address up once. All calls
+ * BT_ERR_INVALID. The first call on a device looks the array's address up once (a CUDA
+ * runtime query), so make that first call before any stream capture on the device. All calls
  * share the array: calls whose GPU work overlaps race and must be ordered by the caller. */
 BT_API int bt_clip_adam_noalloc(float* params, float* mu, float* nu, const float* grads,
                                 int64_t n, int32_t count, const bt_optimizer* opt, void* stream);

@@ -37,8 +37,11 @@ def test_cuda_gae_matches_the_reference_known_answers(case):
         np.testing.assert_array_equal(adv2, adv)
 
 
+# plain kernel: (1, 1), (7, 5), (3, 33), (1500, 16) (too long for shared memory); tiled, 16
+# columns per block: (128, 16), (64, 8192), (128, 4096), (64, 4096), (33, 96), (500, 64),
+# (512, 48), (513, 32), (2, 48); 32 columns: (16, 9728)
 SHAPES = [(1, 1), (7, 5), (3, 33), (128, 16), (64, 8192), (128, 4096), (64, 4096), (33, 96),
-          (500, 64)]
+          (500, 64), (512, 48), (513, 32), (16, 9728), (1500, 16), (2, 48)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=[f"{t}x{n}" for t, n in SHAPES])
