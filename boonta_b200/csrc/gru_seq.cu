@@ -5,10 +5,9 @@
 // instead of two launches (a GEMM and an elementwise kernel) per step.
 //
 // Work split (both directions): CTA (eb, ub) owns envs [32 eb, 32 eb + 32) of the minibatch
-// and hidden units [16 ub, 16 ub + 16); its 256 threads each own two envs x one unit, so
-// the three gates of a unit (r, z, n) meet in one thread and the gate math follows the
-// product without another pass. The CTA keeps its slice of W_h in shared memory for the
-// whole sequence.
+// and hidden units [16 ub, 16 ub + 16); its 256 threads each own two envs x one unit for
+// the gate math, so the three gates of a unit (r, z, n) meet in one thread. The CTA keeps
+// its slice of W_h in shared memory for the whole sequence.
 //
 //   forward step t   stage the 32 carry rows hin_t (all H) from L2; hp = hin_t W_h for the
 //                    CTA's 48 gate columns (fp32 FMA); gates, h_t, the saved r, z, n,
@@ -172,6 +171,10 @@ __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_forward_kernel(GruS
   }
 }
 
+// Backward thread layout: thread (env pair, unit pair, kh) with kh = lane & 1; for the
+// gate gradients it owns envs 2 ep, 2 ep + 1 of unit 2 up + kh, and in the carry product it
+// sums the float4 columns of parity kh for both units of its pair (four accumulators, two
+// dhp and two W_h rows per float4 step), the two parities then combined with a shuffle.
 __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_backward_kernel(GruSeqParams p) {
   extern __shared__ __align__(16) float sm[];
   __shared__ int s_fail;
@@ -179,8 +182,10 @@ __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_backward_kernel(Gru
   float* w_s = sm;                              // [16][3H + 4]: rows of W_h
   float* d_s = sm + kGruSeqUnits * ld;          // [32][3H + 4]: dhp rows of the step
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int u_l = 8 * (warp & 1) + (lane & 7);
-  const int e_l = 2 * (4 * (warp >> 1) + (lane >> 3));
+  const int kh = lane & 1;
+  const int up = ((lane >> 1) & 3) + 4 * (warp & 1);  // unit pair 0..7
+  const int u_l = 2 * up + kh;                        // the thread's unit (gate gradients)
+  const int e_l = 2 * ((lane >> 3) + 4 * (warp >> 1));
   const int e0 = blockIdx.x * kGruSeqEnvs;
   const int U = blockIdx.y * kGruSeqUnits + u_l;
   const int live = live_rows(p.env_count, p.envs);
@@ -230,28 +235,39 @@ __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_backward_kernel(Gru
       *reinterpret_cast<float4*>(d_s + e * ld + 4 * q) = v;
     }
     __syncthreads();
-    float acc0 = 0.f, acc1 = 0.f;
+    // acc[env j][unit of the pair v]
+    float acc[2][2] = {};
     const float* a0 = d_s + e_l * ld;
     const float* a1 = a0 + ld;
-    const float* w = w_s + u_l * ld;
+    const float* w0 = w_s + (2 * up) * ld;
+    const float* w1 = w0 + ld;
 #pragma unroll 4
-    for (int c = 0; c < H3; c += 4) {
+    for (int c = 4 * kh; c < H3; c += 8) {
       const float4 x0 = *reinterpret_cast<const float4*>(a0 + c);
       const float4 x1 = *reinterpret_cast<const float4*>(a1 + c);
-      const float4 wv = *reinterpret_cast<const float4*>(w + c);
-      acc0 = fmaf(x0.x, wv.x, acc0);
-      acc0 = fmaf(x0.y, wv.y, acc0);
-      acc0 = fmaf(x0.z, wv.z, acc0);
-      acc0 = fmaf(x0.w, wv.w, acc0);
-      acc1 = fmaf(x1.x, wv.x, acc1);
-      acc1 = fmaf(x1.y, wv.y, acc1);
-      acc1 = fmaf(x1.z, wv.z, acc1);
-      acc1 = fmaf(x1.w, wv.w, acc1);
+      const float4 v0 = *reinterpret_cast<const float4*>(w0 + c);
+      const float4 v1 = *reinterpret_cast<const float4*>(w1 + c);
+#define BT_GRU_DOT4(A, W, ACC)  \
+  ACC = fmaf(A.x, W.x, ACC);     \
+  ACC = fmaf(A.y, W.y, ACC);     \
+  ACC = fmaf(A.z, W.z, ACC);     \
+  ACC = fmaf(A.w, W.w, ACC);
+      BT_GRU_DOT4(x0, v0, acc[0][0]);
+      BT_GRU_DOT4(x0, v1, acc[0][1]);
+      BT_GRU_DOT4(x1, v0, acc[1][0]);
+      BT_GRU_DOT4(x1, v1, acc[1][1]);
+#undef BT_GRU_DOT4
+    }
+    // combine the two column parities; this thread keeps its own unit (2 up + kh)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int v = 0; v < 2; ++v) acc[j][v] += __shfl_xor_sync(0xffffffffu, acc[j][v], 1);
     }
     // the carry gradient into step t - 1 (zero across a reset at step t)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float v = j == 0 ? acc0 : acc1;
+      const float v = kh ? acc[j][1] : acc[j][0];
       carry[j] = on[j] && !p.reset[(size_t)(e0 + e_l + j) * T + t] ? v + direct[j] : 0.f;
     }
     __syncthreads();  // d_s is restaged in the next step

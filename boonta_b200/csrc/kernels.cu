@@ -51,12 +51,82 @@ __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int
   }
 }
 
+// Vectorised forward for n = 128 NV (NV <= 8): lane `l` owns the float4 columns l, l + 32, ...
+// of its warp's row, read once into registers (the scalar kernel above reads each row twice).
+template <int NV>
+__global__ void __launch_bounds__(256) ln_forward_vec_kernel(
+    const float* z, const float* sb, int rows, int n, int act, float* y, float* h,
+    __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb, float* mean_out, float* rstd_out,
+    const int* count) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
+  if (row >= live_rows(count, rows)) return;
+  const float4* zr = reinterpret_cast<const float4*>(z + (size_t)row * n);
+  float4 v[NV];
+  float s = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = zr[lane + 32 * i];
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
+    s2 += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  s = warp_sum(s);
+  s2 = warp_sum(s2);
+  const float mean = s / n;
+  const float var = fmaxf(s2 / n - mean * mean, 0.f);
+  const float r = rsqrtf(var + kLnEps);
+  const float4* sc = reinterpret_cast<const float4*>(sb);
+  const float4* bi = reinterpret_cast<const float4*>(sb + n);
+  with_act(act, [&](auto tag) {
+    constexpr int A = decltype(tag)::value;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int q = lane + 32 * i;
+      const float4 a = __ldg(sc + q), b = __ldg(bi + q);
+      float4 yv;
+      yv.x = (v[i].x - mean) * (r * a.x) + b.x;
+      yv.y = (v[i].y - mean) * (r * a.y) + b.y;
+      yv.z = (v[i].z - mean) * (r * a.z) + b.z;
+      yv.w = (v[i].w - mean) * (r * a.w) + b.w;
+      reinterpret_cast<float4*>(y + (size_t)row * n)[q] = yv;
+      const float4 hv = make_float4(act_fwd<A>(yv.x), act_fwd<A>(yv.y), act_fwd<A>(yv.z),
+                                    act_fwd<A>(yv.w));
+      if (h) reinterpret_cast<float4*>(h + (size_t)row * n)[q] = hv;
+      if (hb) store_bf16x4(hb, hb_lo, (size_t)row * ldhb + 4 * q, hv);
+    }
+  });
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = r;
+  }
+}
+
 int launch_ln_forward(const float* z, const float* scale_bias, int rows, int n, int act, float* y,
                       float* h, __nv_bfloat16* hb, __nv_bfloat16* hb_lo, int ldhb, float* mean,
                       float* rstd, const int* count, cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
-  BT_CUDA(launch_pdl(ln_forward_kernel, dim3(ceil_div(rows * 32, 256)), dim3(256), 0, stream, z,
-                     scale_bias, rows, n, act, y, h, hb, hb_lo, ldhb, mean, rstd, count));
+  const dim3 grid(ceil_div(rows * 32, 256));
+  const bool vec = n % 128 == 0 && n <= 1024 && (uintptr_t)z % 16 == 0 &&
+                   (uintptr_t)scale_bias % 16 == 0 && (uintptr_t)y % 16 == 0 &&
+                   (uintptr_t)h % 16 == 0 && (!hb || (ldhb % 4 == 0 && (uintptr_t)hb % 8 == 0 &&
+                                                      (uintptr_t)hb_lo % 8 == 0));
+  if (vec) {
+    switch (n / 128) {
+#define BT_LN_FWD(NV)                                                                          \
+  case NV:                                                                                     \
+    BT_CUDA(launch_pdl(ln_forward_vec_kernel<NV>, grid, dim3(256), 0, stream, z, scale_bias,   \
+                       rows, n, act, y, h, hb, hb_lo, ldhb, mean, rstd, count));               \
+    return BT_OK;
+      BT_LN_FWD(1) BT_LN_FWD(2) BT_LN_FWD(3) BT_LN_FWD(4)
+      BT_LN_FWD(5) BT_LN_FWD(6) BT_LN_FWD(7) BT_LN_FWD(8)
+#undef BT_LN_FWD
+      default: break;
+    }
+  }
+  BT_CUDA(launch_pdl(ln_forward_kernel, grid, dim3(256), 0, stream, z, scale_bias, rows, n, act,
+                     y, h, hb, hb_lo, ldhb, mean, rstd, count));
   return BT_OK;
 }
 
@@ -133,11 +203,115 @@ __global__ void __launch_bounds__(256) ln_backward_kernel(const float* d_y, cons
   }
 }
 
+// Vectorised backward for n = 128 NV (NV <= 8): as ln_backward_kernel, with each row's d_y
+// and z read once into registers as float4 (lane l owns float4 columns l, l + 32, ...). The
+// column partial sums are reduced over the block's warps 128 columns at a time.
+template <int NV>
+__global__ void __launch_bounds__(256) ln_backward_vec_kernel(
+    const float* d_y, const float* z, const float* mean, const float* rstd, const float* scale,
+    int rows, int n, float* d_z, __nv_bfloat16* d_zb, __nv_bfloat16* d_zb_lo, float* partials,
+    const int* count) {
+  __shared__ float4 red[8][2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int warps_total = gridDim.x * 8;
+  const int live = live_rows(count, rows);
+  float4 sc[NV], ds[NV], db[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    sc[i] = __ldg(reinterpret_cast<const float4*>(scale) + lane + 32 * i);
+    ds[i] = db[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int row = blockIdx.x * 8 + warp; row < live; row += warps_total) {
+    const float4* dyr = reinterpret_cast<const float4*>(d_y + (size_t)row * n);
+    const float4* zr = reinterpret_cast<const float4*>(z + (size_t)row * n);
+    const float mu = mean[row], r = rstd[row];
+    float4 dy[NV], xh[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      dy[i] = dyr[lane + 32 * i];
+      xh[i] = zr[lane + 32 * i];
+    }
+    float m1 = 0.f, m2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      xh[i].x = (xh[i].x - mu) * r;
+      xh[i].y = (xh[i].y - mu) * r;
+      xh[i].z = (xh[i].z - mu) * r;
+      xh[i].w = (xh[i].w - mu) * r;
+      const float dx0 = dy[i].x * sc[i].x, dx1 = dy[i].y * sc[i].y;
+      const float dx2 = dy[i].z * sc[i].z, dx3 = dy[i].w * sc[i].w;
+      m1 += dx0 + dx1 + dx2 + dx3;
+      m2 += dx0 * xh[i].x + dx1 * xh[i].y + dx2 * xh[i].z + dx3 * xh[i].w;
+      ds[i].x += dy[i].x * xh[i].x;
+      ds[i].y += dy[i].y * xh[i].y;
+      ds[i].z += dy[i].z * xh[i].z;
+      ds[i].w += dy[i].w * xh[i].w;
+      db[i].x += dy[i].x;
+      db[i].y += dy[i].y;
+      db[i].z += dy[i].z;
+      db[i].w += dy[i].w;
+    }
+    m1 = warp_sum(m1) / n;
+    m2 = warp_sum(m2) / n;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float4 g;
+      g.x = r * (dy[i].x * sc[i].x - m1 - xh[i].x * m2);
+      g.y = r * (dy[i].y * sc[i].y - m1 - xh[i].y * m2);
+      g.z = r * (dy[i].z * sc[i].z - m1 - xh[i].z * m2);
+      g.w = r * (dy[i].w * sc[i].w - m1 - xh[i].w * m2);
+      const size_t e = (size_t)row * n + 4 * (lane + 32 * i);
+      if (d_z) *reinterpret_cast<float4*>(d_z + e) = g;
+      if (d_zb) store_bf16x4(d_zb, d_zb_lo, e, g);
+    }
+  }
+  // Block reduction of the column partial sums in warp order, 128 columns at a time: thread
+  // t < 64 sums the d-scale float4 of lanes t (columns 4 (t + 32 i) ...), t >= 64 the d-bias.
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    __syncthreads();
+    red[warp][0][lane] = ds[i];
+    red[warp][1][lane] = db[i];
+    __syncthreads();
+    if (threadIdx.x < 64) {
+      const int which = threadIdx.x >> 5, l = threadIdx.x & 31;
+      float4 a = red[0][which][l];
+      for (int w = 1; w < 8; ++w) {
+        const float4 b = red[w][which][l];
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+      }
+      reinterpret_cast<float4*>(partials + (size_t)blockIdx.x * 2 * n + which * n)[l + 32 * i] = a;
+    }
+  }
+}
+
 int launch_ln_backward(const float* d_y, const float* z, const float* mean, const float* rstd,
                        const float* scale, int rows, int n, float* d_z, __nv_bfloat16* d_zb,
                        __nv_bfloat16* d_zb_lo, float* partials, int blocks, const int* count,
                        cudaStream_t stream) {
   BT_CHECK_ARG(n <= kLnMaxCols, "layernorm width %d > %d", n, kLnMaxCols);
+  const bool vec = n % 128 == 0 && (uintptr_t)d_y % 16 == 0 && (uintptr_t)z % 16 == 0 &&
+                   (uintptr_t)scale % 16 == 0 && (uintptr_t)d_z % 16 == 0 &&
+                   (uintptr_t)partials % 16 == 0 && (uintptr_t)d_zb % 8 == 0 &&
+                   (uintptr_t)d_zb_lo % 8 == 0;
+  if (vec) {
+    switch (n / 128) {
+#define BT_LN_BWD(NV)                                                                         \
+  case NV:                                                                                    \
+    ln_backward_vec_kernel<NV><<<blocks, 256, 0, stream>>>(d_y, z, mean, rstd, scale, rows, n, \
+                                                           d_z, d_zb, d_zb_lo, partials,      \
+                                                           count);                            \
+    BT_LAUNCH_CHECK("ln_backward_vec_kernel");                                                \
+    return BT_OK;
+      BT_LN_BWD(1) BT_LN_BWD(2) BT_LN_BWD(3) BT_LN_BWD(4)
+      BT_LN_BWD(5) BT_LN_BWD(6) BT_LN_BWD(7) BT_LN_BWD(8)
+#undef BT_LN_BWD
+      default: break;
+    }
+  }
   ln_backward_kernel<<<blocks, 256, 0, stream>>>(d_y, z, mean, rstd, scale, rows, n, d_z, d_zb,
                                                  d_zb_lo, partials, count);
   BT_LAUNCH_CHECK("ln_backward_kernel");
