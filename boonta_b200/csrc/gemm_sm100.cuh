@@ -38,11 +38,13 @@ constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each on half t
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13,
               kErrTimeoutEpiIn = 14;
-// Store epilogues (kTma): each epilogue warp owns an 8 KB piece of the (then idle) stage
-// ring: a 32 x 32 fp32 sub-tile (4 KB, 128-byte swizzle) and two 32 x 32 bf16 sub-tiles
-// (2 KB each, 64-byte swizzle), written in the swizzled order the tensor maps expect and
-// sent out by TMA stores.
-constexpr int kEpiWarpBytes = 8192;
+// Store epilogues (kTma): each epilogue warp owns 4 KB of shared memory that holds, one
+// after the other, the 32 x 32 fp32 input sub-tile (dX), the fp32 output sub-tile (128-byte
+// swizzle) and the two 32 x 32 bf16 output sub-tiles (2 KB each, 64-byte swizzle), written in
+// the swizzled order the tensor maps expect and sent out by TMA stores.
+constexpr int kEpiWarpBytes = 4096;
+// Dynamic shared memory per CTA on sm_100 (227 KB).
+constexpr int kMaxSmem = 227 * 1024;
 
 // Shared-memory budget: a ring of stages of A (and, in the split mode, A_lo) and B (B_lo)
 // tiles, each stage 1024-byte aligned. The ring is sized so that two to three CTAs fit on
@@ -359,13 +361,51 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0 && s_fail && sh.err) atomicExch(sh.err, s_fail);
 }
 
+// Swizzled staging of one thread's row of a 32 x 32 sub-tile (thread = row `lane`). The
+// orders are the TMA engine's: 128-byte swizzle for fp32 rows (16-byte chunk j of row r at
+// chunk j ^ (r % 8)), 64-byte swizzle for bf16 rows (chunk j at j ^ ((r / 2) % 4)); both keep
+// the warp's 16-byte shared stores free of bank conflicts.
+__device__ __forceinline__ void stage_row_f32(uint8_t* tile, int lane, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+__device__ __forceinline__ float4 load_row_f32(const uint8_t* tile, int lane, int j) {
+  return *reinterpret_cast<const float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+// bf16 of v (hi) and, when `lo` is set, of the remainders v - hi.
+__device__ __forceinline__ void stage_row_bf16(uint8_t* hi, uint8_t* lo, int lane,
+                                               const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = v[8 * j + 2 * i], b = v[8 * j + 2 * i + 1];
+      h[i] = pack_bf16(a, b);
+      if (lo) {
+        const __nv_bfloat162 hp = *reinterpret_cast<__nv_bfloat162*>(&h[i]);
+        l[i] = pack_bf16(a - __low2float(hp), b - __high2float(hp));
+      }
+    }
+    const int off = lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    if (lo) *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 // ---- persistent kernel with store epilogues ------------------------------------------------
 // One CTA per SM walks the output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... (N tile
 // fastest, so the CTAs running at the same time share the A row block through L2). The
 // accumulator is double-buffered in TMEM (2 x BN columns): the MMA warp fills buffer i % 2
 // while the epilogue warps drain the other, so a tile's epilogue overlaps the next tile's
-// main loop. The stage ring runs on across tiles; the epilogue has its own 64 KB of shared
-// memory (8 KB per warp, kEpiWarpBytes). Barriers: full/empty per stage (TMA -> MMA ->
+// main loop. The stage ring runs on across tiles; the epilogue has its own 32 KB of shared
+// memory (4 KB per warp, kEpiWarpBytes), and the ring takes what is left. Barriers: full/empty per stage (TMA -> MMA ->
 // TMA), acc_full per buffer (MMA commit -> epilogue), acc_empty per buffer (the eight
 // epilogue warps -> MMA, after their last tcgen05.ld of the buffer), and one input barrier
 // per epilogue warp for the dX pre-activation tile. Every wait is bounded; a role that
@@ -377,7 +417,7 @@ struct PCfg {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = (kABytes + kBBytes) * (X3 ? 2 : 1);
   static constexpr int kEpiBytes = kEpiWarps * kEpiWarpBytes;
-  static constexpr int kFit = (224 * 1024 - kEpiBytes - 2048) / kStageBytes;
+  static constexpr int kFit = (kMaxSmem - kEpiBytes - 1024 /*align*/ - 256) / kStageBytes;
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmem = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 256;
@@ -527,15 +567,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     uint8_t* wbuf = epi_smem + (warp - 2) * kEpiWarpBytes;
     uint64_t* ibar = &epi_in[warp - 2];
-    uint8_t* in_f32 = wbuf;
-    uint8_t* out_f32 = wbuf + (Epi::kIn ? 4096 : 0);
-    uint8_t* out_hi = wbuf + 4096;
-    uint8_t* out_lo = wbuf + 6144;
     const bool load_in = Epi::kIn && epi.uses_in();
     constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
     const int c_begin = half * kHalf, c_end = min(BN, (half + 1) * kHalf);
     int loads = 0;        // input tiles loaded by this warp (parity of ibar)
-    bool pending = false;  // stores committed from this warp's staging buffers
+    bool pending = false;  // stores committed from this warp's staging buffer
     int i = 0;
     for (int t = blockIdx.x; t < tiles && !failed(); t += gridDim.x, ++i) {
       const int b = i & 1;
@@ -549,13 +585,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = m0 + q * 32;
       const bool live = row0 + lane < M;
       bool released = false;
+      bool broke = false;
       for (int c = c_begin; c < c_end; c += 32) {
         const int col0 = n0 + c;
         const bool last = c + 32 >= c_end || col0 + 32 >= sh.N;
         if (col0 >= sh.N) break;
+        if (pending) {  // earlier stores have read the staging buffer
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          pending = false;
+        }
         if (load_in && lane == 0) {
           mbar_arrive_expect_tx(ibar, 32 * 32 * 4);
-          tma_load_2d(in_f32, &epi.in_map, col0, row0, ibar);
+          tma_load_2d(wbuf, &epi.in_map, col0, row0, ibar);
         }
         float v[32];
         tmem_ld32(tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
@@ -571,21 +613,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!got) {
             if (lane == 0) atomicExch(&s_fail, kErrTimeoutEpiIn);
             mbar_wait_bounded(ibar, (loads - 1) & 1);  // let the copy land before leaving
+            broke = true;
             break;
           }
         }
-        if (pending) {
-          if (lane == 0) bulk_wait_read_all();  // earlier stores have read the staging tiles
+        epi.prep(v, wbuf, lane, col0, live, sh.N);
+        __syncwarp();  // the input tile is consumed before the buffer is overwritten
+        if (epi.has_f32) {
+          stage_row_f32(wbuf, lane, v);
+          fence_proxy_async_smem();  // generic-proxy smem writes before the async proxy reads
           __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&epi.f32_map, wbuf, col0, row0);
+            bulk_commit();
+          }
+          if (epi.has_hi) {
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+          }
         }
-        epi.stage(v, in_f32, out_f32, out_hi, out_lo, lane, col0, live, sh.N);
-        fence_proxy_async_smem();  // generic-proxy smem writes before the async proxy reads
-        __syncwarp();
-        if (lane == 0) {
-          if (epi.has_f32) tma_store_2d(&epi.f32_map, out_f32, col0, row0);
-          if (epi.has_hi) tma_store_2d(&epi.hi_map, out_hi, col0, row0);
-          if (epi.has_lo) tma_store_2d(&epi.lo_map, out_lo, col0, row0);
-          bulk_commit();
+        if (epi.has_hi) {
+          epi.post(v);
+          stage_row_bf16(wbuf, epi.has_lo ? wbuf + 2048 : nullptr, lane, v);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&epi.hi_map, wbuf, col0, row0);
+            if (epi.has_lo) tma_store_2d(&epi.lo_map, wbuf + 2048, col0, row0);
+            bulk_commit();
+          }
         }
         pending = true;
       }
@@ -593,6 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_before_sync();
         if (lane == 0) mbar_arrive(&acc_empty[b]);
       }
+      if (broke) break;
     }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
@@ -615,44 +672,6 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bflo
 // Staged epilogues (kStaged) see one element at a time with consecutive lanes on
 // consecutive columns; unstaged ones see a thread's 32 consecutive columns of one row.
 
-// Swizzled staging of one thread's row of a 32 x 32 sub-tile (thread = row `lane`). The
-// orders are the TMA engine's: 128-byte swizzle for fp32 rows (16-byte chunk j of row r at
-// chunk j ^ (r % 8)), 64-byte swizzle for bf16 rows (chunk j at j ^ ((r / 2) % 4)); both keep
-// the warp's 16-byte shared stores free of bank conflicts.
-__device__ __forceinline__ void stage_row_f32(uint8_t* tile, int lane, const float (&v)[32]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    *reinterpret_cast<float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
-__device__ __forceinline__ float4 load_row_f32(const uint8_t* tile, int lane, int j) {
-  return *reinterpret_cast<const float4*>(tile + lane * 128 + ((j ^ (lane & 7)) << 4));
-}
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&p);
-}
-// bf16 of v (hi) and, when `lo` is set, of the remainders v - hi.
-__device__ __forceinline__ void stage_row_bf16(uint8_t* hi, uint8_t* lo, int lane,
-                                               const float (&v)[32]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = v[8 * j + 2 * i], b = v[8 * j + 2 * i + 1];
-      h[i] = pack_bf16(a, b);
-      if (lo) {
-        const __nv_bfloat162 hp = *reinterpret_cast<__nv_bfloat162*>(&h[i]);
-        l[i] = pack_bf16(a - __low2float(hp), b - __high2float(hp));
-      }
-    }
-    const int off = lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4);
-    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-    if (lo) *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
-  }
-}
-
 // Forward: z = acc + bias; stores z (fp32, when has_f32) and h = act(z) as bf16 (split into
 // hi/lo halves when has_lo) through TMA. Maps: f32_map over z (fp32, box 32 x 32, 128-byte
 // swizzle), hi_map / lo_map over the bf16 outputs (box 32 x 32, 64-byte swizzle).
@@ -667,8 +686,9 @@ struct EpiFwd {
   int act;
   bool has_f32, has_hi, has_lo;
   __device__ __forceinline__ bool uses_in() const { return false; }
-  __device__ __forceinline__ void stage(float (&v)[32], const uint8_t*, uint8_t* of, uint8_t* oh,
-                                        uint8_t* ol, int lane, int col0, bool live, int N) const {
+  // v = acc + bias (zero for rows past the live count): the fp32 output z
+  __device__ __forceinline__ void prep(float (&v)[32], const uint8_t*, int, int col0, bool live,
+                                       int N) const {
     if (col0 + 32 <= N) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -686,14 +706,13 @@ struct EpiFwd {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = 0.f;
     }
-    if (has_f32) stage_row_f32(of, lane, v);
-    if (has_hi) {
-      with_act(act, [&](auto tag) {
+  }
+  // the bf16 output h = act(z)
+  __device__ __forceinline__ void post(float (&v)[32]) const {
+    with_act(act, [&](auto tag) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = act_fwd<decltype(tag)::value>(v[j]);
-      });
-      stage_row_bf16(oh, has_lo ? ol : nullptr, lane, v);
-    }
+      for (int j = 0; j < 32; ++j) v[j] = act_fwd<decltype(tag)::value>(v[j]);
+    });
   }
 };
 
@@ -710,9 +729,9 @@ struct EpiDx {
   int act;
   bool has_f32, has_hi, has_lo;
   __device__ __forceinline__ bool uses_in() const { return act != BT_ACT_NONE; }
-  __device__ __forceinline__ void stage(float (&v)[32], const uint8_t* in, uint8_t* of,
-                                        uint8_t* oh, uint8_t* ol, int lane, int, bool live,
-                                        int) const {
+  // g = acc * act'(pre) with pre from the input tile (zero for rows past the live count)
+  __device__ __forceinline__ void prep(float (&v)[32], const uint8_t* in, int lane, int,
+                                       bool live, int) const {
     with_act(act, [&](auto tag) {
       constexpr int A = decltype(tag)::value;
       if constexpr (A != BT_ACT_NONE) {
@@ -730,9 +749,8 @@ struct EpiDx {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = 0.f;
     }
-    if (has_f32) stage_row_f32(of, lane, v);
-    if (has_hi) stage_row_bf16(oh, has_lo ? ol : nullptr, lane, v);
   }
+  __device__ __forceinline__ void post(float (&)[32]) const {}
 };
 
 // dW^T tile: acc[m = output feature][n = input feature (bias row last)] stored transposed

@@ -5,19 +5,22 @@
 // instead of two launches (a GEMM and an elementwise kernel) per step.
 //
 // Work split (both directions): CTA (eb, ub) owns envs [32 eb, 32 eb + 32) of the minibatch
-// and hidden units [16 ub, 16 ub + 16); its 256 threads each own two envs x one unit for
-// the gate math, so the three gates of a unit (r, z, n) meet in one thread. The CTA keeps
-// its slice of W_h in shared memory for the whole sequence.
+// and hidden units [16 ub, 16 ub + 16). The per-step products run on the tensor cores as
+// warp-level mma.sync (m16n8k16, bf16 operands, fp32 accumulation) in the split-bf16 form
+// x = hi + lo with three products (lo hi + hi lo + hi hi, relative error ~1e-5, the scheme
+// of BT_PREC_BF16X3); the CTA's W_h fragments stay in registers for the whole sequence and
+// the step's fp32 rows are split as they are read from shared memory. Each thread ends a
+// product owning one env x two units, with all three gates of those units, so the gate
+// math follows in registers.
 //
 //   forward step t   stage the 32 carry rows hin_t (all H) from L2; hp = hin_t W_h for the
-//                    CTA's 48 gate columns (fp32 FMA); gates, h_t, the saved r, z, n,
-//                    h W_hn + b_hn; hin_{t+1} = reset ? 0 : h_t; barrier
-//   backward step t  gate gradients of the CTA's (env, unit) pairs from dL/dh_t (heads) and
-//                    the carry gradient kept in registers; dxp_t, dhp_t written; barrier;
+//                    CTA's 48 gate columns; gates, h_t, the saved r, z, n, h W_hn + b_hn;
+//                    hin_{t+1} = reset ? 0 : h_t; barrier
+//   backward step t  gate gradients of the thread's (env, unit) pairs from dL/dh_t (heads)
+//                    and the carry gradient kept in registers; dxp_t, dhp_t written; barrier;
 //                    stage the 32 dhp_t rows (all 3H); carry = reset ? 0 : dh z + dhp_t W_h^T
 //
-// The arithmetic is fp32 with the same gate formulas as the per-step kernels in
-// recurrent.cu; only the summation order of the products differs.
+// The gate formulas are those of the per-step fp32 kernels in recurrent.cu.
 //
 // The barrier: thread 0 of every CTA adds one to a device counter (zeroed before the launch)
 // and spins until it reaches (step + 1) * CTAs. All CTAs must be resident at once: the host
@@ -81,27 +84,88 @@ __device__ __forceinline__ bool gru_grid_barrier(const GruSeqParams& p, unsigned
 
 __device__ __forceinline__ float gru_sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
 
+// fp32 pair (a, b) as bf16x2 hi = bf16(a, b) and lo = bf16 of the remainders (a in the low
+// half, the order mma.sync expects for consecutive K or column indices).
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - __low2float(h), b - __high2float(h));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// D (16 x 8, fp32) += A (16 x 16, bf16, row) B (16 x 8, bf16, col): warp-level tensor-core
+// product. Fragments (gid = lane / 4, tig = lane % 4): A regs {rows gid, gid + 8} x
+// {cols 2 tig.., 2 tig + 8..}, B regs k = {2 tig.., 2 tig + 8..} at n = gid, D regs
+// (gid, 2 tig), (gid, 2 tig + 1), (gid + 8, 2 tig), (gid + 8, 2 tig + 1).
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One k-step of a split-bf16 product: A from an fp32 shared tile (row pointers a0 for rows
+// gid and a1 for gid + 8, already offset to column 2 tig of the step), B as hi/lo fragments;
+// D += A_lo B_hi + A_hi B_lo + A_hi B_hi.
+__device__ __forceinline__ void load_a_split(const float* a0, const float* a1, uint32_t (&ah)[4],
+                                             uint32_t (&al)[4]) {
+  const float2 p00 = *reinterpret_cast<const float2*>(a0);
+  const float2 p10 = *reinterpret_cast<const float2*>(a1);
+  const float2 p01 = *reinterpret_cast<const float2*>(a0 + 8);
+  const float2 p11 = *reinterpret_cast<const float2*>(a1 + 8);
+  split_pair(p00.x, p00.y, ah[0], al[0]);
+  split_pair(p10.x, p10.y, ah[1], al[1]);
+  split_pair(p01.x, p01.y, ah[2], al[2]);
+  split_pair(p11.x, p11.y, ah[3], al[3]);
+}
+__device__ __forceinline__ void mma_split(float (&d)[4], const uint32_t (&ah)[4],
+                                          const uint32_t (&al)[4], const uint32_t (&bh)[2],
+                                          const uint32_t (&bl)[2]) {
+  mma_16816(d, al, bh[0], bh[1]);
+  mma_16816(d, ah, bl[0], bl[1]);
+  mma_16816(d, ah, bh[0], bh[1]);
+}
+
+// Warp roles (both kernels): warp = mt + 2 * nt + 4 * kh, with m-tile mt (envs 16 mt ..),
+// n-tile nt (8 units) and K half kh. After the product the two K halves of a tile meet in
+// shared memory (fixed order: half 0 + half 1); a thread then owns env row
+// 16 mt + gid + 8 kh and the two units 8 nt + 2 tig + {0, 1} of its tile.
+constexpr int kXch = 4 * 32;  // floats per (warp tile, gate) exchange slot
+
+template <int H>
 __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_forward_kernel(GruSeqParams p) {
+  constexpr int KS = H / 32;  // 16-wide K steps per K half
+  constexpr int LD = H + 8;   // row stride of the staged carry rows (conflict-free float2)
   extern __shared__ __align__(16) float sm[];
   __shared__ int s_fail;
-  const int H = p.H, T = p.T, ld = H + 4;
-  float* wt_s = sm;                              // [48][H + 4]: W_h columns, transposed
-  float* hin_s = sm + 3 * kGruSeqUnits * ld;     // [32][H + 4]
+  float* hin_s = sm;                                // [32][LD]
+  float* xch = sm + kGruSeqEnvs * LD;               // [kh][mt][nt][gate][lane][4]
+  const int T = p.T, H3 = 3 * H;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int u_l = 8 * (warp & 1) + (lane & 7);          // unit within the CTA
-  const int e_l = 2 * (4 * (warp >> 1) + (lane >> 3));  // first of the thread's two envs
-  const int e0 = blockIdx.x * kGruSeqEnvs;
-  const int U = blockIdx.y * kGruSeqUnits + u_l;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int mt = warp & 1, nt = (warp >> 1) & 1, kh = warp >> 2;
+  const int e0 = blockIdx.x * kGruSeqEnvs, u0 = blockIdx.y * kGruSeqUnits;
   const int live = live_rows(p.env_count, p.envs);
   if (tid == 0) s_fail = 0;
-  // W_h[:, g H + u] for the CTA's units, gate-major: row c = g * 16 + unit
-  for (int i = tid; i < 3 * kGruSeqUnits * H; i += kGruSeqThreads) {
-    const int c = i / H, k = i - c * H;
-    const int g = c / kGruSeqUnits, u = blockIdx.y * kGruSeqUnits + (c - g * kGruSeqUnits);
-    wt_s[c * ld + k] = p.wh[(size_t)k * 3 * H + g * H + u];
+  // B fragments of W_h for the whole sequence: gate g, unit u0 + 8 nt + gid, K rows of half kh
+  uint32_t bh[3][KS][2], bl[3][KS][2];
+#pragma unroll
+  for (int g = 0; g < 3; ++g) {
+    const float* w = p.wh + g * H + u0 + nt * 8 + gid;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int k = kh * (H / 2) + ks * 16 + tig * 2;
+      split_pair(w[(size_t)k * H3], w[(size_t)(k + 1) * H3], bh[g][ks][0], bl[g][ks][0]);
+      split_pair(w[(size_t)(k + 8) * H3], w[(size_t)(k + 9) * H3], bh[g][ks][1], bl[g][ks][1]);
+    }
   }
-  const float bhn = p.bhn[U];
-  const int h4 = H / 4;
+  const int r_l = mt * 16 + gid + 8 * kh;  // the thread's env row in the CTA
+  const int ub = u0 + nt * 8 + tig * 2;    // its first unit
+  const bool on = e0 + r_l < live;
+  const float bhn0 = p.bhn[ub], bhn1 = p.bhn[ub + 1];
+  constexpr int h4 = H / 4;
   for (int t = 0; t < T; ++t) {
     // carry rows of the CTA's envs at step t (written by every CTA in step t - 1)
     for (int i = tid; i < kGruSeqEnvs * h4; i += kGruSeqThreads) {
@@ -109,120 +173,117 @@ __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_forward_kernel(GruS
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (e0 + e < live)
         v = __ldcg(reinterpret_cast<const float4*>(p.hin + ((size_t)(e0 + e) * T + t) * H) + k4);
-      *reinterpret_cast<float4*>(hin_s + e * ld + 4 * k4) = v;
+      *reinterpret_cast<float4*>(hin_s + e * LD + 4 * k4) = v;
     }
-    // the input projections and reset flags of the thread's two outputs
+    const size_t row = (size_t)(e0 + r_l) * T + t;
     float x[2][3];
-    bool on[2];
-    size_t row[2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      on[j] = e0 + e_l + j < live;
-      row[j] = (size_t)(e0 + e_l + j) * T + t;
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int g = 0; g < 3; ++g) x[j][g] = on[j] ? p.xp[row[j] * 3 * H + g * H + U] : 0.f;
-    }
+      for (int g = 0; g < 3; ++g) x[j][g] = on ? p.xp[row * H3 + g * H + ub + j] : 0.f;
     __syncthreads();
-    float acc[2][3] = {};
-    const float* a0 = hin_s + e_l * ld;
-    const float* a1 = a0 + ld;
-    const float* w0 = wt_s + u_l * ld;
-    const float* w1 = w0 + kGruSeqUnits * ld;
-    const float* w2 = w1 + kGruSeqUnits * ld;
-#pragma unroll 4
-    for (int k = 0; k < H; k += 4) {
-      const float4 x0 = *reinterpret_cast<const float4*>(a0 + k);
-      const float4 x1 = *reinterpret_cast<const float4*>(a1 + k);
-      const float4 wr = *reinterpret_cast<const float4*>(w0 + k);
-      const float4 wz = *reinterpret_cast<const float4*>(w1 + k);
-      const float4 wn = *reinterpret_cast<const float4*>(w2 + k);
-#define BT_GRU_FMA4(A, W, ACC)     \
-  ACC = fmaf(A.x, W.x, ACC);       \
-  ACC = fmaf(A.y, W.y, ACC);       \
-  ACC = fmaf(A.z, W.z, ACC);       \
-  ACC = fmaf(A.w, W.w, ACC);
-      BT_GRU_FMA4(x0, wr, acc[0][0]);
-      BT_GRU_FMA4(x0, wz, acc[0][1]);
-      BT_GRU_FMA4(x0, wn, acc[0][2]);
-      BT_GRU_FMA4(x1, wr, acc[1][0]);
-      BT_GRU_FMA4(x1, wz, acc[1][1]);
-      BT_GRU_FMA4(x1, wn, acc[1][2]);
-#undef BT_GRU_FMA4
+    float acc[3][4] = {};
+    const float* a0 = hin_s + (mt * 16 + gid) * LD + kh * (H / 2) + tig * 2;
+    const float* a1 = a0 + 8 * LD;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t ah[4], al[4];
+      load_a_split(a0 + ks * 16, a1 + ks * 16, ah, al);
+#pragma unroll
+      for (int g = 0; g < 3; ++g) mma_split(acc[g], ah, al, bh[g][ks], bl[g][ks]);
     }
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      if (!on[j]) continue;
-      const float r = gru_sigmoid(x[j][0] + acc[j][0]);
-      const float z = gru_sigmoid(x[j][1] + acc[j][1]);
-      const float hn = acc[j][2] + bhn;
-      const float n = tanhf(x[j][2] + r * hn);
-      const float hi = hin_s[(e_l + j) * ld + U];
-      const float out = (1.f - z) * n + z * hi;
-      const size_t o = row[j] * H + U;
-      p.h[o] = out;
-      p.gr[o] = r;
-      p.gz[o] = z;
-      p.gn[o] = n;
-      p.ghn[o] = hn;
-      if (t + 1 < T) p.hin[o + H] = p.reset[row[j] + 1] ? 0.f : out;
+    for (int g = 0; g < 3; ++g)
+      *reinterpret_cast<float4*>(xch + ((warp * 3 + g) * 32 + lane) * 4) =
+          make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    __syncthreads();
+    if (on) {
+      const int w0 = warp & 3, w1 = w0 + 4;  // the tile's two K halves
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float hp[3];
+#pragma unroll
+        for (int g = 0; g < 3; ++g)
+          hp[g] = xch[((w0 * 3 + g) * 32 + lane) * 4 + 2 * kh + j] +
+                  xch[((w1 * 3 + g) * 32 + lane) * 4 + 2 * kh + j];
+        const int U = ub + j;
+        const float r = gru_sigmoid(x[j][0] + hp[0]);
+        const float z = gru_sigmoid(x[j][1] + hp[1]);
+        const float hn = hp[2] + (j ? bhn1 : bhn0);
+        const float n = tanhf(x[j][2] + r * hn);
+        const float hi = hin_s[r_l * LD + U];
+        const float out = (1.f - z) * n + z * hi;
+        const size_t o = row * H + U;
+        p.h[o] = out;
+        p.gr[o] = r;
+        p.gz[o] = z;
+        p.gn[o] = n;
+        p.ghn[o] = hn;
+        if (t + 1 < T) p.hin[o + H] = p.reset[row + 1] ? 0.f : out;
+      }
     }
     if (t + 1 < T && !gru_grid_barrier(p, (unsigned)(t + 1) * gridDim.x * gridDim.y, &s_fail))
       return;
   }
 }
 
-// Backward thread layout: thread (env pair, unit pair, kh) with kh = lane & 1; for the
-// gate gradients it owns envs 2 ep, 2 ep + 1 of unit 2 up + kh, and in the carry product it
-// sums the float4 columns of parity kh for both units of its pair (four accumulators, two
-// dhp and two W_h rows per float4 step), the two parities then combined with a shuffle.
+template <int H>
 __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_backward_kernel(GruSeqParams p) {
+  constexpr int H3 = 3 * H;
+  constexpr int KS = H3 / 32;  // 16-wide K steps per K half
+  constexpr int LD = H3 + 8;
   extern __shared__ __align__(16) float sm[];
   __shared__ int s_fail;
-  const int H = p.H, T = p.T, H3 = 3 * H, ld = H3 + 4;
-  float* w_s = sm;                              // [16][3H + 4]: rows of W_h
-  float* d_s = sm + kGruSeqUnits * ld;          // [32][3H + 4]: dhp rows of the step
+  float* d_s = sm;                        // [32][LD]: dhp rows of the step
+  float* xch = sm + kGruSeqEnvs * LD;     // [kh][mt][nt][lane][4]
+  const int T = p.T;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kh = lane & 1;
-  const int up = ((lane >> 1) & 3) + 4 * (warp & 1);  // unit pair 0..7
-  const int u_l = 2 * up + kh;                        // the thread's unit (gate gradients)
-  const int e_l = 2 * ((lane >> 3) + 4 * (warp >> 1));
-  const int e0 = blockIdx.x * kGruSeqEnvs;
-  const int U = blockIdx.y * kGruSeqUnits + u_l;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int mt = warp & 1, nt = (warp >> 1) & 1, kh = warp >> 2;
+  const int e0 = blockIdx.x * kGruSeqEnvs, u0 = blockIdx.y * kGruSeqUnits;
   const int live = live_rows(p.env_count, p.envs);
   if (tid == 0) s_fail = 0;
-  for (int i = tid; i < kGruSeqUnits * H3; i += kGruSeqThreads) {
-    const int u = i / H3, c = i - u * H3;
-    w_s[u * ld + c] = p.wh[(size_t)(blockIdx.y * kGruSeqUnits + u) * H3 + c];
-  }
-  float carry[2] = {0.f, 0.f};
-  bool on[2];
+  // B fragments of W_h^T: unit u0 + 8 nt + gid (a row of W_h), K = the 3H columns of half kh
+  uint32_t bh[KS][2], bl[KS][2];
+  {
+    const float* w = p.wh + (size_t)(u0 + nt * 8 + gid) * H3 + kh * (H3 / 2) + tig * 2;
 #pragma unroll
-  for (int j = 0; j < 2; ++j) on[j] = e0 + e_l + j < live;
-  const int c4 = H3 / 4;
+    for (int ks = 0; ks < KS; ++ks) {
+      split_pair(w[ks * 16], w[ks * 16 + 1], bh[ks][0], bl[ks][0]);
+      split_pair(w[ks * 16 + 8], w[ks * 16 + 9], bh[ks][1], bl[ks][1]);
+    }
+  }
+  const int r_l = mt * 16 + gid + 8 * kh;
+  const int ub = u0 + nt * 8 + tig * 2;
+  const bool on = e0 + r_l < live;
+  float carry[2] = {0.f, 0.f};
+  constexpr int c4 = H3 / 4;
   unsigned int step = 0;
   for (int t = T - 1; t >= 0; --t) {
+    const size_t row = (size_t)(e0 + r_l) * T + t;
     float direct[2] = {0.f, 0.f};
+    if (on) {
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      if (!on[j]) continue;
-      const size_t row = (size_t)(e0 + e_l + j) * T + t;
-      const size_t i = row * H + U;
-      const float dh = p.dhs[i] + carry[j];
-      const float r = p.gr[i], z = p.gz[i], n = p.gn[i], hn = p.ghn[i], hi = p.hin[i];
-      const float dn = dh * (1.f - z);
-      const float dz = dh * (hi - n);
-      const float dan = dn * (1.f - n * n);
-      const float dar = (dan * hn) * r * (1.f - r);
-      const float daz = dz * z * (1.f - z);
-      float* dx = p.dxp + row * H3;
-      float* dp = p.dhp + row * H3;
-      dx[U] = dar;
-      dx[H + U] = daz;
-      dx[2 * H + U] = dan;
-      dp[U] = dar;
-      dp[H + U] = daz;
-      dp[2 * H + U] = dan * r;
-      direct[j] = dh * z;
+      for (int j = 0; j < 2; ++j) {
+        const int U = ub + j;
+        const size_t i = row * H + U;
+        const float dh = p.dhs[i] + carry[j];
+        const float r = p.gr[i], z = p.gz[i], n = p.gn[i], hn = p.ghn[i], hi = p.hin[i];
+        const float dn = dh * (1.f - z);
+        const float dz = dh * (hi - n);
+        const float dan = dn * (1.f - n * n);
+        const float dar = (dan * hn) * r * (1.f - r);
+        const float daz = dz * z * (1.f - z);
+        float* dx = p.dxp + row * H3;
+        float* dp = p.dhp + row * H3;
+        dx[U] = dar;
+        dx[H + U] = daz;
+        dx[2 * H + U] = dan;
+        dp[U] = dar;
+        dp[H + U] = daz;
+        dp[2 * H + U] = dan * r;
+        direct[j] = dh * z;
+      }
     }
     if (t == 0) break;  // no carry into step -1
     ++step;
@@ -232,52 +293,40 @@ __global__ void __launch_bounds__(kGruSeqThreads, 1) gru_seq_backward_kernel(Gru
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (e0 + e < live)
         v = __ldcg(reinterpret_cast<const float4*>(p.dhp + ((size_t)(e0 + e) * T + t) * H3) + q);
-      *reinterpret_cast<float4*>(d_s + e * ld + 4 * q) = v;
+      *reinterpret_cast<float4*>(d_s + e * LD + 4 * q) = v;
     }
     __syncthreads();
-    // acc[env j][unit of the pair v]
-    float acc[2][2] = {};
-    const float* a0 = d_s + e_l * ld;
-    const float* a1 = a0 + ld;
-    const float* w0 = w_s + (2 * up) * ld;
-    const float* w1 = w0 + ld;
-#pragma unroll 4
-    for (int c = 4 * kh; c < H3; c += 8) {
-      const float4 x0 = *reinterpret_cast<const float4*>(a0 + c);
-      const float4 x1 = *reinterpret_cast<const float4*>(a1 + c);
-      const float4 v0 = *reinterpret_cast<const float4*>(w0 + c);
-      const float4 v1 = *reinterpret_cast<const float4*>(w1 + c);
-#define BT_GRU_DOT4(A, W, ACC)  \
-  ACC = fmaf(A.x, W.x, ACC);     \
-  ACC = fmaf(A.y, W.y, ACC);     \
-  ACC = fmaf(A.z, W.z, ACC);     \
-  ACC = fmaf(A.w, W.w, ACC);
-      BT_GRU_DOT4(x0, v0, acc[0][0]);
-      BT_GRU_DOT4(x0, v1, acc[0][1]);
-      BT_GRU_DOT4(x1, v0, acc[1][0]);
-      BT_GRU_DOT4(x1, v1, acc[1][1]);
-#undef BT_GRU_DOT4
-    }
-    // combine the two column parities; this thread keeps its own unit (2 up + kh)
+    float acc[4] = {};
+    const float* a0 = d_s + (mt * 16 + gid) * LD + kh * (H3 / 2) + tig * 2;
+    const float* a1 = a0 + 8 * LD;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-#pragma unroll
-      for (int v = 0; v < 2; ++v) acc[j][v] += __shfl_xor_sync(0xffffffffu, acc[j][v], 1);
+    for (int ks = 0; ks < KS; ++ks) {
+      uint32_t ah[4], al[4];
+      load_a_split(a0 + ks * 16, a1 + ks * 16, ah, al);
+      mma_split(acc, ah, al, bh[ks], bl[ks]);
     }
+    *reinterpret_cast<float4*>(xch + (warp * 32 + lane) * 4) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
     // the carry gradient into step t - 1 (zero across a reset at step t)
+    const int w0 = warp & 3, w1 = w0 + 4;
+    const bool keep = on && !p.reset[row];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float v = kh ? acc[j][1] : acc[j][0];
-      carry[j] = on[j] && !p.reset[(size_t)(e0 + e_l + j) * T + t] ? v + direct[j] : 0.f;
+      const float v = xch[(w0 * 32 + lane) * 4 + 2 * kh + j] + xch[(w1 * 32 + lane) * 4 + 2 * kh + j];
+      carry[j] = keep ? v + direct[j] : 0.f;
     }
-    __syncthreads();  // d_s is restaged in the next step
   }
 }
 
 namespace {
 
-size_t fwd_smem(int H) { return (size_t)(3 * kGruSeqUnits + kGruSeqEnvs) * (H + 4) * 4; }
-size_t bwd_smem(int H) { return (size_t)(kGruSeqUnits + kGruSeqEnvs) * (3 * H + 4) * 4; }
+size_t fwd_smem(int H) {
+  return ((size_t)kGruSeqEnvs * (H + 8) + 8 * 3 * kXch) * sizeof(float);
+}
+size_t bwd_smem(int H) {
+  return ((size_t)kGruSeqEnvs * (3 * H + 8) + 8 * kXch) * sizeof(float);
+}
 
 dim3 seq_grid(int envs, int H) {
   return dim3((unsigned)ceil_div(envs, kGruSeqEnvs), (unsigned)(H / kGruSeqUnits));
@@ -296,30 +345,55 @@ int seq_fits(const void* kernel, size_t smem, dim3 grid, bool* ok) {
   return BT_OK;
 }
 
-}  // namespace
-
-// Whether the one-launch kernels serve a sequence of `envs` envs with H hidden units.
-int gru_seq_supported(int envs, int H, bool* ok) {
-  *ok = false;
-  if (H % kGruSeqUnits != 0 || H > 256 || envs < 1) return BT_OK;
+template <int H>
+int supported_h(int envs, bool* ok) {
   const dim3 grid = seq_grid(envs, H);
   bool f = false, b = false;
-  BT_TRY(seq_fits((const void*)gru_seq_forward_kernel, fwd_smem(H), grid, &f));
-  BT_TRY(seq_fits((const void*)gru_seq_backward_kernel, bwd_smem(H), grid, &b));
+  BT_TRY(seq_fits((const void*)gru_seq_forward_kernel<H>, fwd_smem(H), grid, &f));
+  BT_TRY(seq_fits((const void*)gru_seq_backward_kernel<H>, bwd_smem(H), grid, &b));
   *ok = f && b;
   return BT_OK;
 }
 
+}  // namespace
+
+// Whether the one-launch kernels serve a sequence of `envs` envs with H hidden units
+// (H = 64, 128 or 256, every CTA of the grid resident at once).
+int gru_seq_supported(int envs, int H, bool* ok) {
+  *ok = false;
+  if (envs < 1) return BT_OK;
+  switch (H) {
+    case 64: return supported_h<64>(envs, ok);
+    case 128: return supported_h<128>(envs, ok);
+    case 256: return supported_h<256>(envs, ok);
+    default: return BT_OK;
+  }
+}
+
 int launch_gru_seq_forward(const GruSeqParams& p, cudaStream_t s) {
   BT_CUDA(cudaMemsetAsync(p.bar, 0, sizeof(unsigned int), s));
-  gru_seq_forward_kernel<<<seq_grid(p.envs, p.H), kGruSeqThreads, fwd_smem(p.H), s>>>(p);
+  const dim3 grid = seq_grid(p.envs, p.H);
+  const size_t smem = fwd_smem(p.H);
+  switch (p.H) {
+    case 64: gru_seq_forward_kernel<64><<<grid, kGruSeqThreads, smem, s>>>(p); break;
+    case 128: gru_seq_forward_kernel<128><<<grid, kGruSeqThreads, smem, s>>>(p); break;
+    case 256: gru_seq_forward_kernel<256><<<grid, kGruSeqThreads, smem, s>>>(p); break;
+    default: BT_CHECK_ARG(false, "gru sequence kernel: hidden size %d", p.H);
+  }
   BT_LAUNCH_CHECK("gru_seq_forward_kernel");
   return BT_OK;
 }
 
 int launch_gru_seq_backward(const GruSeqParams& p, cudaStream_t s) {
   BT_CUDA(cudaMemsetAsync(p.bar, 0, sizeof(unsigned int), s));
-  gru_seq_backward_kernel<<<seq_grid(p.envs, p.H), kGruSeqThreads, bwd_smem(p.H), s>>>(p);
+  const dim3 grid = seq_grid(p.envs, p.H);
+  const size_t smem = bwd_smem(p.H);
+  switch (p.H) {
+    case 64: gru_seq_backward_kernel<64><<<grid, kGruSeqThreads, smem, s>>>(p); break;
+    case 128: gru_seq_backward_kernel<128><<<grid, kGruSeqThreads, smem, s>>>(p); break;
+    case 256: gru_seq_backward_kernel<256><<<grid, kGruSeqThreads, smem, s>>>(p); break;
+    default: BT_CHECK_ARG(false, "gru sequence kernel: hidden size %d", p.H);
+  }
   BT_LAUNCH_CHECK("gru_seq_backward_kernel");
   return BT_OK;
 }
