@@ -33,7 +33,8 @@ EXPORTS = (
     "bt_last_error", "bt_version", "bt_gae", "bt_learner_create", "bt_learner_destroy",
     "bt_learner_num_params", "bt_learner_param_count", "bt_learner_param_info",
     "bt_learner_set_state", "bt_learner_get_state", "bt_learner_update", "bt_learner_targets",
-    "bt_learner_loss_grads", "bt_learner_act", "bt_sample_categorical", "bt_nccl_unique_id",
+    "bt_learner_loss_grads", "bt_learner_act", "bt_learner_act_recurrent",
+    "bt_sample_categorical", "bt_nccl_unique_id",
     "bt_learner_comm_init", "bt_learner_profile", "bt_learner_profile_read",
     "bt_learner_launch_count", "bt_gemm_bf16", "bt_gemm_bf16x3", "bt_clip_adam",
     "bt_clip_adam_noalloc", "bt_learner_use_graphs", "bt_learner_check",
@@ -126,6 +127,8 @@ def lib() -> C.CDLL:
         "bt_learner_targets": (C.c_int, [vp, vp, vp, vp, vp]),
         "bt_learner_loss_grads": (C.c_int, [vp, C.POINTER(Batch), vp, vp, vp, i32, vp, vp, vp]),
         "bt_learner_act": (C.c_int, [vp, vp, i32, vp, f32, vp, vp, vp, vp]),
+        "bt_learner_act_recurrent": (C.c_int, [vp, vp, vp, vp, i32, vp, f32, vp, vp, vp, vp,
+                                               vp]),
         "bt_sample_categorical": (C.c_int, [vp, vp, i32, i32, f32, vp, vp, vp]),
         "bt_nccl_unique_id": (C.c_int, [vp, i32]),
         "bt_learner_comm_init": (C.c_int, [vp, vp, i32]),

@@ -1101,12 +1101,36 @@ int launch_sample(const float* out, const float* scale, int head, int A, int row
                   cudaStream_t stream);
 }
 
+namespace bt {
+int recurrent_act(bt_learner* L, const float* obs, const uint8_t* reset, const float* carry,
+                  int num, const float* noise, float temperature, void* action, float* log_prob,
+                  float* value, float* carry_out, cudaStream_t s);
+}
+
+extern "C" int bt_learner_act_recurrent(bt_learner* L, const float* obs, const uint8_t* reset,
+                                        const float* carry, int32_t num, const float* noise,
+                                        float temperature, void* action, float* log_prob,
+                                        float* value, float* carry_out, void* stream) {
+  BT_CHECK_ARG(L && obs && reset && carry && action && log_prob && carry_out,
+               "bt_learner_act_recurrent: null argument");
+  if (!L->recurrent) {
+    set_error("bt_learner_act_recurrent: the network has no GRU layer (use bt_learner_act)");
+    return BT_ERR_INVALID;
+  }
+  const int cap = std::min(L->act_rows, L->N);
+  BT_CHECK_ARG(num >= 0 && num <= cap, "bt_learner_act_recurrent: %d rows > capacity %d", num,
+               cap);
+  if (num == 0) return BT_OK;
+  return bt::recurrent_act(L, obs, reset, carry, num, noise, temperature, action, log_prob, value,
+                           carry_out, (cudaStream_t)stream);
+}
+
 extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, const float* noise,
                               float temperature, void* action, float* log_prob, float* value,
                               void* stream) {
   BT_CHECK_ARG(L && obs && action && log_prob, "bt_learner_act: null argument");
   if (L->recurrent) {
-    set_error("bt_learner_act: recurrent networks need a carry; not available in this build");
+    set_error("bt_learner_act: recurrent networks need a carry (use bt_learner_act_recurrent)");
     return BT_ERR_UNSUPPORTED;
   }
   BT_CHECK_ARG(num >= 0 && num <= L->act_rows, "bt_learner_act: %d rows > capacity %d", num,

@@ -216,6 +216,26 @@ class Learner:
             float(temperature), _ptr(action), _ptr(lp), _ptr(value), _stream()))
         return action, lp, value
 
+    def act_recurrent(self, obs: torch.Tensor, reset: torch.Tensor, carry: torch.Tensor,
+                      noise: torch.Tensor | None = None, temperature: float = 1.0):
+        """One step of a GRU network (RecurrentPPO.step): obs [num, D], reset [num] (the carry
+        is zeroed where set), carry [num, H]. Returns (action, log_prob, value, new carry)."""
+        num = obs.shape[0]
+        a = self.network.action_dim
+        if self.network.head == "categorical":
+            action = torch.empty(num, dtype=torch.int32, device=self.device)
+        else:
+            action = torch.empty(num, a, dtype=torch.float32, device=self.device)
+        lp = torch.empty(num, dtype=torch.float32, device=self.device)
+        value = torch.empty(num, dtype=torch.float32, device=self.device)
+        new_carry = torch.empty_like(carry, dtype=torch.float32)
+        _lib.check(_lib.lib().bt_learner_act_recurrent(
+            self._h, _ptr(obs.contiguous()), _ptr(reset.to(torch.uint8).contiguous()),
+            _ptr(carry.to(torch.float32).contiguous()), num,
+            _ptr(noise.contiguous()) if noise is not None else None, float(temperature),
+            _ptr(action), _ptr(lp), _ptr(value), _ptr(new_carry), _stream()))
+        return action, lp, value, new_carry
+
     # ---- tracing -------------------------------------------------------------------------------
     def profile(self, enable: bool = True):
         _lib.check(_lib.lib().bt_learner_profile(self._h, int(enable)))

@@ -271,9 +271,28 @@ class RecurrentPPO(PPO):
         return state, carry
 
     def step(self, state, carry, key, timestep, temperature: float = 1.0):
-        raise NotImplementedError(
-            "RecurrentPPO.step: the recurrent act step (GRU carry in/out) is not available in "
-            "this build; the learner update is")
+        """recurrent_ppo.py:72-96: one step of the network on timestep.obs [N, ...] from
+        `carry` [N, H], zeroed first where the timestep starts an episode (terminated or
+        truncated set, boonta/networks/blocks/rnn.py:42-45). Returns (state, new carry,
+        action, {"log_prob", "value"})."""
+        obs = _flat(timestep.obs, self.network.obs_dim)
+        n = obs.shape[0]
+        lrn = self._act_learner(n)
+        self._load(lrn, state)
+        reset = torch.zeros(n, dtype=torch.uint8, device=obs.device)
+        for flag in (timestep.terminated, timestep.truncated):
+            if flag is not None:
+                reset |= torch.as_tensor(flag, device=obs.device).reshape(n).to(torch.uint8)
+        g = torch.Generator(device=obs.device).manual_seed(_seed(key))
+        a = self.network.action_dim
+        if self.network.head == "categorical":
+            tiny = torch.finfo(torch.float32).tiny
+            noise = torch.rand((n, a), generator=g, device=obs.device).clamp_(min=tiny)
+        else:
+            noise = torch.randn((n, a), generator=g, device=obs.device)
+        action, log_prob, value, new_carry = lrn.act_recurrent(obs, reset, carry, noise,
+                                                               temperature)
+        return state, new_carry, action, {"log_prob": log_prob, "value": value}
 
     def _perm_size(self, t: int, n: int) -> int:
         return n  # recurrent_ppo.py:270-276 permutes environments

@@ -21,6 +21,8 @@
  *                           boonta/podracers/anakin.py:165-186
  *   bt_learner_act          boonta/algorithms/ppo.py:57-74 (PPO.step) with
  *                           boonta/networks/distributions.py:21-23 (Gumbel-argmax sample)
+ *   bt_learner_act_recurrent
+ *                           boonta/algorithms/recurrent_ppo.py:72-96 (RecurrentPPO.step)
  *   bt_learner_set_state /
  *   bt_learner_get_state    the PPOState pytree (ppo.py:30-34): params and the optax
  *                           chain state (clip: empty; adam: count, mu, nu)
@@ -214,6 +216,16 @@ BT_API int bt_learner_loss_grads(bt_learner* learner, const bt_batch* batch,
 BT_API int bt_learner_act(bt_learner* learner, const float* obs, int32_t num, const float* noise,
                    float temperature, void* action, float* log_prob, float* value,
                    void* stream);
+
+/* Act for GRU networks (RecurrentPPO.step, boonta/algorithms/recurrent_ppo.py:72-96): one time
+ * step on num envs. obs [num, obs_dim]; reset u8 [num] (1 = the episode starts at this step:
+ * the carry is zeroed first, boonta/networks/blocks/rnn.py:42-45); carry [num, H] entering the
+ * step; noise, temperature, action, log_prob, value as in bt_learner_act; carry_out [num, H]
+ * the carry leaving the step. num is at most N (the learner's envs per rank). */
+BT_API int bt_learner_act_recurrent(bt_learner* learner, const float* obs, const uint8_t* reset,
+                                    const float* carry, int32_t num, const float* noise,
+                                    float temperature, void* action, float* log_prob,
+                                    float* value, float* carry_out, void* stream);
 
 /* Categorical sampling alone (boonta/networks/distributions.py:8-23): action =
  * argmax(log_softmax(logits / temperature) + (-log(-log(u)))), first index on ties; the

@@ -24,8 +24,11 @@ PARAM_RTOL = 1e-3
 # The "param" bound is on the parameter *change* of a full update: Adam's first steps move
 # every weight by about lr * sign(gradient), so a weight whose true gradient is within the
 # GEMM's rounding of zero can step either way; parameters themselves stay within 1e-3.
+# bf16 operands: the probability ratios of the two implementations differ by ~1e-3, so a
+# sample whose ratio lies that close to 1 +- clip_coefficient can fall on either side; the
+# clip fraction (a count over the minibatch) gets an absolute bound of 1 % of the rows.
 BF16_TOL = {"grad": 2e-3, "param": 1e-1, "params": 1e-1, "target_rtol": 1e-2,
-            "target_atol": 3e-3, "stats_rtol": 1e-2, "stats_atol": 2e-3}
+            "target_atol": 3e-3, "stats_rtol": 1e-2, "stats_atol": 2e-3, "clipfrac_atol": 1e-2}
 FP32_TOL = {"grad": GRAD_RTOL, "param": PARAM_RTOL, "params": PARAM_RTOL, "target_rtol": 1e-4,
             "target_atol": 1e-4, "stats_rtol": 2e-3, "stats_atol": 2e-4}
 
@@ -149,8 +152,13 @@ def test_full_update_matches_the_oracle(name):
         d_oracle = op[k].astype(np.float64) - params[k]
         assert _rel(d_native, d_oracle) <= tol["param"], (k, _rel(d_native, d_oracle))
         assert _rel(new[k], op[k]) <= tol["params"], (k, _rel(new[k], op[k]))
-    np.testing.assert_allclose(st.cpu().numpy(), ostats, rtol=tol["stats_rtol"],
+    stats = st.cpu().numpy()
+    clip = 3  # actor/clip_fraction (ppo.py:170-179 order)
+    other = [i for i in range(stats.shape[-1]) if i != clip]
+    np.testing.assert_allclose(stats[..., other], ostats[..., other], rtol=tol["stats_rtol"],
                                atol=tol["stats_atol"])
+    np.testing.assert_allclose(stats[..., clip], ostats[..., clip], rtol=0,
+                               atol=tol.get("clipfrac_atol", tol["stats_atol"]))
     _, _, _, count = lrn.get_state()
     assert count == w.ppo.update_epochs * w.ppo.num_minibatches
 

@@ -56,3 +56,38 @@ def test_recurrent_update_matches_the_oracle(shape):
         d_oracle = op[k].astype(np.float64) - params[k]
         assert _rel(d_native, d_oracle) <= 1e-3, (k, _rel(d_native, d_oracle))
     np.testing.assert_allclose(st.cpu().numpy(), ostats, rtol=2e-3, atol=2e-4)
+
+
+@pytest.mark.parametrize("n", [64, 16], ids=["n64", "n16"])
+def test_recurrent_act_matches_the_oracle(n):
+    """bt_learner_act_recurrent (RecurrentPPO.step): value, carry out and the sample against
+    the oracle's forward over a one-step sequence from the same carry and resets, then a
+    second step chained on the returned carry."""
+    import torch
+
+    from boonta_b200.learner import Learner
+    from oracle import ppo as oppo
+    from oracle import recurrent
+
+    w = small_c4(t=16, n=n, epochs=1, minibatches=2)
+    lrn = Learner.from_workload(w)
+    params = init_params(w.network, seed=5)
+    lrn.set_state(params)
+    rng = np.random.default_rng(11)
+    h, a, d = w.network.torso[-1].features, w.network.action_dim, w.network.obs_dim
+    obs = rng.standard_normal((2, n, d)).astype(np.float32)
+    carry = (0.1 * rng.standard_normal((n, h))).astype(np.float32)
+    reset = np.stack([(rng.random(n) < 0.3), np.zeros(n, bool)]).astype(np.uint8)
+    u = rng.random((2, n, a)).astype(np.float32).clip(np.finfo(np.float32).tiny, None)
+    c = lambda x: torch.as_tensor(x).cuda()
+    out, val, cache = recurrent.forward_seq(w.network, params, obs.transpose(1, 0, 2),
+                                            reset.T, carry)
+    cur = c(carry)
+    for t in range(2):
+        action, lp, value, cur = lrn.act_recurrent(c(obs[t]), c(reset[t]), cur, c(u[t]))
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(value.cpu().numpy(), val[:, t], rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(cur.cpu().numpy(), cache["hs"][:, t], rtol=1e-4, atol=1e-5)
+        ref_action, ref_lp = oppo.sample_categorical(out[:, t], u[t])
+        np.testing.assert_array_equal(action.cpu().numpy(), ref_action)
+        np.testing.assert_allclose(lp.cpu().numpy(), ref_lp, rtol=1e-4, atol=1e-5)

@@ -127,6 +127,8 @@ def test_gae_estimator_matches_the_oracle():
 
 @pytest.mark.gpu
 def test_recurrent_ppo_update_runs_and_counts():
+    import torch
+
     w = configs.make("c4").scaled(num_steps=8, num_envs=32, num_minibatches=2, update_epochs=2)
     ppo = RecurrentPPO(w.ppo, w.network, w.optimizer)
     roll = configs.rollout(w, seed=1)
@@ -136,5 +138,13 @@ def test_recurrent_ppo_update_runs_and_counts():
     new = ppo.update(state, 2, tr)
     assert new.optimizer_state.count == w.ppo.update_epochs * w.ppo.num_minibatches
     assert bool(np.isfinite(new.params.cpu().numpy()).all())
-    with pytest.raises(NotImplementedError):
-        ppo.step(new, carry, 0, Timestep(obs=tr.first.obs[0]))
+    # act with the carry (RecurrentPPO.step): the carry changes, a reset zeroes it first
+    obs = tr.first.obs[0]
+    done = torch.zeros(w.num_envs, dtype=torch.bool, device="cuda")
+    s2, c2, action, aux = ppo.step(new, carry, 3, Timestep(obs=obs, terminated=done))
+    assert s2 is new and tuple(c2.shape) == tuple(carry.shape)
+    assert action.shape == (w.num_envs,) and aux["value"].shape == (w.num_envs,)
+    assert bool((aux["log_prob"] <= 0).all()) and not torch.equal(c2, carry)
+    _, c3, _, _ = ppo.step(new, c2, 3, Timestep(obs=obs, terminated=~done))
+    _, c4, _, _ = ppo.step(new, torch.zeros_like(c2), 3, Timestep(obs=obs))
+    assert torch.equal(c3, c4)  # reset everywhere == starting from a zero carry
