@@ -26,6 +26,7 @@
 // deterministic for a fixed grid.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "mma_sync.cuh"
 
 namespace bt {
 
@@ -37,8 +38,10 @@ constexpr float kLog2Pi = 1.8378770664093453f;
 // Shared-memory layout of the heads kernel, in floats (every region 16-byte aligned).
 struct HeadsLayout {
   int F, Fv, A, JP;
-  bool shared;
+  bool shared, mma;
   int ldf, ldv;
+  int ldj;  // row stride of the head kernel in shared memory (see heads_layout)
+  int ldd;  // row stride of the output gradients d
   size_t f, fv, wj, wv, bias, red, vred, d, sig, isig, lsig, total;
 };
 
@@ -50,15 +53,23 @@ __host__ __device__ inline int heads_inst_jp(int A, bool fuse) {
   return n <= 16 ? 16 : n <= 32 ? 32 : n <= 48 ? 48 : 64;
 }
 
-__host__ __device__ inline HeadsLayout heads_layout(int F, int Fv, int A, bool shared, int JP) {
+// Wide heads (JP >= 32, no fused head dW) may run the head products on warp-level tensor
+// cores (`mma`): the head kernel is then kept feature-major, wj[k][j] with row stride
+// ldj = JP + 8, and the features and output gradients get row strides (F + 8, JP + 8) whose
+// 16-byte fragment reads fall on distinct banks. Otherwise wj[j][k] (stride F), rows F + 4.
+__host__ __device__ inline HeadsLayout heads_layout(int F, int Fv, int A, bool shared, int JP,
+                                                    bool mma = false) {
   HeadsLayout L{};
   L.F = F;
   L.Fv = Fv;
   L.A = A;
   L.JP = JP;
   L.shared = shared;
-  L.ldf = F + 4;
+  L.mma = mma;
+  L.ldf = F + (mma ? 8 : 4);
   L.ldv = Fv + 4;
+  L.ldj = mma ? JP + 8 : F;
+  L.ldd = mma ? JP + 8 : JP;
   size_t o = 0;
   auto take = [&](size_t n) {
     const size_t at = o;
@@ -67,16 +78,16 @@ __host__ __device__ inline HeadsLayout heads_layout(int F, int Fv, int A, bool s
   };
   L.f = take((size_t)kTileRows * L.ldf);
   L.fv = take(shared ? 0 : (size_t)kTileRows * L.ldv);
-  L.wj = take((size_t)L.JP * F);
+  L.wj = take(mma ? (size_t)F * L.ldj : (size_t)L.JP * F);
   L.wv = take(shared ? 0 : Fv);
   L.bias = take(L.JP);
   // phase-2 partials; after the last tile the same space holds the final reductions
   // (32 x 12 doubles of statistics and 32 x JP floats of gaussian scale gradient)
-  const size_t red_a = (size_t)kHeadWarps * kTileRows * L.JP;
+  const size_t red_a = (size_t)(mma ? 1 : kHeadWarps) * kTileRows * L.JP;
   const size_t red_b = (size_t)kTileRows * kNumStatSums * 2 + (size_t)kTileRows * L.JP;
   L.red = take(red_a > red_b ? red_a : red_b);
   L.vred = take(shared ? 0 : (size_t)kHeadWarps * kTileRows);
-  L.d = take((size_t)kTileRows * L.JP);
+  L.d = take((size_t)kTileRows * L.ldd);
   L.sig = take(L.JP);
   L.isig = take(L.JP);
   L.lsig = take(L.JP);
@@ -88,8 +99,20 @@ bool heads_fuse_dw(int F_pi, int F_v, int A, bool /*shared*/) {
   return A + 1 <= 16 && F_pi <= kHeadThreads && F_v <= kHeadThreads;
 }
 
+// Whether the instance serving these heads runs its products on tensor cores: wide heads
+// without the fused weight gradient, features in whole 16-column steps, and the layout within
+// the 227 KB of shared memory.
+static bool heads_use_mma(int F_pi, int F_v, int A, bool shared, bool fuse) {
+  const int jp = heads_inst_jp(A, fuse);
+  if (fuse || jp < 32 || F_pi % 16 != 0) return false;
+  return heads_layout(F_pi, F_v, A, shared, jp, true).total * sizeof(float) <= 227 * 1024;
+}
+
 static size_t heads_smem_for(int F_pi, int F_v, int A, bool shared, bool fuse) {
-  return heads_layout(F_pi, F_v, A, shared, heads_inst_jp(A, fuse)).total * sizeof(float);
+  return heads_layout(F_pi, F_v, A, shared, heads_inst_jp(A, fuse),
+                      heads_use_mma(F_pi, F_v, A, shared, fuse))
+             .total *
+         sizeof(float);
 }
 
 size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared) {
@@ -174,7 +197,7 @@ __device__ __forceinline__ void stage_features(const float* pre, int F, int ld, 
 template <int JP, int Act>
 __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int row0,
                                                    int live, int rows_cap, const float* d_s,
-                                                   const float* w_s, int nj, int jcol,
+                                                   int ldd, const float* w_s, int nj, int jcol,
                                                    float* df, __nv_bfloat16* dfb,
                                                    __nv_bfloat16* dfb_lo) {
   const int q4 = F / 4, total = kTileRows * q4;
@@ -203,7 +226,7 @@ __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int 
       if (nj > 1) {
 #pragma unroll 4
         for (int j = 0; j < JP; ++j) {
-          const float dj = d_s[r * JP + j];
+          const float dj = d_s[r * ldd + j];
           const float4 wv = *reinterpret_cast<const float4*>(w_s + (size_t)j * F + 4 * q);
           g.x = fmaf(dj, wv.x, g.x);
           g.y = fmaf(dj, wv.y, g.y);
@@ -211,7 +234,7 @@ __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int 
           g.w = fmaf(dj, wv.w, g.w);
         }
       } else {
-        const float dj = d_s[r * JP + jcol];
+        const float dj = d_s[r * ldd + jcol];
         const float4 wv = *reinterpret_cast<const float4*>(w_s + 4 * q);
         g = make_float4(dj * wv.x, dj * wv.y, dj * wv.z, dj * wv.w);
       }
@@ -231,13 +254,105 @@ __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int 
   }
 }
 
-template <int JP, bool FUSE, int ACT>
+// Phase 2 on tensor cores (MMA instances): out[32][JP] = f[32][F] W[F][JP] in split bf16.
+// Warp w takes m-tile w % 2 (16 rows) and the n-tiles w / 2 and w / 2 + 4 (8 outputs each).
+template <int JP>
+__device__ __forceinline__ void heads_outputs_mma(const float* f_s, int ldf, const float* wj_s,
+                                                  int ldj, int F, float* out_s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3, mt = warp & 1, nt0 = warp >> 1;
+  constexpr int NT = JP / 8;
+  float acc[2][4] = {};
+  const float* a0 = f_s + (mt * 16 + gid) * ldf + 2 * tig;
+  const float* a1 = a0 + 8 * ldf;
+  for (int ks = 0; ks < F / 16; ++ks) {
+    uint32_t ah[4], al[4];
+    load_a_split(a0 + 16 * ks, a1 + 16 * ks, ah, al);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int nt = nt0 + 4 * i;
+      if (nt >= NT) continue;
+      const float* b = wj_s + (16 * ks + 2 * tig) * ldj + nt * 8 + gid;
+      uint32_t bh[2], bl[2];
+      split_pair(b[0], b[ldj], bh[0], bl[0]);
+      split_pair(b[8 * ldj], b[9 * ldj], bh[1], bl[1]);
+      mma_split(acc[i], ah, al, bh, bl);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int nt = nt0 + 4 * i;
+    if (nt >= NT) continue;
+    float* o = out_s + (mt * 16 + gid) * JP + nt * 8 + 2 * tig;
+    o[0] = acc[i][0];
+    o[1] = acc[i][1];
+    o[8 * JP] = acc[i][2];
+    o[8 * JP + 1] = acc[i][3];
+  }
+}
+
+// Phase 4 of the actor tower on tensor cores (MMA instances): dL/d pre [32][F] =
+// (d[32][JP] W^T) * act'(pre), stored as fp32 or bf16 (hi/lo). Warp w takes m-tile w % 2 and
+// the feature n-tiles w / 2, w / 2 + 4, ...; the d fragments stay in registers across them.
+template <int JP, int Act>
+__device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, int row0,
+                                                       int live, int rows_cap, const float* d_s,
+                                                       int ldd, const float* wj_s, int ldj,
+                                                       float* df, __nv_bfloat16* dfb,
+                                                       __nv_bfloat16* dfb_lo) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3, mt = warp & 1;
+  constexpr int KD = JP / 16;
+  uint32_t dh[KD][4], dl[KD][4];
+  const float* a0 = d_s + (mt * 16 + gid) * ldd + 2 * tig;
+#pragma unroll
+  for (int kd = 0; kd < KD; ++kd) load_a_split(a0 + 16 * kd, a0 + 8 * ldd + 16 * kd, dh[kd], dl[kd]);
+  for (int nt = warp >> 1; nt < F / 8; nt += 4) {
+    float acc[4] = {};
+    const float* wb = wj_s + (nt * 8 + gid) * ldj + 2 * tig;
+#pragma unroll
+    for (int kd = 0; kd < KD; ++kd) {
+      const float2 b0 = *reinterpret_cast<const float2*>(wb + 16 * kd);
+      const float2 b1 = *reinterpret_cast<const float2*>(wb + 16 * kd + 8);
+      uint32_t bh[2], bl[2];
+      split_pair(b0.x, b0.y, bh[0], bl[0]);
+      split_pair(b1.x, b1.y, bh[1], bl[1]);
+      mma_split(acc, dh[kd], dl[kd], bh, bl);
+    }
+    const int c = nt * 8 + 2 * tig;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = row0 + mt * 16 + gid + 8 * h;
+      if (row >= rows_cap) continue;
+      float2 g = make_float2(acc[2 * h], acc[2 * h + 1]);
+      if constexpr (Act != BT_ACT_NONE) {
+        float2 z = make_float2(0.f, 0.f);
+        if (row < live) z = __ldg(reinterpret_cast<const float2*>(pre + (size_t)row * F + c));
+        g.x *= act_dz<Act>(z.x);
+        g.y *= act_dz<Act>(z.y);
+      }
+      const size_t e = (size_t)row * F + c;
+      if (dfb) {
+        const __nv_bfloat162 hv = __floats2bfloat162_rn(g.x, g.y);
+        *reinterpret_cast<__nv_bfloat162*>(dfb + e) = hv;
+        if (dfb_lo)
+          *reinterpret_cast<__nv_bfloat162*>(dfb_lo + e) =
+              __floats2bfloat162_rn(g.x - __low2float(hv), g.y - __high2float(hv));
+      } else {
+        *reinterpret_cast<float2*>(df + e) = g;
+      }
+    }
+  }
+}
+
+template <int JP, bool FUSE, int ACT, bool MMA>
 __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams p) {
   constexpr int JJ = (JP + 7) / 8;  // outputs per thread in the loss phase
+  static_assert(!MMA || (!FUSE && JP % 16 == 0), "tensor-core heads: wide, unfused");
   extern __shared__ __align__(16) float sm[];
   const int F = p.F_pi, Fv = p.F_v, A = p.A;
   const bool shared = (p.f_v == p.f_pi);
-  const HeadsLayout Lo = heads_layout(F, Fv, A, shared, JP);
+  const HeadsLayout Lo = heads_layout(F, Fv, A, shared, JP, MMA);
   float* f_s = sm + Lo.f;
   float* fv_s = sm + Lo.fv;
   float* wj_s = sm + Lo.wj;
@@ -258,11 +373,18 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
   // head kernels as columns wj[j][k] (j < A actor outputs, j = A the value when the torso
   // is shared, the rest zero), biases, gaussian constants
   for (int i = tid; i < JP * F; i += kHeadThreads) {
-    const int j = i / F, k = i - j * F;
+    int j, k;
+    if constexpr (MMA) {  // feature-major: wj[k][j]
+      k = i / JP;
+      j = i - k * JP;
+    } else {
+      j = i / F;
+      k = i - j * F;
+    }
     float w = 0.f;
     if (j < A) w = p.w_pi[(size_t)k * A + j];
     else if (j == A && shared) w = p.w_v[k];
-    wj_s[i] = w;
+    wj_s[MMA ? k * Lo.ldj + j : i] = w;
   }
   if (!shared)
     for (int k = tid; k < Fv; k += kHeadThreads) wv_s[k] = p.w_v[k];
@@ -299,8 +421,24 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
     if (!shared) stage_features<ACT>(p.f_v, Fv, Lo.ldv, row0, live, fv_s);
     __syncthreads();
 
-    // 2. head outputs: warp partials over interleaved 4-feature slices
-    {
+    // 2. head outputs: warp partials over interleaved 4-feature slices (CUDA cores), or the
+    // finished outputs from the tensor cores
+    if constexpr (MMA) {
+      heads_outputs_mma<JP>(f_s, Lo.ldf, wj_s, Lo.ldj, F, red_s);
+      if (!shared) {
+        float v = 0.f;
+        const float* vrow = fv_s + lane * Lo.ldv;
+        for (int sl = warp; sl < Fv / 4; sl += kHeadWarps) {
+          const float4 x = *reinterpret_cast<const float4*>(vrow + 4 * sl);
+          const float4 w = *reinterpret_cast<const float4*>(wv_s + 4 * sl);
+          v = fmaf(x.x, w.x, v);
+          v = fmaf(x.y, w.y, v);
+          v = fmaf(x.z, w.z, v);
+          v = fmaf(x.w, w.w, v);
+        }
+        vred_s[warp * kTileRows + lane] = v;
+      }
+    } else {
       float acc[JP];
 #pragma unroll
       for (int j = 0; j < JP; ++j) acc[j] = 0.f;
@@ -347,13 +485,21 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
         float t = 0.f;
         if (j < JP) {
           t = bias_s[j];
-          for (int w = 0; w < kHeadWarps; ++w) t += red_s[(size_t)(w * kTileRows + r) * JP + j];
+          if constexpr (MMA) {
+            t += red_s[(size_t)r * JP + j];
+          } else {
+            for (int w = 0; w < kHeadWarps; ++w) t += red_s[(size_t)(w * kTileRows + r) * JP + j];
+          }
         }
         o[jj] = t;
       }
       float value = bias_s[A];
       if (shared) {
-        for (int w = 0; w < kHeadWarps; ++w) value += red_s[(size_t)(w * kTileRows + r) * JP + A];
+        if constexpr (MMA) {
+          value += red_s[(size_t)r * JP + A];
+        } else {
+          for (int w = 0; w < kHeadWarps; ++w) value += red_s[(size_t)(w * kTileRows + r) * JP + A];
+        }
       } else {
         for (int w = 0; w < kHeadWarps; ++w) value += vred_s[w * kTileRows + r];
       }
@@ -458,7 +604,7 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
           }
           if (p.d_out) p.d_out[(size_t)row * A + j] = g;
         }
-        d_s[r * JP + j] = (j == A) ? d_value : g;
+        d_s[r * Lo.ldd + j] = (j == A) ? d_value : g;
       }
       if (sub == 0 && on) {
         if (p.d_val) p.d_val[row] = d_value;
@@ -480,10 +626,15 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
     __syncthreads();
 
     // 4. dL/d pre for the towers
-    store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, wj_s, JP, 0, p.d_fpi,
-                                p.d_fpi_b, p.d_fpi_b_lo);
+    if constexpr (MMA) {
+      heads_feature_grad_mma<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, Lo.ldj,
+                                      p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
+    } else {
+      store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, JP, 0,
+                                  p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
+    }
     if (!shared)
-      store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, wv_s, 1, A, p.d_fv,
+      store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, Lo.ldd, wv_s, 1, A, p.d_fv,
                                   p.d_fv_b, p.d_fv_b_lo);
     // 5. head weight gradients
     if constexpr (FUSE) {
@@ -501,9 +652,9 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
         }
       }
       if (!shared && tid < Fv)
-        for (int rr = 0; rr < kTileRows; ++rr) accv = fmaf(fv_s[rr * Lo.ldv + tid], d_s[rr * JP + A], accv);
+        for (int rr = 0; rr < kTileRows; ++rr) accv = fmaf(fv_s[rr * Lo.ldv + tid], d_s[rr * Lo.ldd + A], accv);
       if (tid < JP)
-        for (int rr = 0; rr < kTileRows; ++rr) accb += d_s[rr * JP + tid];
+        for (int rr = 0; rr < kTileRows; ++rr) accb += d_s[rr * Lo.ldd + tid];
     }
     __syncthreads();
   }
@@ -561,9 +712,9 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
   }
 }
 
-template <int JP, bool FUSE, int ACT>
+template <int JP, bool FUSE, int ACT, bool MMA = false>
 int launch_heads_inst(const HeadsParams& p, int blocks, size_t smem, cudaStream_t stream) {
-  auto kernel = heads_loss_kernel<JP, FUSE, ACT>;
+  auto kernel = heads_loss_kernel<JP, FUSE, ACT, MMA>;
   static size_t configured = 0;
   if (smem > 48 * 1024 && smem > configured) {
     BT_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -575,13 +726,13 @@ int launch_heads_inst(const HeadsParams& p, int blocks, size_t smem, cudaStream_
 
 // The activation of the towers' last layers is a template parameter (one instance per
 // activation keeps each kernel's code small); both towers must end in the same one.
-template <int JP, bool FUSE>
+template <int JP, bool FUSE, bool MMA = false>
 int launch_heads_jp(const HeadsParams& p, int blocks, size_t smem, cudaStream_t stream) {
   switch (p.act_pi) {
-    case BT_ACT_TANH: return launch_heads_inst<JP, FUSE, BT_ACT_TANH>(p, blocks, smem, stream);
-    case BT_ACT_RELU: return launch_heads_inst<JP, FUSE, BT_ACT_RELU>(p, blocks, smem, stream);
-    case BT_ACT_SILU: return launch_heads_inst<JP, FUSE, BT_ACT_SILU>(p, blocks, smem, stream);
-    default: return launch_heads_inst<JP, FUSE, BT_ACT_NONE>(p, blocks, smem, stream);
+    case BT_ACT_TANH: return launch_heads_inst<JP, FUSE, BT_ACT_TANH, MMA>(p, blocks, smem, stream);
+    case BT_ACT_RELU: return launch_heads_inst<JP, FUSE, BT_ACT_RELU, MMA>(p, blocks, smem, stream);
+    case BT_ACT_SILU: return launch_heads_inst<JP, FUSE, BT_ACT_SILU, MMA>(p, blocks, smem, stream);
+    default: return launch_heads_inst<JP, FUSE, BT_ACT_NONE, MMA>(p, blocks, smem, stream);
   }
 }
 
@@ -606,6 +757,11 @@ int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
     return launch_heads_jp<16, true>(p, blocks, smem, stream);
   }
   if (jp <= 16) return launch_heads_jp<16, false>(p, blocks, smem, stream);
+  if (heads_use_mma(p.F_pi, p.F_v, p.A, shared, false)) {
+    if (jp <= 32) return launch_heads_jp<32, false, true>(p, blocks, smem, stream);
+    if (jp <= 48) return launch_heads_jp<48, false, true>(p, blocks, smem, stream);
+    return launch_heads_jp<64, false, true>(p, blocks, smem, stream);
+  }
   if (jp <= 32) return launch_heads_jp<32, false>(p, blocks, smem, stream);
   if (jp <= 48) return launch_heads_jp<48, false>(p, blocks, smem, stream);
   return launch_heads_jp<64, false>(p, blocks, smem, stream);

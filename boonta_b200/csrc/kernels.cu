@@ -823,6 +823,8 @@ int launch_skinny_dw(const float* f, int F, int act, const float* d, int n, int 
     launch_skinny_n<16>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   } else if (n <= 32) {
     launch_skinny_n<32>(grid, f, F, act, d, n, rows, count, rps, out, stream);
+  } else if (n <= 48) {
+    launch_skinny_n<48>(grid, f, F, act, d, n, rows, count, rps, out, stream);
   } else {
     BT_CHECK_ARG(n <= 64, "skinny dW with %d outputs", n);
     launch_skinny_n<64>(grid, f, F, act, d, n, rows, count, rps, out, stream);
