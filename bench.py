@@ -139,9 +139,10 @@ def roofline(w, prof: dict, pk: dict, pk_kind: str) -> dict:
 # launch, that launch's algorithmic bytes)}, from the ncu --set full captures summarised in
 # profiles/<class>_<workload>_<precision>.md.
 TRAFFIC = {
-    ("c2_brax", "bf16x3", "gemm_dw"): (34.11e6, 35.9e6),    # a 256-wide layer
-    ("c2_brax", "bf16x3", "gemm_fwd"): (6.05e6, 39.4e6),    # first layer, outputs stay in L2
-    ("c2_brax", "bf16x3", "heads_loss"): (42.2e6, 67.8e6),
+    ("c2_brax", "bf16x3", "gemm_fwd"): (17.93e6, 50.6e6),   # a 256-wide layer; outputs stay in L2
+    ("c2_brax", "bf16x3", "gemm_dx"): (33.96e6, 50.6e6),    # a 256-wide layer; outputs stay in L2
+    ("c2_brax", "bf16x3", "gemm_dw"): (34.11e6, 39.9e6),    # a 256-wide layer
+    ("c2_brax", "bf16x3", "heads_loss"): (43.23e6, 101.6e6),
 }
 
 
