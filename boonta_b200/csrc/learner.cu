@@ -666,11 +666,13 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
     hp.dw_v_partials = L->head_v_part;
   }
   BT_K(L, kProfHeads, s, launch_heads_loss(hp, L->heads_blocks, s));
-  BT_K(L, kProfStats, s, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, s));
-  // head weight gradients when not fused: [F + 1, A] = [f, 1]^T d_out and
-  // [F + 1, 1] = [f, 1]^T d_value, on a side stream next to the towers' backward
+  // The statistics reduction and the head weight gradients (when not fused: [F + 1, A] =
+  // [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value) run on a side stream next to the
+  // towers' backward; it joins the caller's stream before the gradient reduction, so the
+  // next minibatch's heads kernel finds the partial sums consumed.
   cudaStream_t sh = side_stream(L, 3, s);
   BT_TRY(stream_dep(L, s, sh));
+  BT_K(L, kProfStats, sh, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, sh));
   if (!L->heads_fused_dw) {
     BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_pi.pre(), L->F_pi, last_pi.act, L->d_out,
                                               L->A, rows, in.count, L->head_pi_splits,
