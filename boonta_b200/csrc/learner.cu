@@ -201,7 +201,6 @@ int allocate(bt_learner* L) {
   L->T = c.num_steps;
   L->N = c.num_envs;
   L->B = (int64_t)L->T * L->N;
-  const int64_t B_global = L->B * world;
   BT_CHECK_ARG(M >= 1 && E >= 1, "num_minibatches %d / update_epochs %d", M, E);
   // Minibatches are over samples (t, n), or over whole env sequences for a recurrent torso
   // (recurrent_ppo.py:269-276); `units` is what the permutation runs over.
