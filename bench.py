@@ -1,6 +1,6 @@
 """Benchmark of the PPO learner step (boonta PPO.update) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl native|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5] [--impl native|reference]
 
 Metric: learner env-steps/s = world * T * N / t_update (the reference's `update/SPS`,
 hangar/scripts/benchmark_boonta.py:154-177, 214), weak scaling (N envs per GPU fixed).
@@ -33,7 +33,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 from boonta_b200 import configs  # noqa: E402
-from boonta_b200.spec import Conv3x3, Dense, init_params, param_layout  # noqa: E402
+from boonta_b200.spec import GRU, Conv3x3, Dense, init_params, param_layout  # noqa: E402
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -51,9 +51,13 @@ def class_work(w) -> dict:
     """{kernel class: (FLOPs, bytes)} of one learner update, counted algorithmically: every
     GEMM as 2*M*N*K (the split-bf16 mode issues three products per term; they are not
     counted), every operand read once and every output written once, in the precision the
-    path stores it (bf16 2 B, split-bf16 pairs 4 B, fp32 4 B)."""
+    path stores it (bf16 2 B, split-bf16 pairs 4 B, fp32 4 B). A GRU layer (fp32) counts its
+    input projection [x, 1] W_i and its recurrence h W_h (forward), the recurrence's carry
+    products and the GRU input's gradient (dX), and the three weight gradients (dW); its
+    gate arithmetic is not counted."""
     net = w.network
-    rows = w.minibatch_size
+    # rows of one minibatch: samples, or whole env sequences times T (recurrent)
+    rows = w.minibatch_size * (w.num_steps if net.recurrent else 1)
     steps = w.ppo.update_epochs * w.ppo.num_minibatches
     tc = w.precision in ("bf16", "bf16x3")
     e = {"fp32": 4, "bf16": 2, "bf16x3": 4}[w.precision]
@@ -63,6 +67,18 @@ def class_work(w) -> dict:
         dim = net.obs_dim
         for i, layer in enumerate(tower):
             last = i + 1 == len(tower)
+            if isinstance(layer, GRU):
+                h = layer.features
+                g3 = 3 * h
+                out["gemm_fwd"][0] += 2.0 * rows * ((dim + 1) * g3 + h * g3)
+                # x read, xp written and re-read, the carry-in, output and three gates written
+                out["gemm_fwd"][1] += rows * (dim * 4 + g3 * 8 + 5 * h * 4) + ((dim + 1) + h) * g3 * 4
+                out["gemm_dx"][0] += 2.0 * rows * (h * g3 + dim * g3)
+                out["gemm_dx"][1] += rows * (g3 * 8 + 6 * h * 4 + dim * 4) + (h + dim) * g3 * 4
+                out["gemm_dw"][0] += 2.0 * rows * ((dim + 1) * g3 + h * g3 + h)
+                out["gemm_dw"][1] += rows * (dim * 4 + g3 * 8 + 2 * h * 4) + ((dim + 1) + h + 1) * g3 * 4
+                dim = h
+                continue
             if isinstance(layer, Conv3x3):
                 m = rows * layer.height * layer.width
                 k, n = 9 * layer.in_channels + 1, layer.features
@@ -80,7 +96,7 @@ def class_work(w) -> dict:
             out["gemm_fwd"][1] += a_bytes + w_bytes + out_fwd
             dz_bytes = rows * width * (e if tc else 4)
             out["gemm_dw"][0] += 2.0 * m * k * n
-            out["gemm_dw"][1] += dz_bytes + a_bytes + rows * 0 + k * n * 4
+            out["gemm_dw"][1] += dz_bytes + a_bytes + k * n * 4
             if i > 0:
                 out["gemm_dx"][0] += 2.0 * m * (k - 1) * n
                 out["gemm_dx"][1] += dz_bytes + w_bytes + rows * dim * (4 + (e if tc else 4))
@@ -97,6 +113,25 @@ def class_work(w) -> dict:
     out["head_dw"][0] += 2.0 * rows * ((f_pi + 1) * a + (f_v + 1))
     out["head_dw"][1] += rows * (f_pi + f_v) * 4 + rows * (a + 1) * 4
     return {k: (v[0] * steps, v[1] * steps) for k, v in out.items()}
+
+
+def class_table(w, prof: dict, pk: dict) -> dict:
+    """Every profiled kernel class with its device time per update, achieved TFLOP/s against
+    the measured sustained bf16 peak and achieved GB/s of algorithmic bytes against the
+    measured copy bandwidth."""
+    work = class_work(w)
+    tflops_peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    out = {}
+    for cls, (ms, n) in sorted(prof.items(), key=lambda kv: -kv[1][0]):
+        row = {"ms": ms, "launches": n}
+        if cls in work and ms > 0:
+            flops, nbytes = work[cls]
+            row["tflops"] = flops / (ms / 1e3) / 1e12
+            row["frac_bf16_sustained"] = row["tflops"] / tflops_peak
+            row["gbs"] = nbytes / (ms / 1e3) / 1e9
+            row["frac_hbm"] = row["gbs"] / pk["hbm_gbs"]
+        out[cls] = row
+    return out
 
 
 def roofline(w, prof: dict, pk: dict, pk_kind: str) -> dict:
@@ -311,67 +346,148 @@ class ClockSampler:
 
 
 # ---- CPU baseline (the reference's algorithm on the host) -----------------------------------
-def cpu_baseline(w, budget_s: float = 15.0) -> dict:
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def bench_config(w, world: int) -> dict:
+    """The workload description both arms print (identical keys and values)."""
+    return {"workload": w.name, "T": w.num_steps, "N_per_gpu": w.num_envs,
+            "epochs": w.ppo.update_epochs, "minibatches": w.ppo.num_minibatches,
+            "minibatch_rows": w.minibatch_size * (w.num_steps if w.network.recurrent else 1),
+            "precision": w.precision, "parallelism": f"dp{world}",
+            "l2": ("inputs larger than L2 (obs rollout "
+                   f"{w.batch_size * w.network.obs_dim * 4 / 1e6:.0f} MB per GPU)"),
+            "description": w.description}
+
+
+def _host_minibatch(w, seed: int = 77) -> dict:
+    """One full-size minibatch of the workload on the host (its rows only), in the oracle's
+    input layout: flat samples, or whole env sequences [envs, T] for a recurrent network."""
+    if w.network.recurrent:
+        sub = w.scaled(num_envs=w.minibatch_size)
+        roll = configs.rollout(sub, seed=seed)
+        tr = lambda a: np.moveaxis(a, 0, 1)  # [T, N, ...] -> [N, T, ...]
+        rng = np.random.default_rng(seed + 1)
+        return {"obs": tr(roll["obs"]), "done": tr(roll["first_done"]),
+                "action": tr(roll["action"]), "log_prob": tr(roll["log_prob"]),
+                "value": tr(roll["value"]),
+                "advantages": rng.standard_normal(roll["value"].shape, dtype=np.float32).T,
+                "returns": rng.standard_normal(roll["value"].shape, dtype=np.float32).T,
+                "carry": roll["carry"]}
+    rows = w.minibatch_size
+    rng = np.random.default_rng(seed)
+    a = w.network.action_dim
+    mb = {"obs": configs._obs(rng, w, (rows, w.network.obs_dim))}
+    if w.network.head == "gaussian":
+        mb["action"] = rng.standard_normal((rows, a), dtype=np.float32)
+        mb["log_prob"] = (-0.5 * mb["action"] ** 2 - 0.9189385).sum(-1).astype(np.float32)
+    else:
+        mb["action"] = rng.integers(0, a, rows, dtype=np.int32)
+        mb["log_prob"] = np.full(rows, np.log(1.0 / a), np.float32)
+    for k in ("value", "advantages", "returns"):
+        mb[k] = rng.standard_normal(rows, dtype=np.float32)
+    return mb
+
+
+_HOST_INPUTS: dict = {}
+
+
+def _host_inputs(w):
+    """The host rollout (without its [T, N, D] observations unless the network is recurrent)
+    and one full-size minibatch, made once per workload and reused by every timed sample."""
+    if w.name not in _HOST_INPUTS:
+        _HOST_INPUTS[w.name] = (configs.rollout(w, include_obs=w.network.recurrent),
+                                _host_minibatch(w))
+    return _HOST_INPUTS[w.name]
+
+
+def cpu_baseline(w, budget_s: float = 4.0) -> dict:
+    """The reference's algorithm (the NumPy port in oracle/, float32) on the host cores, on a
+    bounded sample of one update of the workload: the bootstrap value and GAE over the whole
+    [T, N] rollout, then minibatch steps of the full minibatch size (forward, loss, backward,
+    clip + Adam) until `budget_s` is spent (at least one). One update's time is extrapolated
+    as targets + (E x M) x the mean minibatch step; `value` = T*N / that time."""
+    from oracle import gae as ogae
+    from oracle import network as onet
     from oracle import optim
     from oracle import ppo as oppo
     from oracle import recurrent as orec
 
-    # the recurrent learner step (env-minibatches, GRU) for recurrent networks
-    step = orec.update if w.network.recurrent else oppo.update
+    threads = host_threads()
+    try:
+        from threadpoolctl import threadpool_limits
 
-    threads = len(os.sched_getaffinity(0))
-    rng_w = w
-    roll = configs.rollout(rng_w) if w.batch_size * w.network.obs_dim < 6e8 else None
-    if roll is None:  # C5: a full-size host rollout is 8.7 GB; sample 1/16 of the envs
-        rng_w = w.scaled(num_envs=max(w.num_envs // 16, w.ppo.num_minibatches))
-        roll = configs.rollout(rng_w)
+        limiter = threadpool_limits(limits=threads)
+    except Exception:
+        limiter = None
     params = init_params(w.network, seed=0, init=w.init)
-    perms = configs.permutations(rng_w)
-    # GAE + bootstrap alone
+    opt_state = optim.init_state(params)
+    roll, mb = _host_inputs(w)
+    wall0 = time.perf_counter()
     t0 = time.perf_counter()
-    step(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
-         max_minibatches=0)
-    t_gae = time.perf_counter() - t0
-    # minibatch steps until the budget is used (at least one)
-    mb_ratio = w.minibatch_size / rng_w.minibatch_size
+    if w.network.recurrent:
+        seq_obs = np.stack([roll["obs"][-1], roll["bootstrap_obs"]], axis=1)
+        second_done = roll["terminated"][-1] | roll["truncated"][-1]
+        seq_done = np.stack([roll["first_done"][-1], second_done], axis=1)
+        _, v2, _ = orec.forward_seq(w.network, params, seq_obs, seq_done, roll["last_carry"])
+        boot = v2[:, -1]
+    else:
+        _, boot, _ = onet.forward(w.network, params, roll["bootstrap_obs"])
+    ogae.gae(roll["reward"], roll["terminated"], roll["truncated"], roll["value"], boot,
+             w.ppo.gamma, w.ppo.gae_lambda)
+    t_targets = time.perf_counter() - t0
     done, t_mb = 0, 0.0
-    while done < w.ppo.update_epochs * w.ppo.num_minibatches:
+    total = w.ppo.update_epochs * w.ppo.num_minibatches
+    while done < total:
         t0 = time.perf_counter()
-        step(w.network, w.ppo, w.optimizer, params, optim.init_state(params), roll, perms,
-             max_minibatches=done + 1)
-        t_mb = time.perf_counter() - t0 - t_gae
+        if w.network.recurrent:
+            traj = {k: v for k, v in mb.items() if k != "carry"}
+            _, _, grads = orec.loss_and_grads(w.network, w.ppo, params, traj, mb["carry"])
+        else:
+            _, _, grads = oppo.loss_and_grads(w.network, w.ppo, params, mb)
+        params, opt_state = optim.clip_adam(params, grads, opt_state, w.optimizer)
+        t_mb += time.perf_counter() - t0
         done += 1
-        if t_mb * 1 > budget_s / 4 or t_mb > budget_s / (done + 1):
+        if t_targets + t_mb >= budget_s:
             break
-    per_mb = max(t_mb, 1e-9) / done * mb_ratio
-    t_update = t_gae * (w.batch_size / rng_w.batch_size) + per_mb * w.ppo.update_epochs * w.ppo.num_minibatches
-    value = w.batch_size / t_update
-    return {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
-            "sample": (f"NumPy oracle (float32, BLAS threads={threads}) on the {rng_w.name} "
-                       f"rollout T={rng_w.num_steps} N={rng_w.num_envs}: bootstrap+GAE plus {done} "
-                       f"of {w.ppo.update_epochs * w.ppo.num_minibatches} minibatch steps "
-                       f"(rows scaled x{mb_ratio:g}), extrapolated to one full update")}
+    sample_s = time.perf_counter() - wall0
+    if limiter is not None:
+        limiter.unregister()
+    t_update = t_targets + t_mb / done * total
+    return {"value": w.batch_size / t_update, "unit": "env-steps/s", "cores": threads,
+            "kind": "port", "sample_s": sample_s, "minibatch_steps_timed": done,
+            "minibatch_steps_per_update": total, "extrapolated": done < total,
+            "sample": (f"NumPy oracle (float32, {threads} BLAS threads) on the {w.name} workload: "
+                       f"bootstrap + GAE over the full T={w.num_steps} x N={w.num_envs} rollout, "
+                       f"then {done} of the update's {total} minibatch steps at the full "
+                       f"minibatch size; one update's time extrapolated as targets + "
+                       f"{total} x the mean minibatch step")}
 
 
 def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps = []
+    steps, samples = [], []
     cb = None
     for _ in range(args.warmup + args.steps):
-        cb = cpu_baseline(w, budget_s=8.0)
+        cb = cpu_baseline(w)
         steps.append(cb["value"])
-    value = statistics.median(steps[args.warmup:]) if args.steps else steps[-1]
+        samples.append(cb["sample_s"])
+    timed = steps[args.warmup:] or steps[-1:]
+    value = statistics.median(timed)
     cb["value"] = value
+    sample_ms = 1000.0 * statistics.mean(samples[args.warmup:] or samples[-1:])
     line = {
         "impl": "reference", "metric": "ppo_learner_env_steps_per_sec", "value": value,
         "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * w.batch_size / value, "higher_is_better": True,
+        # each step is the bounded sample above, timed on the host; one full update's time
+        # is extrapolated from it (extrapolated_update_ms)
+        "ms_per_step": sample_ms, "extrapolated_update_ms": 1000.0 * w.batch_size / value,
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "T": w.num_steps, "N_per_gpu": w.num_envs,
-                   "epochs": w.ppo.update_epochs, "minibatches": w.ppo.num_minibatches,
-                   "description": w.description},
+        "config": bench_config(w, args.gpus),
         "cpu_baseline": cb,
         "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -384,7 +500,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c2")
+    ap.add_argument("--config", default="c5")
     ap.add_argument("--precision", default=None)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -513,13 +629,9 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": {"fp32": "f32", "bf16": "bf16", "bf16x3": "bf16x3"}[w.precision],
         "data": "synthetic",
-        "config": {"workload": w.name, "T": w.num_steps, "N_per_gpu": w.num_envs,
-                   "epochs": w.ppo.update_epochs, "minibatches": w.ppo.num_minibatches,
-                   "minibatch_rows": w.minibatch_size, "precision": w.precision,
-                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (obs rollout "
-                   f"{w.batch_size * w.network.obs_dim * 4 / 1e6:.0f} MB per GPU)",
-                   "description": w.description},
+        "config": bench_config(w, world),
         "roofline": roof,
+        "classes": class_table(w, prof, pk),
         "gae_hbm_gbs": gae_bw["gbs"],
         "gae": gae_bw,
         "kernel_ms_per_step": {k: v[0] for k, v in sorted(prof.items())},

@@ -191,13 +191,17 @@ def _obs(rng, w: Workload, shape):
     return rng.standard_normal(shape, dtype=np.float32)
 
 
-def rollout(w: Workload, seed: int | None = None) -> dict:
-    """One seeded learner input (numpy arrays, host memory)."""
+def rollout(w: Workload, seed: int | None = None, include_obs: bool = True) -> dict:
+    """One seeded learner input (numpy arrays, host memory). With `include_obs=False` the
+    `[T, N, D]` observations are left out (the caller makes them elsewhere, e.g. on the
+    device for a rollout too large for host-side checking); the other leaves then come from
+    a different point of the random stream."""
     rng = np.random.default_rng(w.seed if seed is None else seed)
     t, n, d = w.num_steps, w.num_envs, w.network.obs_dim
     a = w.network.action_dim
     out = {}
-    out["obs"] = _obs(rng, w, (t, n, d))
+    if include_obs:
+        out["obs"] = _obs(rng, w, (t, n, d))
     out["bootstrap_obs"] = _obs(rng, w, (n, d))
     if w.network.head == "gaussian":
         out["action"] = rng.standard_normal((t, n, a), dtype=np.float32)

@@ -9,7 +9,7 @@ import bench
 from boonta_b200 import configs
 
 # MFLOP per env-step: 2 x MACs per sample per epoch x epochs (+ the bootstrap forward)
-EXPECTED_MFLOP = {"c1": 0.1071, "c2": 7.07, "c3": 5.87, "c5": 81.0}
+EXPECTED_MFLOP = {"c1": 0.1071, "c2": 7.07, "c3": 5.87, "c4": 4.89, "c5": 81.0}
 
 
 @pytest.mark.parametrize("name", sorted(EXPECTED_MFLOP))

@@ -1,0 +1,247 @@
+"""Parity at the workloads' full sizes (C2-C5 at the T x N the benchmarks run), through the
+C-ABI, against the CPU oracle.
+
+Three checks per workload, each on the precision the workload benchmarks with:
+
+  * targets over the whole rollout: the bootstrap values V(second.obs[T-1])
+    (boonta/algorithms/ppo.py:208-212; the GRU tail bootstrap of
+    boonta/algorithms/recurrent_ppo.py:188-198 for C4) against the oracle's forward pass,
+    and the advantages / returns against the oracle's GAE
+    (boonta/algorithms/advantage_estimators.py:8-56) evaluated on the learner's own
+    bootstrap values, which isolates the scan (1e-5 relative, the fp32 bound);
+  * the loss gradient of one full-size minibatch (16,384 rows for C2 and C5, 65,536 for
+    C3; ppo.py:148-157) per parameter tensor;
+  * one full update with update_epochs = 1 (every minibatch of one epoch, with clip + Adam
+    after each, ppo.py:205-233): the parameters and the logged statistics. C5's host-side
+    oracle cannot hold its 8.7 GB rollout, so this check runs C5 with 256 envs (1/16 of
+    the benchmark's 4,096; the network, T and the minibatch count are unchanged).
+
+Tolerances. fp32 and split-bf16 (bf16x3) arithmetic are held to the fp32 bounds: gradients
+1e-4 relative per tensor (L2 norm), parameters after the update 1e-3 relative per tensor,
+and the parameter change of the update 1e-3 relative per tensor. bf16 GEMM operands (C5)
+are compared with the oracle's bf16-operand arithmetic; the bounds for them and the reason
+they are what they are are given beside BF16 below.
+"""
+import numpy as np
+import pytest
+
+from boonta_b200 import configs
+from boonta_b200.spec import init_params
+
+pytestmark = pytest.mark.gpu
+
+FP32 = {"boot": 1e-5, "grad": 1e-4, "params": 1e-3, "delta": 1e-3, "stats_rtol": 2e-3,
+        "stats_atol": 2e-4}
+# bf16 operands on both sides: the two sum the same bf16 products in different orders, so a
+# layer output that lies within ~1e-7 relative of a bf16 rounding boundary rounds to one
+# neighbour here and the other there before the next GEMM (one bf16 step, 2^-8 relative, in
+# that element). Such flips touch ~1e-4 of the activations and leave the per-tensor L2 error
+# of the gradients near 1e-4. The parameter change of an Adam step is lr * m / sqrt(v): for
+# a weight whose minibatch gradients are themselves within those flips of zero the step's
+# direction is noise on both sides, so the change is bounded in aggregate (per tensor, L2)
+# rather than element by element.
+BF16 = {"boot": 1e-3, "grad": 1e-3, "params": 1e-4, "delta": 5e-2, "stats_rtol": 1e-2,
+        "stats_atol": 2e-3, "clipfrac_atol": 1e-2}
+
+
+def _tol(w):
+    return BF16 if w.precision == "bf16" else FP32
+
+
+def _oracle_precision(w):
+    return "bf16" if w.precision == "bf16" else "fp32"
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _one_epoch(w):
+    return w.scaled(update_epochs=1)
+
+
+def _device_obs(w, seed):
+    """The [T, N, D] observations made on the device with the workload's distribution."""
+    import torch
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    shape = (w.num_steps, w.num_envs, w.network.obs_dim)
+    if w.obs_kind == "sparse_uniform":
+        x = torch.rand(shape, generator=g, device="cuda")
+        keep = torch.rand(shape, generator=g, device="cuda") >= w.obs_sparsity
+        return torch.where(keep, x, torch.zeros((), device="cuda"))
+    if w.obs_kind == "bernoulli":
+        return (torch.rand(shape, generator=g, device="cuda") < 1 - w.obs_sparsity).float()
+    return torch.randn(shape, generator=g, device="cuda")
+
+
+def _rollout(w):
+    """Host rollout plus its device copy. Observations too large for the host (C5) are made
+    on the device only; the host dict then has no "obs" (the targets need only the
+    bootstrap observation)."""
+    from boonta_b200.learner import to_device
+
+    big = w.batch_size * w.network.obs_dim > 6e8
+    roll = configs.rollout(w, include_obs=not big)
+    dev = to_device(roll)
+    if big:
+        dev["obs"] = _device_obs(w, seed=w.seed + 50)
+    return roll, dev
+
+
+@pytest.mark.parametrize("name", ["c2", "c3", "c4", "c5"])
+def test_full_size_targets(name):
+    import torch
+
+    from boonta_b200.learner import Learner
+    from oracle import gae as ogae
+    from oracle import network as onet
+    from oracle import recurrent as orec
+
+    w = _one_epoch(configs.make(name))
+    tol = _tol(w)
+    lrn = Learner.from_workload(w)
+    params = init_params(w.network, seed=7, init=w.init)
+    lrn.set_state(params)
+    roll, dev = _rollout(w)
+    perms = torch.as_tensor(configs.permutations(w))
+    lrn.update(dev, perms, stats=False)
+    adv, ret, boot = lrn.targets()
+    torch.cuda.synchronize()
+    adv = adv.cpu().numpy().reshape(w.num_steps, w.num_envs)
+    ret = ret.cpu().numpy().reshape(w.num_steps, w.num_envs)
+    boot = boot.cpu().numpy()
+
+    if w.network.recurrent:
+        seq_obs = np.stack([roll["obs"][-1], roll["bootstrap_obs"]], axis=1)
+        second_done = roll["terminated"][-1] | roll["truncated"][-1]
+        seq_done = np.stack([roll["first_done"][-1], second_done], axis=1)
+        _, v2, _ = orec.forward_seq(w.network, params, seq_obs, seq_done, roll["last_carry"])
+        oboot = v2[:, -1]
+    else:
+        _, oboot, _ = onet.forward(w.network, params, roll["bootstrap_obs"],
+                                   _oracle_precision(w))
+    rel_boot = _rel(boot, oboot)
+    print(f"{w.name} bootstrap rel {rel_boot:.3e}")
+    assert rel_boot <= tol["boot"], rel_boot
+
+    # the scan itself, on the learner's own bootstrap values
+    oadv, oret = ogae.gae(roll["reward"], roll["terminated"], roll["truncated"], roll["value"],
+                          boot, w.ppo.gamma, w.ppo.gae_lambda)
+    np.testing.assert_allclose(adv, oadv, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(ret, oret, rtol=1e-5, atol=1e-6)
+
+
+def _flat_minibatch(w, rows, seed):
+    """One minibatch as a flat rollout of `rows` samples (its own index space 0..rows-1), so
+    that a full-size minibatch needs only its own rows on the host."""
+    rng = np.random.default_rng(seed)
+    d, a = w.network.obs_dim, w.network.action_dim
+    obs = configs._obs(rng, w, (rows, d))
+    if w.network.head == "gaussian":
+        action = rng.standard_normal((rows, a), dtype=np.float32)
+        lp = (-0.5 * action ** 2 - 0.5 * np.log(2 * np.pi)).sum(-1)
+        lp = (lp + 0.05 * rng.standard_normal(rows)).astype(np.float32)
+    else:
+        action = rng.integers(0, a, rows, dtype=np.int32)
+        lp = (np.log(1.0 / a) + 0.05 * rng.standard_normal(rows)).astype(np.float32)
+    return {
+        "obs": obs,
+        "bootstrap_obs": obs[: w.num_envs] if rows >= w.num_envs else obs,
+        "action": action,
+        "reward": np.zeros(rows, np.float32),
+        "terminated": np.zeros(rows, np.uint8),
+        "truncated": np.zeros(rows, np.uint8),
+        "log_prob": lp,
+        "value": rng.standard_normal(rows, dtype=np.float32),
+        "advantages": rng.standard_normal(rows, dtype=np.float32),
+        "returns": rng.standard_normal(rows, dtype=np.float32),
+    }
+
+
+@pytest.mark.parametrize("name", ["c2", "c3", "c5"])
+def test_full_size_minibatch_gradient(name):
+    import torch
+
+    from boonta_b200.learner import Learner, to_device
+    from oracle import ppo as oppo
+
+    w = configs.make(name)
+    tol = _tol(w)
+    rows = w.minibatch_size
+    lrn = Learner.from_workload(w)
+    params = init_params(w.network, seed=5, init=w.init)
+    lrn.set_state(params)
+    mb = _flat_minibatch(w, rows, seed=31)
+    idx = np.random.default_rng(32).permutation(rows).astype(np.int32)
+    dev = to_device({k: v for k, v in mb.items() if k not in ("advantages", "returns")})
+    g, st = lrn.loss_grads(dev, torch.as_tensor(mb["advantages"], device="cuda"),
+                           torch.as_tensor(mb["returns"], device="cuda"), torch.as_tensor(idx))
+    torch.cuda.synchronize()
+    g = lrn.layout.unflatten(g.cpu().numpy())
+    omb = {k: mb[k][idx] for k in ("obs", "action", "log_prob", "value", "advantages", "returns")}
+    _, ost, og = oppo.loss_and_grads(w.network, w.ppo, params, omb,
+                                     precision=_oracle_precision(w))
+    for k in og:
+        print(f"{w.name} rows {rows} gradient {k} rel {_rel(g[k], og[k]):.3e}")
+    for k in og:
+        assert _rel(g[k], og[k]) <= tol["grad"], (k, _rel(g[k], og[k]))
+    np.testing.assert_allclose(st.cpu().numpy(), ost, rtol=tol["stats_rtol"] / 10,
+                               atol=tol["stats_atol"] / 10)
+
+
+def _update_workload(name):
+    w = _one_epoch(configs.make(name))
+    if name == "c5":
+        # the host oracle cannot hold the full 8.7 GB C5 rollout: 256 envs (1/16)
+        w = w.scaled(num_envs=256)
+    return w
+
+
+@pytest.mark.parametrize("name", ["c2", "c3", "c4", "c5"])
+def test_full_size_update_one_epoch(name):
+    import torch
+
+    from boonta_b200.learner import Learner, to_device
+    from oracle import optim
+    from oracle import ppo as oppo
+    from oracle import recurrent as orec
+
+    w = _update_workload(name)
+    tol = _tol(w)
+    lrn = Learner.from_workload(w)
+    params = init_params(w.network, seed=3, init=w.init)
+    lrn.set_state(params)
+    roll = configs.rollout(w)
+    perms = configs.permutations(w)
+    st = lrn.update(to_device(roll), torch.as_tensor(perms))
+    torch.cuda.synchronize()
+    new = lrn.params()
+    stats = st.cpu().numpy()
+    if w.network.recurrent:
+        op, _, ostats, _ = orec.update(w.network, w.ppo, w.optimizer, params,
+                                       optim.init_state(params), roll, perms)
+    else:
+        op, _, ostats, _ = oppo.update(w.network, w.ppo, w.optimizer, params,
+                                       optim.init_state(params), roll, perms,
+                                       precision=_oracle_precision(w))
+    for k in op:
+        dn = new[k].astype(np.float64) - params[k]
+        do = op[k].astype(np.float64) - params[k]
+        print(f"{w.name} T={w.num_steps} N={w.num_envs} {k} params rel {_rel(new[k], op[k]):.3e} "
+              f"change rel {_rel(dn, do):.3e} |p| {np.linalg.norm(params[k]):.3e} "
+              f"|change| {np.linalg.norm(do):.3e}")
+    for k in op:
+        d_native = new[k].astype(np.float64) - params[k]
+        d_oracle = op[k].astype(np.float64) - params[k]
+        assert _rel(new[k], op[k]) <= tol["params"], (k, _rel(new[k], op[k]))
+        assert _rel(d_native, d_oracle) <= tol["delta"], (k, _rel(d_native, d_oracle))
+    clip = 3  # actor/clip_fraction
+    other = [i for i in range(stats.shape[-1]) if i != clip]
+    np.testing.assert_allclose(stats[..., other], ostats[..., other], rtol=tol["stats_rtol"],
+                               atol=tol["stats_atol"])
+    np.testing.assert_allclose(stats[..., clip], ostats[..., clip], rtol=0,
+                               atol=tol.get("clipfrac_atol", tol["stats_atol"]))

@@ -47,6 +47,11 @@ def small(name: str, t: int, n: int, epochs: int, minibatches: int, **kw):
     return w.scaled(num_steps=t, num_envs=n, num_minibatches=minibatches, update_epochs=epochs)
 
 
+def normalized(w):
+    """The same workload with normalize_advantage=True (boonta/algorithms/ppo.py:220-221)."""
+    return dataclasses.replace(w, ppo=dataclasses.replace(w.ppo, normalize_advantage=True))
+
+
 CASES = {
     "c1": lambda: configs.c1(),  # full size: CPU-runnable reference case
     "c2": lambda: small("c2", 8, 256, 2, 4, precision="fp32"),
@@ -60,6 +65,9 @@ CASES = {
     # fp32 conv kernels handing bf16 operands to a tensor-core dense layer
     "c3_bf16x3": lambda: small("c3", 4, 64, 2, 2, precision="bf16x3"),
     "c3_bf16": lambda: small("c3", 4, 64, 2, 2, precision="bf16"),
+    # advantage normalisation over the whole [T, N] batch
+    "c1_norm": lambda: normalized(configs.c1()),
+    "c2_bf16x3_norm": lambda: normalized(small("c2", 8, 256, 2, 4, precision="bf16x3")),
 }
 
 

@@ -1,6 +1,7 @@
 """Multi-GPU learner (NCCL all-reduce per minibatch) on 2 GPUs, one process per GPU: the
 ranks end bitwise identical and equal to the single-process oracle update of the global
 batch (global permutation, boonta/algorithms/ppo.py:200). Skipped with fewer than 2 GPUs."""
+import dataclasses
 import os
 
 import numpy as np
@@ -17,6 +18,11 @@ WORLD = 2
 def _workload(kind):
     if kind == "c4":
         return configs.c4().scaled(num_steps=8, num_envs=32, num_minibatches=4, update_epochs=2)
+    if kind == "fp32_norm":
+        # advantage normalisation over the global batch: the moments are summed across ranks
+        # (boonta/algorithms/ppo.py:220-221 over the sharded [T, N_global] advantages)
+        w = _workload("fp32")
+        return dataclasses.replace(w, ppo=dataclasses.replace(w.ppo, normalize_advantage=True))
     return configs.c2(precision=kind).scaled(num_steps=8, num_envs=64, num_minibatches=4,
                                              update_epochs=2)
 
@@ -61,7 +67,7 @@ def _global(w):
     return out
 
 
-@pytest.mark.parametrize("kind", ["fp32", "bf16x3", "c4"])
+@pytest.mark.parametrize("kind", ["fp32", "bf16x3", "c4", "fp32_norm"])
 def test_two_gpu_update_matches_the_global_oracle(kind):
     import multiprocessing as mp
     import socket
