@@ -767,10 +767,27 @@ int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
   return launch_heads_jp<64, false>(p, blocks, smem, stream);
 }
 
+bool heads_split_products(int F_pi, int F_v, int A, bool shared) {
+  return heads_use_mma(F_pi, F_v, A, shared, heads_fuse_dw(F_pi, F_v, A, shared));
+}
+
+// x * w as the split-bf16 product of the wide heads: lo(x) hi(w) + hi(x) lo(w) + hi(x) hi(w),
+// each term exact in fp32, added to acc in that order.
+__device__ __forceinline__ float split_fma(float x, float w, float acc) {
+  const float xh = __bfloat162float(__float2bfloat16_rn(x));
+  const float wh = __bfloat162float(__float2bfloat16_rn(w));
+  const float xl = __bfloat162float(__float2bfloat16_rn(x - xh));
+  const float wl = __bfloat162float(__float2bfloat16_rn(w - wh));
+  acc = fmaf(xl, wh, acc);
+  acc = fmaf(xh, wl, acc);
+  return fmaf(xh, wh, acc);
+}
+
 // Head outputs only (bootstrap values, act): one warp per row; the head input is act(f).
 __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v, int Fv,
                                      const float* w_pi, const float* w_v, int A, int rows,
-                                     int act_pi, int act_v, float* out, float* value) {
+                                     int act_pi, int act_v, float* out, float* value,
+                                     bool split_pi, bool split_v) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -778,8 +795,10 @@ __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v,
   if (out) {
     for (int j = 0; j < A; ++j) {
       float acc = 0.f;
-      for (int k = lane; k < F; k += 32)
-        acc = fmaf(act_forward(f[k], act_pi), w_pi[(size_t)k * A + j], acc);
+      for (int k = lane; k < F; k += 32) {
+        const float x = act_forward(f[k], act_pi), w = w_pi[(size_t)k * A + j];
+        acc = split_pi ? split_fma(x, w, acc) : fmaf(x, w, acc);
+      }
       acc = warp_sum(acc);
       if (lane == 0) out[(size_t)warp * A + j] = acc + w_pi[(size_t)F * A + j];
     }
@@ -787,7 +806,10 @@ __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v,
   if (value) {
     const float* fv = f_v + (size_t)warp * Fv;
     float acc = 0.f;
-    for (int k = lane; k < Fv; k += 32) acc = fmaf(act_forward(fv[k], act_v), w_v[k], acc);
+    for (int k = lane; k < Fv; k += 32) {
+      const float x = act_forward(fv[k], act_v), w = w_v[k];
+      acc = split_v ? split_fma(x, w, acc) : fmaf(x, w, acc);
+    }
     acc = warp_sum(acc);
     if (lane == 0) value[warp] = acc + w_v[Fv];
   }
@@ -795,10 +817,10 @@ __global__ void heads_forward_kernel(const float* f_pi, int F, const float* f_v,
 
 int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
                          const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
-                         float* value, cudaStream_t stream) {
+                         float* value, bool split_pi, bool split_v, cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
   heads_forward_kernel<<<ceil_div(rows * 32, 256), 256, 0, stream>>>(
-      f_pi, F, f_v, Fv, w_pi, w_v, A, rows, act_pi, act_v, out, value);
+      f_pi, F, f_v, Fv, w_pi, w_v, A, rows, act_pi, act_v, out, value, split_pi, split_v);
   BT_LAUNCH_CHECK("heads_forward_kernel");
   return BT_OK;
 }

@@ -56,9 +56,15 @@ int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream);
 size_t heads_smem_bytes(int F_pi, int F_v, int A, bool shared);
 // Whether the heads kernel can accumulate the head weight gradients itself (small heads).
 bool heads_fuse_dw(int F_pi, int F_v, int A, bool shared);
+// Whether the heads kernel computes the actor outputs (and, for a shared torso, the value)
+// with split-bf16 products (wide heads on warp-level tensor cores).
+bool heads_split_products(int F_pi, int F_v, int A, bool shared);
+// Head outputs only (act, bootstrap values). split_pi / split_v: evaluate the actor outputs /
+// the value with the split-bf16 products of the heads kernel (hi*hi + hi*lo + lo*hi per term,
+// fp32 accumulation), so that act and update agree to fp32 rounding.
 int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
                          const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
-                         float* value, cudaStream_t stream);
+                         float* value, bool split_pi, bool split_v, cudaStream_t stream);
 
 // Conv 3x3 SAME stride 1 on NHWC rows (conv.cu): forward z = conv + bias, h = act(z)
 // ([rows, H*W*Cout]); weight gradient as per-block partials [blocks][(9C + 1) * Cout].

@@ -298,6 +298,9 @@ int allocate(bt_learner* L) {
     L->heads_blocks = ceil_div(tiles, rounds);
   }
   L->heads_fused_dw = heads_fuse_dw(L->F_pi, L->F_v, A, L->shared);
+  // act and the bootstrap evaluate the heads with the update's product arithmetic
+  L->split_pi = heads_split_products(L->F_pi, L->F_v, A, L->shared);
+  L->split_v = L->split_pi && L->shared;
   if (L->heads_fused_dw) {
     // the heads kernel accumulates the head weight gradients, one partial per block
     L->head_pi_splits = L->head_v_splits = L->heads_blocks;
@@ -717,7 +720,8 @@ int bootstrap_and_gae(bt_learner* L, const bt_batch* b, cudaStream_t s) {
   BT_TRY(forward_tower(L, tv, b->bootstrap_obs, nullptr, L->N, nullptr, s));
   BT_K(L, kProfHeadsFwd, s, launch_heads_forward(tv.layers.back().pre(), L->F_v, tv.layers.back().pre(), L->F_v,
                               L->params + L->head_pi_off, L->params + L->head_v_off, L->A, L->N,
-                              tv.layers.back().act, tv.layers.back().act, nullptr, L->boot, s));
+                              tv.layers.back().act, tv.layers.back().act, nullptr, L->boot,
+                              L->split_pi, L->split_v, s));
   BT_K(L, kProfGae, s, launch_gae_internal(b->reward, b->terminated, b->truncated, b->value, L->boot, L->T,
                              L->N, L->cfg.ppo.gamma, L->cfg.ppo.gae_lambda, L->adv, L->ret,
                              L->err_d, s));
@@ -1145,7 +1149,7 @@ extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, cons
   BT_K(L, kProfHeadsFwd, s, launch_heads_forward(t0.layers.back().pre(), L->F_pi, tv.layers.back().pre(), L->F_v,
                               L->params + L->head_pi_off, L->params + L->head_v_off, L->A, num,
                               t0.layers.back().act, tv.layers.back().act, L->act_out,
-                              value ? value : L->act_val, s));
+                              value ? value : L->act_val, L->split_pi, L->split_v, s));
   BT_K(L, kProfMisc, s, launch_sample(L->act_out,
                        L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr,
                        L->cfg.network.head, L->A, num, noise, temperature, action, log_prob, s));

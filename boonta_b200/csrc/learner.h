@@ -159,6 +159,7 @@ struct bt_learner {
   double* stat_part = nullptr;
   int heads_blocks = 0;
   bool heads_fused_dw = false;  // the heads kernel writes the head weight-gradient partials
+  bool split_pi = false, split_v = false;  // heads evaluated with split-bf16 products
   // targets
   float* adv = nullptr;
   float* ret = nullptr;

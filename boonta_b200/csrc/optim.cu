@@ -6,6 +6,8 @@
 // The global norm is summed in two fixed-order stages: per-chunk sums of squares (8192
 // elements per block) into scratch, then every Adam block adds the chunk sums in index
 // order, so the result is deterministic.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "kernels.cuh"
@@ -82,23 +84,43 @@ constexpr int kNoAllocChunks = 16384;
 constexpr int kNoAllocMaxDevices = 64;
 __device__ __align__(256) double g_noalloc_scratch[kNoAllocChunks];
 
-// Device address of g_noalloc_scratch per device, looked up once with that device current
-// (host code cannot use the symbol itself as a device pointer). The lookup happens in the
-// first call on each device, which should therefore come before any stream capture there.
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+// Device address of g_noalloc_scratch per device, looked up with that device current (host
+// code cannot use the symbol itself as a device pointer) and kept together with the id of the
+// CUDA context it was looked up in. The lookup happens in the first call on each device, which
+// should therefore come before any stream capture there. If the caller tears the context down
+// (cudaDeviceReset) and the library's device code is loaded into a new one, the array can sit
+// at a new address: a call made in another context than the cached one looks it up again.
+struct NoAllocSlot {
+  unsigned long long ctx_id = 0;  // cuCtxGetId: unique for the process's lifetime
+  void* ptr = nullptr;
+};
+NoAllocSlot g_noalloc_slot[kNoAllocMaxDevices];
 std::mutex g_noalloc_mutex;
+
+// Id of the calling thread's current context, 0 when none is current yet (the runtime makes
+// one current on its first call on the thread, e.g. the symbol lookup below).
+unsigned long long current_context_id() {
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  if (cuCtxGetId(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 int noalloc_scratch(double** out) {
   int dev = 0;
   BT_CUDA(cudaGetDevice(&dev));
   BT_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "device %d out of range", dev);
+  const unsigned long long id = current_context_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  if (id == 0 || !slot.ptr || slot.ctx_id != id) {
     void* p = nullptr;
     BT_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_ptr[dev] = p;
+    slot.ptr = p;
+    slot.ctx_id = current_context_id();
   }
-  *out = static_cast<double*>(g_noalloc_ptr[dev]);
+  *out = static_cast<double*>(slot.ptr);
   return BT_OK;
 }
 

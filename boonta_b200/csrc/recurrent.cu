@@ -432,7 +432,8 @@ int recurrent_update(bt_learner* L, const bt_batch* b, const int32_t* perm, floa
   BT_K(L, kProfHeadsFwd, s, launch_heads_forward(g.h, L->F_v, g.h, L->F_v,
                                                  L->params + L->head_pi_off,
                                                  L->params + L->head_v_off, L->A, 2 * N,
-                                                 BT_ACT_NONE, BT_ACT_NONE, nullptr, L->act_val, s));
+                                                 BT_ACT_NONE, BT_ACT_NONE, nullptr, L->act_val,
+                                                 L->split_pi, L->split_v, s));
   BT_CUDA(cudaMemcpy2DAsync(L->boot, 4, L->act_val + 1, 8, 4, N, cudaMemcpyDeviceToDevice, s));
   BT_K(L, kProfGae, s, launch_gae_internal(b->reward, b->terminated, b->truncated, b->value,
                                            L->boot, T, N, L->cfg.ppo.gamma, L->cfg.ppo.gae_lambda,
@@ -513,7 +514,8 @@ int recurrent_act(bt_learner* L, const float* obs, const uint8_t* reset, const f
                                                  L->params + L->head_pi_off,
                                                  L->params + L->head_v_off, L->A, num,
                                                  BT_ACT_NONE, BT_ACT_NONE, L->act_out,
-                                                 value ? value : L->act_val, s));
+                                                 value ? value : L->act_val, L->split_pi,
+                                                 L->split_v, s));
   BT_K(L, kProfMisc, s, launch_sample(L->act_out,
                                       L->head_scale_off >= 0 ? L->params + L->head_scale_off
                                                              : nullptr,

@@ -31,7 +31,7 @@
  *
  * The XLA FFI handlers a JAX host would register (jax.ffi.register_ffi_target, the
  * mechanism of boonta/environments/__init__.py:10-15,38-43) wrap these functions one to
- * one; INTEGRATION.md shows that binding.
+ * one (boonta_b200/csrc/xla_ffi.cc, built when jaxlib's headers are available).
  */
 #ifndef BOONTA_B200_H_
 #define BOONTA_B200_H_
@@ -277,9 +277,11 @@ BT_API int bt_clip_adam(float* params, float* mu, float* nu, const float* grads,
  * FFI custom call, which runs after XLA has reserved most of the GPU for its own pool.
  * Scratch is a fixed 128 KB array compiled into the library (resident on every GPU that
  * loads it until exit), so n is limited to 134,217,728 elements; larger n is rejected with
- * BT_ERR_INVALID. The first call on a device looks the array's address up once (a CUDA
- * runtime query), so make that first call before any stream capture on the device. All calls
- * share the array: calls whose GPU work overlaps race and must be ordered by the caller. */
+ * BT_ERR_INVALID. The first call on a device looks the array's address up (a CUDA runtime
+ * query), so make that first call before any stream capture on the device; the address is
+ * kept per device and CUDA context, and looked up again in a new context (after a
+ * cudaDeviceReset). All calls share the array: calls whose GPU work overlaps race and must be
+ * ordered by the caller. */
 BT_API int bt_clip_adam_noalloc(float* params, float* mu, float* nu, const float* grads,
                                 int64_t n, int32_t count, const bt_optimizer* opt, void* stream);
 

@@ -37,8 +37,11 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
 
 
 def quantize(x, precision):
+    """bf16 operands: x rounded to float32 and then to bfloat16, returned in x's own dtype (so
+    that a float64 evaluation multiplies the bf16 values exactly)."""
     if precision == "bf16":
-        return bf16_round(np.asarray(x, np.float32))
+        x = np.asarray(x)
+        return bf16_round(x.astype(np.float32)).astype(x.dtype, copy=False)
     return x
 
 
