@@ -1,0 +1,59 @@
+"""Shared parity arithmetic of the GPU tests (imported by the test modules; not a test).
+
+Errors are relative L2 norms per parameter tensor. The yardstick is the oracle evaluated in
+float64 (the same operations and operand roundings, exact products, accurate sums); a float32
+evaluation of the oracle is carried along to measure how far plain float32 arithmetic of the
+same algorithm already is from it.
+
+fp32-class arithmetic (fp32 CUDA cores, split-bf16 tensor-core products) is held to the
+gradients 1e-4, parameters after an update 1e-3. bf16 GEMM operands are
+held to BF16_NOISE times the float32 oracle's own distance from the float64 oracle (floors
+1e-4 and 1e-3): a layer output within float32 rounding of a bf16 rounding boundary rounds to
+either neighbour depending on the summation order, and Adam's first steps (lr * sign(g) for a
+fresh moment) turn a gradient element that such flips move across zero into a full step the
+other way; any float32-accumulating implementation of the arithmetic shows that noise.
+"""
+import numpy as np
+
+GRAD_RTOL = 1e-4
+PARAM_RTOL = 1e-3
+BF16_NOISE = 3.0
+
+
+def rel(a, b, floor=0.0):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), floor, 1e-30))
+
+
+def check_grads(tag, precision, got, truth, plain):
+    """got / truth / plain: {name: gradient} of the CUDA path, the float64 oracle and the
+    float32 oracle. Returns the tensors over their bound (empty when all pass)."""
+    bad = []
+    for k in truth:
+        e, e32 = rel(got[k], truth[k]), rel(plain[k], truth[k])
+        bound = GRAD_RTOL if precision != "bf16" else max(BF16_NOISE * e32, GRAD_RTOL)
+        print(f"{tag} gradient {k}: native {e:.3e}, fp32 oracle {e32:.3e}, bound {bound:.1e}")
+        if e > bound:
+            bad.append((k, e, bound))
+    return bad
+
+
+def check_params(tag, precision, before, got, truth, plain, steps, lr):
+    """Parameters after an update: got / truth / plain as in check_grads, `before` the
+    parameters the update started from. A tensor that starts at zero (biases) is measured
+    against the largest move Adam can make in `steps` steps (steps * lr per element). Each
+    bound is asserted to lie below the error of an update that changed nothing."""
+    bad = []
+    for k in truth:
+        floor = steps * lr * np.sqrt(truth[k].size) if not np.any(before[k]) else 0.0
+        e = rel(got[k], truth[k], floor)
+        e32 = rel(plain[k], truth[k], floor)
+        noop = rel(before[k], truth[k], floor)
+        bound = PARAM_RTOL if precision != "bf16" else max(BF16_NOISE * e32, PARAM_RTOL)
+        print(f"{tag} params {k}: native {e:.3e}, fp32 oracle {e32:.3e}, no-op update "
+              f"{noop:.3e}, bound {bound:.1e}")
+        assert bound < noop, (k, "the bound would pass an update that changed nothing")
+        if e > bound:
+            bad.append((k, e, bound))
+    return bad
