@@ -38,7 +38,7 @@ EXPORTS = (
     "bt_learner_comm_init", "bt_learner_profile", "bt_learner_profile_read",
     "bt_learner_launch_count", "bt_gemm_bf16", "bt_gemm_bf16x3", "bt_clip_adam",
     "bt_clip_adam_noalloc", "bt_learner_use_graphs", "bt_learner_check",
-    "bt_selftest_bounded_wait",
+    "bt_selftest_bounded_wait", "bt_learner_load_state", "bt_learner_store_state",
 )
 
 
@@ -120,6 +120,8 @@ def lib() -> C.CDLL:
                                             C.POINTER(i32), C.POINTER(i64)]),
         "bt_learner_set_state": (C.c_int, [vp, vp, vp, vp, i32, vp]),
         "bt_learner_get_state": (C.c_int, [vp, vp, vp, vp, C.POINTER(i32), vp]),
+        "bt_learner_load_state": (C.c_int, [vp, vp, vp, vp, vp, vp]),
+        "bt_learner_store_state": (C.c_int, [vp, vp, vp, vp, vp, vp]),
         "bt_learner_update": (C.c_int, [vp, C.POINTER(Batch), vp, vp, vp]),
         "bt_learner_use_graphs": (C.c_int, [vp, i32]),
         "bt_learner_check": (C.c_int, [vp, vp]),

@@ -87,7 +87,7 @@ def build(clean: bool = False, verbose: bool = False, extra: list[str] | None = 
                 print(log, file=sys.stderr)
     objs = [BUILD / (s.stem + ".o") for s in sources]
     if jobs or not LIB.exists():
-        cmd = [nvcc(), "-shared", *ARCH, "-o", str(LIB), *map(str, objs), "-ldl", "-lcuda"]
+        cmd = [nvcc(), "-shared", *ARCH, "-o", str(LIB), *map(str, objs), "-ldl"]
         proc = subprocess.run(cmd, capture_output=True, text=True)
         if proc.returncode != 0:
             raise RuntimeError(f"link failed:\n{proc.stdout}\n{proc.stderr}")

@@ -184,4 +184,12 @@ __device__ __forceinline__ int live_rows(const int* count, int rows) {
   return c < rows ? c : rows;
 }
 
+// End of the rows a bf16 operand of the tensor-core weight-gradient GEMM must hold: its K loop
+// reads whole 64-row blocks up to the live count, so the rows [live, dz_rows_end) are written
+// as zeros by the kernel that produces the operand (padded multi-rank minibatches).
+__device__ __forceinline__ int dz_rows_end(int live, int rows) {
+  const int e = (live + 63) / 64 * 64;
+  return e < rows ? e : rows;
+}
+
 }  // namespace bt

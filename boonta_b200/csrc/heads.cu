@@ -368,7 +368,9 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
   pdl_trigger();
   pdl_wait();  // parameters, features and targets come from earlier kernels
   const int live = live_rows(p.count, p.rows);
-  const int tiles = ceil_div(live, kTileRows);
+  // Tiles up to the next 64-row boundary: the rows past the live count get zero feature
+  // gradients (the bf16 operands of the tensor-core weight-gradient GEMMs need them).
+  const int tiles = ceil_div(dz_rows_end(live, p.rows), kTileRows);
 
   // head kernels as columns wj[j][k] (j < A actor outputs, j = A the value when the torso
   // is shared, the rest zero), biases, gaussian constants

@@ -180,6 +180,11 @@ __global__ void __launch_bounds__(256) ln_backward_kernel(const float* d_y, cons
       }
     }
   }
+  if (d_zb) {  // rows [live, next 64-row boundary) of the bf16 operand: zeros
+    const int end = dz_rows_end(live, rows);
+    for (int row = live + blockIdx.x * 8 + warp; row < end; row += warps_total)
+      for (int k = lane; k < n; k += 32) store_bf16(d_zb, d_zb_lo, (size_t)row * n + k, 0.f);
+  }
   // Block reduction of the column partial sums, 64 columns at a time.
   for (int c0 = 0; c0 < n; c0 += 64) {
     __syncthreads();
@@ -264,6 +269,14 @@ __global__ void __launch_bounds__(256) ln_backward_vec_kernel(
       if (d_z) *reinterpret_cast<float4*>(d_z + e) = g;
       if (d_zb) store_bf16x4(d_zb, d_zb_lo, e, g);
     }
+  }
+  if (d_zb) {  // rows [live, next 64-row boundary) of the bf16 operand: zeros
+    const int end = dz_rows_end(live, rows);
+    for (int row = live + blockIdx.x * 8 + warp; row < end; row += warps_total)
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        store_bf16x4(d_zb, d_zb_lo, (size_t)row * n + 4 * (lane + 32 * i),
+                     make_float4(0.f, 0.f, 0.f, 0.f));
   }
   // Block reduction of the column partial sums in warp order, 128 columns at a time: thread
   // t < 64 sums the d-scale float4 of lanes t (columns 4 (t + 32 i) ...), t >= 64 the d-bias.

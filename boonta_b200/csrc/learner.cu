@@ -683,14 +683,10 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
                                               rows, in.count, L->head_v_splits,
                                               L->head_v_part, sh));
   }
-  if (in.count) {
-    // padded minibatch (multi-GPU): the tensor-core dW GEMMs read whole 64-row blocks, so the
-    // dz rows past the live count must be zero
-    for (int t = 0; t < L->ntowers; ++t)
-      for (LayerPlan& lp : L->towers[t].layers)
-        if (lp.tc)
-          BT_K(L, kProfMisc, s, launch_zero_tail_rows(lp.dzb, lp.dzb_lo, rows, lp.kout, in.count, s));
-  }
+  // Padded minibatches (multi-GPU, bt_learner_loss_grads): the tensor-core dW GEMMs read whole
+  // 64-row blocks up to the live count, and the kernels writing their bf16 dz operands (the
+  // heads, the dX epilogues, LayerNorm backward) write the rows past the count up to the next
+  // 64-row boundary as zeros.
   if (L->ntowers > 1) {
     BT_TRY(stream_dep(L, s, sc));
     BT_TRY(backward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, sc, -1,
@@ -877,6 +873,32 @@ extern "C" int bt_learner_get_state(bt_learner* L, float* params, float* mu, flo
     BT_CUDA(cudaMemcpyAsync(count, L->count_d, 4, cudaMemcpyDefault, s));
     BT_CUDA(cudaStreamSynchronize(s));
   }
+  return BT_OK;
+}
+
+extern "C" int bt_learner_load_state(bt_learner* L, const float* params, const float* mu,
+                                     const float* nu, const int32_t* count, void* stream) {
+  BT_CHECK_ARG(L && params && mu && nu && count, "bt_learner_load_state: null argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t bytes = (size_t)L->num_params * 4;
+  if (params != L->params) BT_CUDA(cudaMemcpyAsync(L->params, params, bytes, cudaMemcpyDeviceToDevice, s));
+  if (L->params_b)
+    BT_K(L, kProfMisc, s, launch_to_bf16(L->params, L->params_b, L->params_b_lo, L->num_params, s));
+  if (mu != L->mu) BT_CUDA(cudaMemcpyAsync(L->mu, mu, bytes, cudaMemcpyDeviceToDevice, s));
+  if (nu != L->nu) BT_CUDA(cudaMemcpyAsync(L->nu, nu, bytes, cudaMemcpyDeviceToDevice, s));
+  BT_CUDA(cudaMemcpyAsync(L->count_d, count, 4, cudaMemcpyDeviceToDevice, s));
+  return BT_OK;
+}
+
+extern "C" int bt_learner_store_state(bt_learner* L, float* params, float* mu, float* nu,
+                                      int32_t* count, void* stream) {
+  BT_CHECK_ARG(L, "null learner");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t bytes = (size_t)L->num_params * 4;
+  if (params) BT_CUDA(cudaMemcpyAsync(params, L->params, bytes, cudaMemcpyDeviceToDevice, s));
+  if (mu) BT_CUDA(cudaMemcpyAsync(mu, L->mu, bytes, cudaMemcpyDeviceToDevice, s));
+  if (nu) BT_CUDA(cudaMemcpyAsync(nu, L->nu, bytes, cudaMemcpyDeviceToDevice, s));
+  if (count) BT_CUDA(cudaMemcpyAsync(count, L->count_d, 4, cudaMemcpyDeviceToDevice, s));
   return BT_OK;
 }
 

@@ -99,11 +99,28 @@ std::mutex g_noalloc_mutex;
 
 // Id of the calling thread's current context, 0 when none is current yet (the runtime makes
 // one current on its first call on the thread, e.g. the symbol lookup below).
+// The driver entry points come through the runtime (cudaGetDriverEntryPoint), so the library
+// does not link libcuda itself.
 unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  if (!get_current || !get_id) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1) != cudaSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2) != cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || !f1 || !f2)
+      return 0;
+    get_current = reinterpret_cast<GetCurrent>(f1);
+    get_id = reinterpret_cast<GetId>(f2);
+  }
   CUcontext ctx = nullptr;
   unsigned long long id = 0;
-  if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || !ctx) return 0;
-  if (cuCtxGetId(ctx, &id) != CUDA_SUCCESS) return 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
   return id;
 }
 

@@ -171,6 +171,16 @@ BT_API int bt_learner_set_state(bt_learner* learner, const float* params, const 
 BT_API int bt_learner_get_state(bt_learner* learner, float* params, float* mu, float* nu,
                          int32_t* count, void* stream);
 
+/* The same state moves without any host synchronisation (only stream-ordered device-to-device
+ * copies, the XLA FFI stream contract): all pointers are device pointers, count an int32 in
+ * device memory. load_state needs every argument; store_state skips the NULL ones. These carry
+ * the functional PPOState of a jitted PPO.update (ppo.py:30-34, 76-233) in and out of the
+ * handle around each update. */
+BT_API int bt_learner_load_state(bt_learner* learner, const float* params, const float* mu,
+                                 const float* nu, const int32_t* count, void* stream);
+BT_API int bt_learner_store_state(bt_learner* learner, float* params, float* mu, float* nu,
+                                  int32_t* count, void* stream);
+
 /* One full learner step. permutations: device int32 [E, T*N*world_size] (or
  * [E, N*world_size] env permutations for recurrent networks); stats: device float
  * [E, M, BT_NUM_STATS] or NULL. */

@@ -26,8 +26,8 @@ Tolerances. fp32 and split-bf16 (bf16x3) arithmetic are held to the north-star b
 the float64 oracle: gradients 1e-4 relative per tensor (L2 norm) and parameters after the update
 1e-3 relative per tensor. For a tensor that starts at zero (biases) the relative error of its
 parameters is taken against the largest move Adam can make in the update (steps * lr per
-element), which keeps the bound meaningful. Every parameter bound is checked to lie below the
-error of an update that changed nothing, so a no-op update fails.
+element), which keeps the bound meaningful. The change each tensor made is checked as well
+(an update that changed nothing fails it).
 
 bf16 GEMM operands (C5) are compared with the oracle's bf16-operand arithmetic in float64. A
 layer output that sits within float32 rounding of a bf16 rounding boundary rounds to one
@@ -239,5 +239,7 @@ def test_full_size_update_one_epoch(name):
         np.testing.assert_allclose(stats[..., other], ostats[..., other], rtol=1e-2, atol=2e-3)
         np.testing.assert_allclose(stats[..., clip], ostats[..., clip], rtol=0, atol=1e-2)
     else:
+        # a sample whose probability ratio lies within the arithmetic's rounding of
+        # 1 +- clip_coefficient counts on either side: up to ~16 of a minibatch's 16,384 rows
         np.testing.assert_allclose(stats[..., other], ostats[..., other], rtol=2e-3, atol=2e-4)
-        np.testing.assert_allclose(stats[..., clip], ostats[..., clip], rtol=0, atol=2e-4)
+        np.testing.assert_allclose(stats[..., clip], ostats[..., clip], rtol=0, atol=1e-3)
