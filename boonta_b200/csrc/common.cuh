@@ -99,6 +99,16 @@ __device__ __forceinline__ float act_dz(float z) {
   return 1.f;
 }
 
+// The derivative from the activation's output h = act(z), for the activations where h
+// determines it (tanh: 1 - h^2, relu: h > 0, none: 1), bit-identical to act_dz<A>(z).
+template <int A>
+__device__ __forceinline__ float act_dz_from_out(float h) {
+  static_assert(A != BT_ACT_SILU, "silu's derivative needs the pre-activation");
+  if constexpr (A == BT_ACT_TANH) return 1.f - h * h;
+  if constexpr (A == BT_ACT_RELU) return h > 0.f ? 1.f : 0.f;
+  return 1.f;
+}
+
 template <int A>
 struct ActTag {
   static constexpr int value = A;

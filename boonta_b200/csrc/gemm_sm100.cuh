@@ -36,6 +36,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle span of bf16
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each on half the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
+// K blocks (64 each) accumulated in tensor memory before the epilogue warps add the partial
+// sum into fp32 registers (two-level accumulation of the split-K kernel).
+constexpr int kChunk = 16;
 constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13,
               kErrTimeoutEpiIn = 14;
 // Store epilogues (kTma): each epilogue warp owns 4 KB of shared memory that holds, one
@@ -192,7 +195,7 @@ struct Operands {
 };
 
 template <int BN, bool A_MN, bool B_MN, bool X3, class Epi>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ Operands ops, GemmShape sh,
                      const __grid_constant__ Epi epi) {
   using C = Cfg<BN, X3, Epi::kDeep>;
@@ -202,8 +205,9 @@ __global__ void __launch_bounds__(kThreads)
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
   uint64_t* empty = full + C::kStages;
-  uint64_t* acc_full = empty + C::kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -218,6 +222,13 @@ __global__ void __launch_bounds__(kThreads)
   const int kb0 = blockIdx.z * sh.kblocks_per_split;
   const int kb1 = min(ceil_div(K, BK), kb0 + sh.kblocks_per_split);
   const int nk = max(0, kb1 - kb0);
+  // Two-level accumulation: the tensor cores' fp32 accumulation loses low bits as a chain of
+  // products grows (measured on B200: the relative error of a 16,384-long chain of positive
+  // products is ~7e-5, growing with the chain), so every kChunk K blocks the TMEM accumulator
+  // is read into fp32 registers by the epilogue warps and added there with round-to-nearest,
+  // while the MMAs start the next chunk in the other of two TMEM buffers.
+  const int nchunks = max(1, ceil_div(nk, kChunk));
+  const uint32_t tcols = nchunks > 1 ? 2 * BN : BN;
 
   if (threadIdx.x == 0) {
     s_fail = 0;
@@ -225,10 +236,13 @@ __global__ void __launch_bounds__(kThreads)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, BN);
+  if (warp == 1) tmem_alloc(tmem_slot, tcols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -286,6 +300,16 @@ __global__ void __launch_bounds__(kThreads)
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc<BN, A_MN, B_MN>();
       for (int i = 0; i < nk; ++i) {
+        const int c = i / kChunk, b = c & 1;
+        const bool fresh = i % kChunk == 0;  // first K block of a chunk: overwrite the buffer
+        if (fresh && c >= 2) {
+          // the epilogue warps have read this buffer's previous chunk
+          if (!mbar_wait_bounded(&acc_empty[b], ((c >> 1) - 1) & 1)) {
+            atomicExch(&s_fail, kErrTimeoutAcc);
+            break;
+          }
+          fence_after_sync();
+        }
         const int s = i % C::kStages;
         if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) {
           atomicExch(&s_fail, kErrTimeoutFull);
@@ -296,21 +320,24 @@ __global__ void __launch_bounds__(kThreads)
         const uint32_t sb = sa + C::kABytes;
         const uint32_t sa_lo = sb + C::kBBytes;
         const uint32_t sb_lo = sa_lo + C::kABytes;
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t ah = operand_desc<A_MN>(sa, k), bh = operand_desc<B_MN>(sb, k);
+          const uint32_t keep = (!fresh || k > 0) ? 1u : 0u;
           if (X3) {
             // small cross terms first, then the leading product
-            mma_bf16(tmem, operand_desc<A_MN>(sa_lo, k), bh, idesc, (i > 0 || k > 0) ? 1u : 0u);
-            mma_bf16(tmem, ah, operand_desc<B_MN>(sb_lo, k), idesc, 1u);
-            mma_bf16(tmem, ah, bh, idesc, 1u);
+            mma_bf16(acc, operand_desc<A_MN>(sa_lo, k), bh, idesc, keep);
+            mma_bf16(acc, ah, operand_desc<B_MN>(sb_lo, k), idesc, 1u);
+            mma_bf16(acc, ah, bh, idesc, 1u);
           } else {
-            mma_bf16(tmem, ah, bh, idesc, (i > 0 || k > 0) ? 1u : 0u);
+            mma_bf16(acc, ah, bh, idesc, keep);
           }
         }
         mma_commit(&empty[s]);
+        if (i % kChunk == kChunk - 1 || i == nk - 1) mma_commit(&acc_full[b]);
       }
-      mma_commit(acc_full);
+      if (nk == 0) mma_commit(&acc_full[0]);  // nothing to accumulate: release the epilogue
     }
   } else {
     // Epilogue warps 2..9: TMEM lane quarter = warp % 4 (the hardware's access rule), column
@@ -320,22 +347,45 @@ __global__ void __launch_bounds__(kThreads)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     float* scr = reinterpret_cast<float*>(smem) + (warp - 2) * (32 * 33);
-    const bool ok = mbar_wait_bounded(acc_full, 0);
-    if (!ok && lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
-    fence_after_sync();
     const int row = m0 + q * 32 + lane;
-    const bool have = ok && nk > 0;
     constexpr int kHalf = BN / 2 >= 32 ? BN / 2 : 32;
-#pragma unroll 1
-    for (int c = half * kHalf; c < (half + 1) * kHalf && c < BN; c += 32) {
-      if (n0 + c >= sh.N) break;
-      float v[32];
-      if (have) {
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-      } else {
+    constexpr int kGroups = kHalf / 32;
+    // this thread's row of its column half, summed over the chunks in fp32
+    float run[kGroups][32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) run[g][j] = 0.f;
+    bool ok = true;
+    for (int c = 0; c < nchunks && ok; ++c) {
+      const int b = c & 1;
+      ok = mbar_wait_bounded(&acc_full[b], (c >> 1) & 1);
+      if (!ok) {
+        if (lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
+        break;
       }
+      fence_after_sync();
+      if (nk > 0) {
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g) {
+          const int col = half * kHalf + 32 * g;
+          if (col >= BN || n0 + col >= sh.N) continue;
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col), v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) run[g][j] += v[j];
+        }
+      }
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+    // (run stays zero without K blocks; after a failed wait the results are invalid anyway)
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) {
+      const int c = half * kHalf + 32 * g;
+      if (c >= BN || n0 + c >= sh.N) break;
+      float(&v)[32] = run[g];
       if constexpr (Epi::kStaged) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) scr[lane * 33 + j] = v[j];
@@ -356,7 +406,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (warp == 1) {
     fence_after_sync();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, tcols);
   }
   if (threadIdx.x == 0 && s_fail && sh.err) atomicExch(sh.err, s_fail);
 }

@@ -49,7 +49,7 @@ struct HeadsLayout {
 // 4, 8, 12 or 16 with the fused head weight gradient, 16, 32, 48 or 64 without.
 __host__ __device__ inline int heads_inst_jp(int A, bool fuse) {
   const int n = A + 1;
-  if (fuse) return n <= 4 ? 4 : n <= 8 ? 8 : n <= 12 ? 12 : 16;
+  if (fuse && n <= 16) return n <= 4 ? 4 : n <= 8 ? 8 : n <= 12 ? 12 : 16;
   return n <= 16 ? 16 : n <= 32 ? 32 : n <= 48 ? 48 : 64;
 }
 
@@ -95,17 +95,21 @@ __host__ __device__ inline HeadsLayout heads_layout(int F, int Fv, int A, bool s
   return L;
 }
 
-bool heads_fuse_dw(int F_pi, int F_v, int A, bool /*shared*/) {
-  return A + 1 <= 16 && F_pi <= kHeadThreads && F_v <= kHeadThreads;
-}
-
 // Whether the instance serving these heads runs its products on tensor cores: wide heads
-// without the fused weight gradient, features in whole 16-column steps, and the layout within
-// the 227 KB of shared memory.
+// (32 or more outputs), features in whole 16-column steps, and the layout within the 227 KB of
+// shared memory.
 static bool heads_use_mma(int F_pi, int F_v, int A, bool shared, bool fuse) {
   const int jp = heads_inst_jp(A, fuse);
-  if (fuse || jp < 32 || F_pi % 16 != 0) return false;
+  if (jp < 32 || F_pi % 16 != 0) return false;
   return heads_layout(F_pi, F_v, A, shared, jp, true).total * sizeof(float) <= 227 * 1024;
+}
+
+// Whether the heads kernel accumulates the head weight gradients itself: small heads with up
+// to one feature per thread, or wide tensor-core heads over a shared torso with up to two
+// features per thread.
+bool heads_fuse_dw(int F_pi, int F_v, int A, bool shared) {
+  if (A + 1 <= 16) return F_pi <= kHeadThreads && F_v <= kHeadThreads;
+  return shared && F_pi <= 2 * kHeadThreads && heads_use_mma(F_pi, F_v, A, shared, true);
 }
 
 static size_t heads_smem_for(int F_pi, int F_v, int A, bool shared, bool fuse) {
@@ -194,17 +198,19 @@ __device__ __forceinline__ void stage_features(const float* pre, int F, int ld, 
 // dL/d pre of the tile: g = (sum_j d[r][j] w[j][k]) * act'(pre), for the actor tower
 // (JP outputs through wj_s) or the critic tower (output jcol through wv_s). Batches of
 // eight chunks as in stage_features (pre-activations loaded first).
+// For tanh / relu the derivative comes from the staged act(pre) in shared memory (f_s, row
+// stride ld); only silu re-reads the pre-activation.
 template <int JP, int Act>
 __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int row0,
                                                    int live, int rows_cap, const float* d_s,
                                                    int ldd, const float* w_s, int nj, int jcol,
-                                                   float* df, __nv_bfloat16* dfb,
-                                                   __nv_bfloat16* dfb_lo) {
+                                                   const float* f_s, int ld, float* df,
+                                                   __nv_bfloat16* dfb, __nv_bfloat16* dfb_lo) {
   const int q4 = F / 4, total = kTileRows * q4;
   ChunkWalk w(q4);
   for (int c0 = threadIdx.x; c0 < total; c0 += kBatch * kHeadThreads) {
     float4 z[kBatch];
-    if constexpr (Act != BT_ACT_NONE) {
+    if constexpr (Act == BT_ACT_SILU) {
       ChunkWalk at = w;
 #pragma unroll
       for (int i = 0; i < kBatch; ++i) {
@@ -238,11 +244,17 @@ __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int 
         const float4 wv = *reinterpret_cast<const float4*>(w_s + 4 * q);
         g = make_float4(dj * wv.x, dj * wv.y, dj * wv.z, dj * wv.w);
       }
-      if constexpr (Act != BT_ACT_NONE) {
+      if constexpr (Act == BT_ACT_SILU) {
         g.x *= act_dz<Act>(z[i].x);
         g.y *= act_dz<Act>(z[i].y);
         g.z *= act_dz<Act>(z[i].z);
         g.w *= act_dz<Act>(z[i].w);
+      } else if constexpr (Act != BT_ACT_NONE) {
+        const float4 h = *reinterpret_cast<const float4*>(f_s + r * ld + 4 * q);
+        g.x *= act_dz_from_out<Act>(h.x);
+        g.y *= act_dz_from_out<Act>(h.y);
+        g.z *= act_dz_from_out<Act>(h.z);
+        g.w *= act_dz_from_out<Act>(h.w);
       }
       const size_t e = (size_t)row * F + 4 * q;
       if (dfb) {
@@ -298,7 +310,8 @@ template <int JP, int Act>
 __device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, int row0,
                                                        int live, int rows_cap, const float* d_s,
                                                        int ldd, const float* wj_s, int ldj,
-                                                       float* df, __nv_bfloat16* dfb,
+                                                       const float* f_s, int ldf, float* df,
+                                                       __nv_bfloat16* dfb,
                                                        __nv_bfloat16* dfb_lo) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3, mt = warp & 1;
@@ -325,11 +338,17 @@ __device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, 
       const int row = row0 + mt * 16 + gid + 8 * h;
       if (row >= rows_cap) continue;
       float2 g = make_float2(acc[2 * h], acc[2 * h + 1]);
-      if constexpr (Act != BT_ACT_NONE) {
+      if constexpr (Act == BT_ACT_SILU) {
         float2 z = make_float2(0.f, 0.f);
         if (row < live) z = __ldg(reinterpret_cast<const float2*>(pre + (size_t)row * F + c));
         g.x *= act_dz<Act>(z.x);
         g.y *= act_dz<Act>(z.y);
+      } else if constexpr (Act != BT_ACT_NONE) {
+        // the derivative from the staged act(pre) (rows past the live count are zero there)
+        const float2 hv =
+            *reinterpret_cast<const float2*>(f_s + (mt * 16 + gid + 8 * h) * ldf + c);
+        g.x *= act_dz_from_out<Act>(hv.x);
+        g.y *= act_dz_from_out<Act>(hv.y);
       }
       const size_t e = (size_t)row * F + c;
       if (dfb) {
@@ -346,9 +365,12 @@ __device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, 
 }
 
 template <int JP, bool FUSE, int ACT, bool MMA>
-__global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams p) {
+__global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
+    heads_loss_kernel(HeadsParams p) {
   constexpr int JJ = (JP + 7) / 8;  // outputs per thread in the loss phase
-  static_assert(!MMA || (!FUSE && JP % 16 == 0), "tensor-core heads: wide, unfused");
+  static_assert(!MMA || JP % 16 == 0, "tensor-core heads: whole 16-output steps");
+  // fused head weight gradient: features k = tid + 256 kf per thread
+  constexpr int KF = (FUSE && MMA) ? 2 : 1;
   extern __shared__ __align__(16) float sm[];
   const int F = p.F_pi, Fv = p.F_v, A = p.A;
   const bool shared = (p.f_v == p.f_pi);
@@ -410,10 +432,12 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
   float dsc[JJ];
 #pragma unroll
   for (int jj = 0; jj < JJ; ++jj) dsc[jj] = 0.f;
-  // fused head dW: thread k of the features
-  float accw[FUSE ? JP : 1];
+  // fused head dW: features tid, tid + 256 (KF of them) of the thread
+  float accw[KF][FUSE ? JP : 1];
 #pragma unroll
-  for (int j = 0; j < (FUSE ? JP : 1); ++j) accw[j] = 0.f;
+  for (int kf = 0; kf < KF; ++kf)
+#pragma unroll
+    for (int j = 0; j < (FUSE ? JP : 1); ++j) accw[kf][j] = 0.f;
   float accv = 0.f, accb = 0.f;
 
   for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -630,26 +654,30 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
     // 4. dL/d pre for the towers
     if constexpr (MMA) {
       heads_feature_grad_mma<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, Lo.ldj,
-                                      p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
+                                      f_s, Lo.ldf, p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
     } else {
-      store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, JP, 0,
-                                  p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
+      store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, JP, 0, f_s,
+                                  Lo.ldf, p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
     }
     if (!shared)
-      store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, Lo.ldd, wv_s, 1, A, p.d_fv,
-                                  p.d_fv_b, p.d_fv_b_lo);
+      store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, Lo.ldd, wv_s, 1, A, fv_s,
+                                  Lo.ldv, p.d_fv, p.d_fv_b, p.d_fv_b_lo);
     // 5. head weight gradients
     if constexpr (FUSE) {
-      if (tid < F) {
-        for (int rr = 0; rr < kTileRows; ++rr) {
-          const float fk = f_s[rr * Lo.ldf + tid];
 #pragma unroll
-          for (int j = 0; j < JP; j += 4) {
-            const float4 dd = *reinterpret_cast<const float4*>(d_s + rr * JP + j);
-            accw[j] = fmaf(fk, dd.x, accw[j]);
-            accw[j + 1] = fmaf(fk, dd.y, accw[j + 1]);
-            accw[j + 2] = fmaf(fk, dd.z, accw[j + 2]);
-            accw[j + 3] = fmaf(fk, dd.w, accw[j + 3]);
+      for (int kf = 0; kf < KF; ++kf) {
+        const int k = tid + kf * kHeadThreads;
+        if (k < F) {
+          for (int rr = 0; rr < kTileRows; ++rr) {
+            const float fk = f_s[rr * Lo.ldf + k];
+#pragma unroll
+            for (int j = 0; j < JP; j += 4) {
+              const float4 dd = *reinterpret_cast<const float4*>(d_s + rr * Lo.ldd + j);
+              accw[kf][j] = fmaf(fk, dd.x, accw[kf][j]);
+              accw[kf][j + 1] = fmaf(fk, dd.y, accw[kf][j + 1]);
+              accw[kf][j + 2] = fmaf(fk, dd.z, accw[kf][j + 2]);
+              accw[kf][j + 3] = fmaf(fk, dd.w, accw[kf][j + 3]);
+            }
           }
         }
       }
@@ -663,22 +691,20 @@ __global__ void __launch_bounds__(kHeadThreads, 2) heads_loss_kernel(HeadsParams
 
   if constexpr (FUSE) {
     float* pp = p.dw_pi_partials + (size_t)blockIdx.x * (F + 1) * A;
-    if (tid < F) {
+    float* pv = p.dw_v_partials + (size_t)blockIdx.x * (Fv + 1);
 #pragma unroll
-      for (int j = 0; j < JP; ++j)
-        if (j < A) pp[(size_t)tid * A + j] = accw[j];
+    for (int kf = 0; kf < KF; ++kf) {
+      const int k = tid + kf * kHeadThreads;
+      if (k < F) {
+#pragma unroll
+        for (int j = 0; j < JP; ++j) {
+          if (j < A) pp[(size_t)k * A + j] = accw[kf][j];
+          if (shared && j == A) pv[k] = accw[kf][j];
+        }
+      }
     }
     if (tid < A) pp[(size_t)F * A + tid] = accb;
-    float* pv = p.dw_v_partials + (size_t)blockIdx.x * (Fv + 1);
-    if (shared) {
-      if (tid < F) {
-#pragma unroll
-        for (int j = 0; j < JP; ++j)
-          if (j == A) pv[tid] = accw[j];
-      }
-    } else if (tid < Fv) {
-      pv[tid] = accv;
-    }
+    if (!shared && tid < Fv) pv[tid] = accv;
     if (tid == A) pv[Fv] = accb;
   }
 
@@ -751,12 +777,15 @@ int launch_heads_loss(const HeadsParams& p, int blocks, cudaStream_t stream) {
   const int jp = heads_inst_jp(p.A, fuse);  // the instance below; its layout uses this JP
   if (fuse) {
     BT_CHECK_ARG(heads_fuse_dw(p.F_pi, p.F_v, p.A, shared) && p.dw_v_partials,
-                 "heads: fused head weight gradient needs A + 1 <= 16 and widths <= %d",
-                 kHeadThreads);
+                 "heads: fused head weight gradient needs A + 1 <= 16 and widths <= %d, or a "
+                 "wide head over a shared torso of width <= %d", kHeadThreads, 2 * kHeadThreads);
     if (jp <= 4) return launch_heads_jp<4, true>(p, blocks, smem, stream);
     if (jp <= 8) return launch_heads_jp<8, true>(p, blocks, smem, stream);
     if (jp <= 12) return launch_heads_jp<12, true>(p, blocks, smem, stream);
-    return launch_heads_jp<16, true>(p, blocks, smem, stream);
+    if (jp <= 16) return launch_heads_jp<16, true>(p, blocks, smem, stream);
+    if (jp <= 32) return launch_heads_jp<32, true, true>(p, blocks, smem, stream);
+    if (jp <= 48) return launch_heads_jp<48, true, true>(p, blocks, smem, stream);
+    return launch_heads_jp<64, true, true>(p, blocks, smem, stream);
   }
   if (jp <= 16) return launch_heads_jp<16, false>(p, blocks, smem, stream);
   if (heads_use_mma(p.F_pi, p.F_v, p.A, shared, false)) {

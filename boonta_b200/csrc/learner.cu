@@ -651,8 +651,9 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   hp.clip_value = c.ppo.clip_value_loss;
   hp.ent_coef = c.ppo.entropy_coefficient;
   hp.vf_coef = c.ppo.value_coefficient;
-  hp.d_out = L->d_out;
-  hp.d_val = L->d_val;
+  // the head outputs' gradients are needed only by the separate head dW kernels
+  hp.d_out = L->heads_fused_dw ? nullptr : L->d_out;
+  hp.d_val = L->heads_fused_dw ? nullptr : L->d_val;
   hp.d_fpi = last_pi.d_pre;
   hp.d_fv = L->shared ? nullptr : last_v.d_pre;
   hp.d_fpi_b = (last_pi.tc && !last_pi.ln) ? last_pi.dzb : nullptr;
