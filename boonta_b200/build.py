@@ -2,7 +2,9 @@
 
 Every `.cu` file under `boonta_b200/csrc/` is compiled with nvcc
 (`-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`) in parallel and linked into one
-shared library with a plain C ABI (`include/boonta_b200.h`). NCCL's header comes from
+shared library with a plain C ABI (`include/boonta_b200.h`). When JAXLIB_INCLUDE names
+jaxlib's FFI headers (`jax.ffi.include_dir()`), `csrc/xla_ffi.cc` (the XLA FFI handlers) is
+compiled into the same library. NCCL's header comes from
 the nvidia-nccl wheel; the library itself is dlopen'ed at run time only when a
 communicator is created. nvcc cross-compiles, so this runs without a GPU.
 
@@ -72,6 +74,11 @@ def build(clean: bool = False, verbose: bool = False, extra: list[str] | None = 
         shutil.rmtree(BUILD)
     BUILD.mkdir(exist_ok=True)
     sources = sorted(CSRC.glob("*.cu"))
+    # the XLA FFI handlers, only against jaxlib's own FFI headers (jax.ffi.include_dir())
+    jaxlib_inc = os.environ.get("JAXLIB_INCLUDE")
+    if jaxlib_inc and (Path(jaxlib_inc) / "xla" / "ffi" / "api" / "ffi.h").exists():
+        sources.append(CSRC / "xla_ffi.cc")
+        extra = [*extra, "-I", jaxlib_inc]
     headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list((ROOT / "include").glob("*.h"))
     newest_header = max((h.stat().st_mtime for h in headers), default=0.0)
     jobs = []

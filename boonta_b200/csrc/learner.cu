@@ -879,15 +879,15 @@ extern "C" int bt_learner_get_state(bt_learner* L, float* params, float* mu, flo
 
 extern "C" int bt_learner_load_state(bt_learner* L, const float* params, const float* mu,
                                      const float* nu, const int32_t* count, void* stream) {
-  BT_CHECK_ARG(L && params && mu && nu && count, "bt_learner_load_state: null argument");
+  BT_CHECK_ARG(L && params, "bt_learner_load_state: null argument");
   cudaStream_t s = (cudaStream_t)stream;
   const size_t bytes = (size_t)L->num_params * 4;
   if (params != L->params) BT_CUDA(cudaMemcpyAsync(L->params, params, bytes, cudaMemcpyDeviceToDevice, s));
   if (L->params_b)
     BT_K(L, kProfMisc, s, launch_to_bf16(L->params, L->params_b, L->params_b_lo, L->num_params, s));
-  if (mu != L->mu) BT_CUDA(cudaMemcpyAsync(L->mu, mu, bytes, cudaMemcpyDeviceToDevice, s));
-  if (nu != L->nu) BT_CUDA(cudaMemcpyAsync(L->nu, nu, bytes, cudaMemcpyDeviceToDevice, s));
-  BT_CUDA(cudaMemcpyAsync(L->count_d, count, 4, cudaMemcpyDeviceToDevice, s));
+  if (mu && mu != L->mu) BT_CUDA(cudaMemcpyAsync(L->mu, mu, bytes, cudaMemcpyDeviceToDevice, s));
+  if (nu && nu != L->nu) BT_CUDA(cudaMemcpyAsync(L->nu, nu, bytes, cudaMemcpyDeviceToDevice, s));
+  if (count) BT_CUDA(cudaMemcpyAsync(L->count_d, count, 4, cudaMemcpyDeviceToDevice, s));
   return BT_OK;
 }
 

@@ -112,6 +112,11 @@ class Learner:
         return cls(w.network, w.ppo, w.optimizer, w.num_steps, w.num_envs,
                    world_size=world_size, rank=rank, **kw)
 
+    @property
+    def handle(self) -> int:
+        """Address of the native bt_learner (the "learner" attribute of the XLA FFI calls)."""
+        return int(self._h.value)
+
     def close(self):
         if getattr(self, "_h", None):
             _lib.lib().bt_learner_destroy(self._h)

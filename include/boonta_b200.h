@@ -173,7 +173,8 @@ BT_API int bt_learner_get_state(bt_learner* learner, float* params, float* mu, f
 
 /* The same state moves without any host synchronisation (only stream-ordered device-to-device
  * copies, the XLA FFI stream contract): all pointers are device pointers, count an int32 in
- * device memory. load_state needs every argument; store_state skips the NULL ones. These carry
+ * device memory. load_state needs params and leaves mu / nu / count as they are where NULL;
+ * store_state skips the NULL ones. These carry
  * the functional PPOState of a jitted PPO.update (ppo.py:30-34, 76-233) in and out of the
  * handle around each update. */
 BT_API int bt_learner_load_state(bt_learner* learner, const float* params, const float* mu,
