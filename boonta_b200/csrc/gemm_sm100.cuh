@@ -36,9 +36,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle span of bf16
 constexpr int kEpiWarps = 8;  // two warps per TMEM lane quarter, each on half the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;
-// K blocks (64 each) accumulated in tensor memory before the epilogue warps add the partial
+// K blocks (64 rows each) accumulated in tensor memory before the epilogue warps add the partial
 // sum into fp32 registers (two-level accumulation of the split-K kernel).
-constexpr int kChunk = 16;
+constexpr int kChunk = 32;
 constexpr int kErrTimeoutFull = 11, kErrTimeoutEmpty = 12, kErrTimeoutAcc = 13,
               kErrTimeoutEpiIn = 14;
 // Store epilogues (kTma): each epilogue warp owns 4 KB of shared memory that holds, one
@@ -224,9 +224,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nk = max(0, kb1 - kb0);
   // Two-level accumulation: the tensor cores' fp32 accumulation loses low bits as a chain of
   // products grows (measured on B200: the relative error of a 16,384-long chain of positive
-  // products is ~7e-5, growing with the chain), so every kChunk K blocks the TMEM accumulator
-  // is read into fp32 registers by the epilogue warps and added there with round-to-nearest,
-  // while the MMAs start the next chunk in the other of two TMEM buffers.
+  // products is ~7e-5, growing with the chain), so every kChunk K blocks (2,048 rows) the TMEM
+  // accumulator is read into fp32 registers by the epilogue warps and added there with
+  // round-to-nearest, while the MMAs start the next chunk in the other of two TMEM buffers.
   const int nchunks = max(1, ceil_div(nk, kChunk));
   const uint32_t tcols = nchunks > 1 ? 2 * BN : BN;
 
