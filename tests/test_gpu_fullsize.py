@@ -41,7 +41,7 @@ floors of 1e-4 (gradients) and 1e-3 (parameters).
 """
 import numpy as np
 import pytest
-from _parity import check_grads, check_params
+from _parity import BF16_NOISE, check_grads, check_params
 from _parity import rel as _rel
 
 from boonta_b200 import configs
@@ -184,7 +184,12 @@ def test_full_size_minibatch_gradient(name):
     _, ost, og = oppo.loss_and_grads(w.network, w.ppo, params, omb, precision=prec,
                                      dtype=np.float64)
     _, _, og32 = oppo.loss_and_grads(w.network, w.ppo, params, omb, precision=prec)
-    bad = check_grads(f"{w.name} rows {rows}", w.precision, g, og, og32)
+    hw = None
+    if w.precision == "bf16":
+        from _cublas_ref import loss_and_grads as cublas_loss_and_grads
+
+        _, hw = cublas_loss_and_grads(w.network, w.ppo, params, omb)
+    bad = check_grads(f"{w.name} rows {rows}", w.precision, g, og, og32, hw)
     assert not bad, bad
     if w.precision == "bf16":
         np.testing.assert_allclose(st, ost, rtol=1e-3, atol=2e-4)
@@ -228,7 +233,7 @@ def test_full_size_update_one_epoch(name):
                            roll, perms, precision=_oracle_precision(w), dtype=dtype)
 
     op, _, ostats, _ = oracle(np.float64)
-    op32, _, _, _ = oracle(np.float32)
+    op32, _, ostats32, _ = oracle(np.float32)
     steps = w.ppo.update_epochs * w.ppo.num_minibatches
     bad = check_params(f"{w.name} T={w.num_steps} N={w.num_envs}", w.precision, params, new, op,
                        op32, steps, w.optimizer.lr)
@@ -236,8 +241,13 @@ def test_full_size_update_one_epoch(name):
     clip = 3  # actor/clip_fraction: a count, compared as a fraction of the rows
     other = [i for i in range(stats.shape[-1]) if i != clip]
     if w.precision == "bf16":
-        np.testing.assert_allclose(stats[..., other], ostats[..., other], rtol=1e-2, atol=2e-3)
-        np.testing.assert_allclose(stats[..., clip], ostats[..., clip], rtol=0, atol=1e-2)
+        # each statistic within the bf16 noise: BF16_NOISE times the float32 oracle's own
+        # distance from the float64 one, plus 2e-3 (the clip fraction: 1 % of the rows)
+        noise = np.abs(ostats32 - ostats)
+        dev = np.abs(stats - ostats)
+        allowed = BF16_NOISE * noise + 2e-3
+        allowed[..., clip] = BF16_NOISE * noise[..., clip] + 1e-2
+        assert np.all(dev <= allowed), (np.argwhere(dev > allowed), dev.max())
     else:
         # a sample whose probability ratio lies within the arithmetic's rounding of
         # 1 +- clip_coefficient counts on either side: up to ~16 of a minibatch's 16,384 rows
