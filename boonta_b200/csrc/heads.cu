@@ -266,10 +266,22 @@ __device__ __forceinline__ void store_feature_grad(const float* pre, int F, int 
   }
 }
 
+// The head kernel of the tensor-core instances is held in shared memory pre-split: one 32-bit
+// word per element, bf16 hi = bf16(w) in the upper half and lo = bf16(w - hi) in the lower
+// (the split of split_pair, done once per block instead of per tile and warp).
+__device__ __forceinline__ uint32_t pack_split(float w) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(w - __bfloat162float(hi));
+  return ((uint32_t)__bfloat16_as_ushort(hi) << 16) | (uint32_t)__bfloat16_as_ushort(lo);
+}
+// The bf16x2 fragment registers (first element in the low half) of two packed words.
+__device__ __forceinline__ uint32_t packed_hi(uint32_t a, uint32_t b) { return __byte_perm(a, b, 0x7632); }
+__device__ __forceinline__ uint32_t packed_lo(uint32_t a, uint32_t b) { return __byte_perm(a, b, 0x5410); }
+
 // Phase 2 on tensor cores (MMA instances): out[32][JP] = f[32][F] W[F][JP] in split bf16.
 // Warp w takes m-tile w % 2 (16 rows) and the n-tiles w / 2 and w / 2 + 4 (8 outputs each).
 template <int JP>
-__device__ __forceinline__ void heads_outputs_mma(const float* f_s, int ldf, const float* wj_s,
+__device__ __forceinline__ void heads_outputs_mma(const float* f_s, int ldf, const uint32_t* wj_s,
                                                   int ldj, int F, float* out_s) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3, mt = warp & 1, nt0 = warp >> 1;
@@ -284,10 +296,10 @@ __device__ __forceinline__ void heads_outputs_mma(const float* f_s, int ldf, con
     for (int i = 0; i < 2; ++i) {
       const int nt = nt0 + 4 * i;
       if (nt >= NT) continue;
-      const float* b = wj_s + (16 * ks + 2 * tig) * ldj + nt * 8 + gid;
-      uint32_t bh[2], bl[2];
-      split_pair(b[0], b[ldj], bh[0], bl[0]);
-      split_pair(b[8 * ldj], b[9 * ldj], bh[1], bl[1]);
+      const uint32_t* b = wj_s + (16 * ks + 2 * tig) * ldj + nt * 8 + gid;
+      const uint32_t w0 = b[0], w1 = b[ldj], w8 = b[8 * ldj], w9 = b[9 * ldj];
+      const uint32_t bh[2] = {packed_hi(w0, w1), packed_hi(w8, w9)};
+      const uint32_t bl[2] = {packed_lo(w0, w1), packed_lo(w8, w9)};
       mma_split(acc[i], ah, al, bh, bl);
     }
   }
@@ -309,7 +321,7 @@ __device__ __forceinline__ void heads_outputs_mma(const float* f_s, int ldf, con
 template <int JP, int Act>
 __device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, int row0,
                                                        int live, int rows_cap, const float* d_s,
-                                                       int ldd, const float* wj_s, int ldj,
+                                                       int ldd, const uint32_t* wj_s, int ldj,
                                                        const float* f_s, int ldf, float* df,
                                                        __nv_bfloat16* dfb,
                                                        __nv_bfloat16* dfb_lo) {
@@ -322,14 +334,13 @@ __device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, 
   for (int kd = 0; kd < KD; ++kd) load_a_split(a0 + 16 * kd, a0 + 8 * ldd + 16 * kd, dh[kd], dl[kd]);
   for (int nt = warp >> 1; nt < F / 8; nt += 4) {
     float acc[4] = {};
-    const float* wb = wj_s + (nt * 8 + gid) * ldj + 2 * tig;
+    const uint32_t* wb = wj_s + (nt * 8 + gid) * ldj + 2 * tig;
 #pragma unroll
     for (int kd = 0; kd < KD; ++kd) {
-      const float2 b0 = *reinterpret_cast<const float2*>(wb + 16 * kd);
-      const float2 b1 = *reinterpret_cast<const float2*>(wb + 16 * kd + 8);
-      uint32_t bh[2], bl[2];
-      split_pair(b0.x, b0.y, bh[0], bl[0]);
-      split_pair(b1.x, b1.y, bh[1], bl[1]);
+      const uint2 b0 = *reinterpret_cast<const uint2*>(wb + 16 * kd);
+      const uint2 b1 = *reinterpret_cast<const uint2*>(wb + 16 * kd + 8);
+      const uint32_t bh[2] = {packed_hi(b0.x, b0.y), packed_hi(b1.x, b1.y)};
+      const uint32_t bl[2] = {packed_lo(b0.x, b0.y), packed_lo(b1.x, b1.y)};
       mma_split(acc, dh[kd], dl[kd], bh, bl);
     }
     const int c = nt * 8 + 2 * tig;
@@ -364,13 +375,47 @@ __device__ __forceinline__ void heads_feature_grad_mma(const float* pre, int F, 
   }
 }
 
+// Phase 5 on tensor cores (fused MMA instances): the tile's head weight gradient
+// dW[F][JP] += f^T[F][32] d[32][JP] in split bf16, accumulated in registers across tiles. Warp w
+// owns the 16-feature m-tiles w, w + 8, w + 16, w + 24 (F <= 512) and every output n-tile.
+template <int JP>
+__device__ __forceinline__ void heads_weight_grad_mma(const float* f_s, int ldf, const float* d_s,
+                                                      int ldd, int F, float (&acc)[4][JP / 8][4]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  constexpr int NT = JP / 8;
+#pragma unroll
+  for (int ks = 0; ks < kTileRows / 16; ++ks) {
+    const int r0 = 16 * ks + 2 * tig;  // rows (the reduction index) of this lane's fragments
+    uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float* d0 = d_s + r0 * ldd + nt * 8 + gid;
+      split_pair(d0[0], d0[ldd], bh[nt][0], bl[nt][0]);
+      split_pair(d0[8 * ldd], d0[9 * ldd], bh[nt][1], bl[nt][1]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m0 = 16 * (warp + 8 * i);
+      if (m0 >= F) break;
+      const float* f0 = f_s + r0 * ldf + m0 + gid;  // f^T[m][k] = f_s[k][m]
+      uint32_t ah[4], al[4];
+      split_pair(f0[0], f0[ldf], ah[0], al[0]);
+      split_pair(f0[8], f0[ldf + 8], ah[1], al[1]);
+      split_pair(f0[8 * ldf], f0[9 * ldf], ah[2], al[2]);
+      split_pair(f0[8 * ldf + 8], f0[9 * ldf + 8], ah[3], al[3]);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma_split(acc[i][nt], ah, al, bh[nt], bl[nt]);
+    }
+  }
+}
+
 template <int JP, bool FUSE, int ACT, bool MMA>
 __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
     heads_loss_kernel(HeadsParams p) {
   constexpr int JJ = (JP + 7) / 8;  // outputs per thread in the loss phase
   static_assert(!MMA || JP % 16 == 0, "tensor-core heads: whole 16-output steps");
-  // fused head weight gradient: features k = tid + 256 kf per thread
-  constexpr int KF = (FUSE && MMA) ? 2 : 1;
+
   extern __shared__ __align__(16) float sm[];
   const int F = p.F_pi, Fv = p.F_v, A = p.A;
   const bool shared = (p.f_v == p.f_pi);
@@ -378,6 +423,7 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
   float* f_s = sm + Lo.f;
   float* fv_s = sm + Lo.fv;
   float* wj_s = sm + Lo.wj;
+  uint32_t* wp_s = reinterpret_cast<uint32_t*>(wj_s);  // packed split words (MMA instances)
   float* wv_s = sm + Lo.wv;
   float* bias_s = sm + Lo.bias;
   float* red_s = sm + Lo.red;
@@ -408,7 +454,11 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
     float w = 0.f;
     if (j < A) w = p.w_pi[(size_t)k * A + j];
     else if (j == A && shared) w = p.w_v[k];
-    wj_s[MMA ? k * Lo.ldj + j : i] = w;
+    if constexpr (MMA) {
+      wp_s[k * Lo.ldj + j] = pack_split(w);
+    } else {
+      wj_s[i] = w;
+    }
   }
   if (!shared)
     for (int k = tid; k < Fv; k += kHeadThreads) wv_s[k] = p.w_v[k];
@@ -432,12 +482,18 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
   float dsc[JJ];
 #pragma unroll
   for (int jj = 0; jj < JJ; ++jj) dsc[jj] = 0.f;
-  // fused head dW: features tid, tid + 256 (KF of them) of the thread
-  float accw[KF][FUSE ? JP : 1];
+  // fused head dW: the thread's feature tid over all outputs (CUDA cores), or its fragments of
+  // the warp's m-tiles (tensor cores)
+  float accw[(FUSE && !MMA) ? JP : 1];
 #pragma unroll
-  for (int kf = 0; kf < KF; ++kf)
+  for (int j = 0; j < ((FUSE && !MMA) ? JP : 1); ++j) accw[j] = 0.f;
+  float accm[(FUSE && MMA) ? 4 : 1][(FUSE && MMA) ? JP / 8 : 1][4];
 #pragma unroll
-    for (int j = 0; j < (FUSE ? JP : 1); ++j) accw[kf][j] = 0.f;
+  for (int i = 0; i < ((FUSE && MMA) ? 4 : 1); ++i)
+#pragma unroll
+    for (int nt = 0; nt < ((FUSE && MMA) ? JP / 8 : 1); ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) accm[i][nt][e] = 0.f;
   float accv = 0.f, accb = 0.f;
 
   for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
@@ -450,7 +506,7 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
     // 2. head outputs: warp partials over interleaved 4-feature slices (CUDA cores), or the
     // finished outputs from the tensor cores
     if constexpr (MMA) {
-      heads_outputs_mma<JP>(f_s, Lo.ldf, wj_s, Lo.ldj, F, red_s);
+      heads_outputs_mma<JP>(f_s, Lo.ldf, wp_s, Lo.ldj, F, red_s);
       if (!shared) {
         float v = 0.f;
         const float* vrow = fv_s + lane * Lo.ldv;
@@ -653,7 +709,7 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
 
     // 4. dL/d pre for the towers
     if constexpr (MMA) {
-      heads_feature_grad_mma<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, Lo.ldj,
+      heads_feature_grad_mma<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wp_s, Lo.ldj,
                                       f_s, Lo.ldf, p.d_fpi, p.d_fpi_b, p.d_fpi_b_lo);
     } else {
       store_feature_grad<JP, ACT>(p.f_pi, F, row0, live, p.rows, d_s, Lo.ldd, wj_s, JP, 0, f_s,
@@ -663,24 +719,24 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
       store_feature_grad<JP, ACT>(p.f_v, Fv, row0, live, p.rows, d_s, Lo.ldd, wv_s, 1, A, fv_s,
                                   Lo.ldv, p.d_fv, p.d_fv_b, p.d_fv_b_lo);
     // 5. head weight gradients
-    if constexpr (FUSE) {
+    if constexpr (FUSE && MMA) {
+      heads_weight_grad_mma<JP>(f_s, Lo.ldf, d_s, Lo.ldd, F, accm);
+    } else if constexpr (FUSE) {
+      if (tid < F) {
+        for (int rr = 0; rr < kTileRows; ++rr) {
+          const float fk = f_s[rr * Lo.ldf + tid];
 #pragma unroll
-      for (int kf = 0; kf < KF; ++kf) {
-        const int k = tid + kf * kHeadThreads;
-        if (k < F) {
-          for (int rr = 0; rr < kTileRows; ++rr) {
-            const float fk = f_s[rr * Lo.ldf + k];
-#pragma unroll
-            for (int j = 0; j < JP; j += 4) {
-              const float4 dd = *reinterpret_cast<const float4*>(d_s + rr * Lo.ldd + j);
-              accw[kf][j] = fmaf(fk, dd.x, accw[kf][j]);
-              accw[kf][j + 1] = fmaf(fk, dd.y, accw[kf][j + 1]);
-              accw[kf][j + 2] = fmaf(fk, dd.z, accw[kf][j + 2]);
-              accw[kf][j + 3] = fmaf(fk, dd.w, accw[kf][j + 3]);
-            }
+          for (int j = 0; j < JP; j += 4) {
+            const float4 dd = *reinterpret_cast<const float4*>(d_s + rr * Lo.ldd + j);
+            accw[j] = fmaf(fk, dd.x, accw[j]);
+            accw[j + 1] = fmaf(fk, dd.y, accw[j + 1]);
+            accw[j + 2] = fmaf(fk, dd.z, accw[j + 2]);
+            accw[j + 3] = fmaf(fk, dd.w, accw[j + 3]);
           }
         }
       }
+    }
+    if constexpr (FUSE) {
       if (!shared && tid < Fv)
         for (int rr = 0; rr < kTileRows; ++rr) accv = fmaf(fv_s[rr * Lo.ldv + tid], d_s[rr * Lo.ldd + A], accv);
       if (tid < JP)
@@ -692,15 +748,27 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
   if constexpr (FUSE) {
     float* pp = p.dw_pi_partials + (size_t)blockIdx.x * (F + 1) * A;
     float* pv = p.dw_v_partials + (size_t)blockIdx.x * (Fv + 1);
+    if constexpr (MMA) {
+      const int gid = lane >> 2, tig = lane & 3;
 #pragma unroll
-    for (int kf = 0; kf < KF; ++kf) {
-      const int k = tid + kf * kHeadThreads;
-      if (k < F) {
+      for (int i = 0; i < 4; ++i) {
+        const int m0 = 16 * (warp + 8 * i);
+        if (m0 >= F) break;
 #pragma unroll
-        for (int j = 0; j < JP; ++j) {
-          if (j < A) pp[(size_t)k * A + j] = accw[kf][j];
-          if (shared && j == A) pv[k] = accw[kf][j];
+        for (int nt = 0; nt < JP / 8; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k = m0 + gid + 8 * (e >> 1), j = nt * 8 + 2 * tig + (e & 1);
+            if (j < A) pp[(size_t)k * A + j] = accm[i][nt][e];
+            if (shared && j == A) pv[k] = accm[i][nt][e];
+          }
         }
+      }
+    } else if (tid < F) {
+#pragma unroll
+      for (int j = 0; j < JP; ++j) {
+        if (j < A) pp[(size_t)tid * A + j] = accw[j];
+        if (shared && j == A) pv[tid] = accw[j];
       }
     }
     if (tid < A) pp[(size_t)F * A + tid] = accb;
