@@ -117,11 +117,14 @@ def c2(precision: str = "bf16x3") -> Workload:
     )
 
 
-def c3(precision: str = "bf16x3") -> Workload:
+def c3(precision: str = "fp32") -> Workload:
     """MinAtar-shaped (hangar/recipes/ppo_minatar.py:110-120) with SAME padding: conv 16@3x3
-    ReLU -> flatten 1600 -> 128 ReLU, categorical(6). The conv runs on fp32 CUDA-core
-    kernels in every precision; the default split-bf16 arithmetic of the 1600 -> 128 layer
-    meets the fp32 tolerances."""
+    ReLU -> flatten 1600 -> 128 ReLU, categorical(6), in its stated fp32 arithmetic (every
+    layer is narrower than 256 outputs: CUDA-core kernels). The split-bf16 tensor-core option
+    for the 1600 -> 128 layer stays available (precision="bf16x3"): on the full 65,536-row
+    minibatch its ~1e-5 per-product error flips the ReLU derivative of pre-activations within
+    that distance of zero often enough to put the layer's gradients at ~2e-4 of the exact ones,
+    above the 1e-4 bound, so it is not the default."""
     return Workload(
         name="c3_minatar",
         description="T=128 x N=4096, conv16 3x3 SAME -> 1600 -> 128 ReLU, categorical(6), 4x8",

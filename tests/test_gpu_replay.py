@@ -37,7 +37,7 @@ def _replay_workload(name, t, n, minibatches):
 CASES = {
     "c1": lambda: _replay_workload("c1", 128, 16, 4),
     "c2_bf16x3": lambda: _replay_workload("c2", 8, 8192, 4),
-    "c3_bf16x3": lambda: _replay_workload("c3", 8, 4096, 4),
+    "c3": lambda: _replay_workload("c3", 8, 4096, 4),
     "c5_bf16": lambda: _replay_workload("c5", 4, 4096, 4),
 }
 
