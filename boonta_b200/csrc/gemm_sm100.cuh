@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         const int col = n0 + c + lane;
         const int row0 = m0 + q * 32;
-        if (col < sh.N) epi.apply_col(row0, min(32, M - row0), col, col_v);
+        if (col < sh.N) epi.apply_col(row0, min(32, M - row0), col, col_v, blockIdx.z);
       } else {
         if (row < M) epi.apply(row, n0 + c, v, blockIdx.z);
       }
@@ -832,10 +832,30 @@ struct EpiStore {
   static constexpr bool kTma = false;
   float* out;
   int ld;
-  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32]) const {
+  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32],
+                                            int) const {
 #pragma unroll
     for (int r = 0; r < 32; ++r)
       if (r < nrows) out[(size_t)(row0 + r) * ld + col] = v[r];
+  }
+};
+
+// dW tile in the parameter layout: acc[m = input feature (the bias row last)][n = output
+// feature] stored as split-K partial out[split][m][n] (the [K_in + 1, N_out] kernel+bias
+// layout), staged so that a warp writes 32 consecutive outputs of a row at a time.
+struct EpiDw {
+  static constexpr bool kStaged = true;
+  static constexpr bool kDeep = true;
+  static constexpr bool kTma = false;
+  float* out;
+  int ld;  // N_out
+  size_t split_stride;
+  __device__ __forceinline__ void apply_col(int row0, int nrows, int col, const float (&v)[32],
+                                            int split) const {
+    float* o = out + (size_t)split * split_stride;
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      if (r < nrows) o[(size_t)(row0 + r) * ld + col] = v[r];
   }
 };
 

@@ -263,10 +263,11 @@ int allocate(bt_learner* L) {
       const int dm = lp.kin + 1, dn = lp.ncol;
       const int dk = L->rows_cap;
       if (lp.tc) {
-        // tcgen05 dW^T: tiles of 128 x BN over [kout, kin + 1], split over K (the rows) to
-        // fill one wave of CTAs with at least 8 K blocks (512 rows) per split.
-        const int bn = 128;
-        const int tiles = ceil_div(lp.kout, 128) * ceil_div(lp.kin + 1, bn);
+        // tcgen05 dW: tiles of 128 x BN over [kin + 1, kout] (M runs over the wide input side,
+        // so the large input operand is re-read only kout / BN times), split over K (the rows)
+        // to fill one wave of CTAs with at least 8 K blocks (512 rows) per split.
+        lp.dw_bn = (L->cfg.precision == BT_PREC_BF16 && lp.kout % 256 == 0) ? 256 : 128;
+        const int tiles = ceil_div(lp.kin + 1, 128) * ceil_div(lp.kout, lp.dw_bn);
         const int nkb = ceil_div(L->rows_cap, 64);
         int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 8));
         lp.dw_kbps = ceil_div(nkb, splits);
@@ -424,8 +425,9 @@ int allocate_tensor_core(bt_learner* L) {
         BT_TRY(umma::encode_map(fb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64, 64));
         BT_TRY(umma::encode_map(xa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 128));
         BT_TRY(umma::encode_map(xb, w, lp.kout, lp.kin, (uint64_t)lp.kout * 2, 64, 128));
-        BT_TRY(umma::encode_map(wa, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 64));
-        BT_TRY(umma::encode_map(wb, xin, lp.kin + 1, R, (uint64_t)lp.ldx * 2, 64, 64));
+        // dW = [x, 1]^T dz: A = the layer input over (kin + 1, rows), B = dz over (kout, rows)
+        BT_TRY(umma::encode_map(wa, xin, lp.kin + 1, R, (uint64_t)lp.ldx * 2, 64, 64));
+        BT_TRY(umma::encode_map(wb, dz, lp.kout, R, (uint64_t)lp.kout * 2, 64, 64));
       }
       const uint64_t rows = (uint64_t)R, f32_ld = (uint64_t)lp.kout * 4;
       BT_TRY(umma::encode_tile_map(&lp.map_z, lp.z, true, lp.kout, rows, f32_ld, 128));
@@ -556,11 +558,13 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
     BT_TRY(stream_dep(L, s, sw));  // dz of this layer is ready
     const int dm = lp.kin + 1, dn = lp.ncol;
     if (lp.tc) {
-      // dW^T [kout, kin + 1] = dz^T [x, 1], stored transposed as [kin + 1, kout] partials
-      umma::GemmShape sh{lp.kout, lp.kin + 1, rows, lp.dw_kbps, nullptr, count, L->err_d};
-      umma::EpiDwT ep{lp.dw_part, lp.kout, (size_t)dm * dn, lp.kin + 1};
+      // dW [kin + 1, kout] = [x, 1]^T dz, split-K partials in the parameter layout
+      umma::GemmShape sh{lp.kin + 1, lp.kout, rows, lp.dw_kbps, nullptr, count, L->err_d};
+      umma::EpiDw ep{lp.dw_part, lp.kout, (size_t)dm * dn};
       if (L->x3) {
         BT_K(L, kProfGemmDw, sw, umma::launch_gemm<128, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
+      } else if (lp.dw_bn == 256) {
+        BT_K(L, kProfGemmDw, sw, umma::launch_gemm<256, true, true, false>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
       } else {
         BT_K(L, kProfGemmDw, sw, umma::launch_gemm<128, true, true, false>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
       }

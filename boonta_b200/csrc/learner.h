@@ -51,6 +51,7 @@ struct LayerPlan {
   // d_pre (fp32, LayerNorm layers)
   CUtensorMap map_z, map_pre, map_hb, map_hb_lo, map_dzb, map_dzb_lo, map_dpre;
   int fwd_bn = 128;
+  int dw_bn = 128;
   int dw_kbps = 1;
   // GRU (recurrent torso); rows are env-major (row = env * T + t)
   int hidden = 0;
