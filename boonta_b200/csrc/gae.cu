@@ -98,6 +98,9 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
 // Wait until at most `pending` of this thread's most recent commit groups are in flight.
 __device__ __forceinline__ void cp_async_wait_pending(int pending) {
   switch (pending) {

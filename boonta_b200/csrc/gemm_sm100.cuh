@@ -186,66 +186,7 @@ struct GemmShape {
   const int* m_count;  // nullable: live rows bound M (forward / dX)
   const int* k_count;  // nullable: live rows bound K (dW)
   int* err;
-  // Gathered A operand (bf16 operands only; nullable): instead of the A tensor map, the
-  // producer warp copies A's rows from the bf16 table gsrc [*, gld] (columns >= gcols read as
-  // zero), row i of the operand being table row gidx[i]: the rows of the minibatch taken
-  // straight from the rollout. A K-major operand gathers over M (the forward), an MN-major one
-  // over K (the weight gradient).
-  const __nv_bfloat16* gsrc;
-  const int* gidx;
-  int gld, gcols;
 };
-
-// cp.async groups a producer lane keeps in flight before it signals a stage as written
-// (the gathered operand; fewer than the stages of the ring, so the ring cannot stall on it).
-template <int kStages>
-__device__ __forceinline__ constexpr int gather_lag() {
-  return kStages - 1 < 2 ? kStages - 1 : 2;
-}
-
-// One stage of a gathered K-major A tile (128 rows x 64 bf16, 128-byte swizzle, the layout a
-// tiled TMA load writes): lane l copies rows l, l + 32, l + 64, l + 96 (row byte offsets in the
-// table `off`, or -1 for a row past the live count: zeros), eight 16-byte chunks each.
-__device__ __forceinline__ void gather_tile_kmajor(uint8_t* sa, const __nv_bfloat16* src,
-                                                   const long long (&off)[4], int k0, int gcols,
-                                                   int lane) {
-  const uint32_t base = smem_u32(sa);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = lane + 32 * i;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int col = k0 + 8 * c;
-      const bool ok = off[i] >= 0 && col < gcols;
-      const __nv_bfloat16* p = src + (ok ? off[i] + col : 0);
-      cp_async16(base + r * 128 + ((c ^ (r & 7)) << 4), p, ok ? 16u : 0u);
-    }
-  }
-}
-
-// One stage of a gathered MN-major A tile (64 K rows x 128 M columns as two 64-column halves of
-// 8 KB, 128-byte swizzle): lane l copies K rows l and l + 32 (table offsets off0 / off1, -1 for
-// zeros), sixteen 16-byte chunks each.
-__device__ __forceinline__ void gather_tile_mnmajor(uint8_t* sa, const __nv_bfloat16* src,
-                                                    long long off0, long long off1, int m0,
-                                                    int gcols, int lane) {
-  const uint32_t base = smem_u32(sa);
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int kr = lane + 32 * i;
-    const long long off = i ? off1 : off0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int col = m0 + 64 * h + 8 * c;
-        const bool ok = off >= 0 && col < gcols;
-        const __nv_bfloat16* p = src + (ok ? off + col : 0);
-        cp_async16(base + h * 8192 + kr * 128 + ((c ^ (kr & 7)) << 4), p, ok ? 16u : 0u);
-      }
-    }
-  }
-}
 
 // Tensor maps of the operands; a_lo / b_lo are the low bf16 halves of split fp32 operands
 // (X3 mode: x = hi + lo, the product taken as hi*hi + hi*lo + lo*hi).
@@ -288,14 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // round-to-nearest, while the MMAs start the next chunk in the other of two TMEM buffers.
   const int nchunks = max(1, ceil_div(nk, kChunk));
   const uint32_t tcols = nchunks > 1 ? 2 * BN : BN;
-  // a gathered A operand (MN-major, K rows by index; bf16 only) is written by the 32 lanes of
-  // warp 0 with cp.async, each lane arriving on the stage's barrier once its copies landed
-  const bool gather = !X3 && A_MN && sh.gsrc != nullptr;
 
   if (threadIdx.x == 0) {
     s_fail = 0;
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], gather ? 33 : 1);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -328,63 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
 
-  if (warp == 0 && gather) {
-    // Producer with a gathered A: lane 0 loads B by TMA and arms the stage barrier with B's
-    // bytes; every lane copies its two K rows of A with cp.async and arrives once they landed
-    // (after a proxy fence, so the tensor cores' reads see them), lagging kLag stages. The
-    // table offsets of a K block's rows are loaded two blocks ahead.
-    constexpr int kLag = gather_lag<C::kStages>();
-    auto row_off = [&](int i, int h) -> long long {
-      const int k = (kb0 + i) * BK + lane + 32 * h;
-      return (i < nk && k < K) ? (long long)__ldg(sh.gidx + k) * sh.gld : -1ll;
-    };
-    long long c0 = row_off(0, 0), c1 = row_off(0, 1);
-    long long p0 = row_off(1, 0), p1 = row_off(1, 1);
-    int issued = 0;
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % C::kStages;
-      int bad = 0;
-      if (lane == 0) {
-        if (*(volatile int*)&s_fail) bad = 1;
-        else if (i >= C::kStages && !mbar_wait_bounded(&empty[s], ((i / C::kStages) - 1) & 1)) {
-          atomicExch(&s_fail, kErrTimeoutEmpty);
-          bad = 1;
-        }
-      }
-      if (__shfl_sync(0xffffffffu, bad, 0)) break;
-      const long long f0 = row_off(i + 2, 0), f1 = row_off(i + 2, 1);
-      uint8_t* sa = smem + s * C::kStageBytes;
-      uint8_t* sb = sa + C::kABytes;
-      const int k0 = (kb0 + i) * BK;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], C::kBBytes);
-        load_b(sb, &ops.b, k0, &full[s]);
-      }
-      gather_tile_mnmajor(sa, sh.gsrc, c0, c1, m0, sh.gcols, lane);
-      cp_async_commit();
-      if (i >= kLag) {
-        cp_async_wait<kLag>();
-        fence_proxy_async_smem();
-        mbar_arrive(&full[(i - kLag) % C::kStages]);
-      }
-      c0 = p0;
-      c1 = p1;
-      p0 = f0;
-      p1 = f1;
-      issued = i + 1;
-    }
-    // the stages still owed an arrival: their copies land, then they are signalled
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (int i = max(0, issued - kLag); i < issued; ++i) mbar_arrive(&full[i % C::kStages]);
-    if (lane == 0) {
-      // let every TMA copy this CTA issued land before the CTA may leave
-      for (int i = max(0, issued - C::kStages); i < issued; ++i) {
-        const int s = i % C::kStages;
-        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) atomicExch(&s_fail, kErrTimeoutFull);
-      }
-    }
-  } else if (warp == 0) {
+  if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
       for (int i = 0; i < nk; ++i) {
@@ -612,14 +494,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // a gathered A operand (K-major, rows by index; bf16 only) is written by the 32 lanes of
-  // warp 0 with cp.async, each lane arriving on the stage's barrier once its copies landed
-  const bool gather = !X3 && !A_MN && sh.gsrc != nullptr;
   pdl_trigger();
   if (threadIdx.x == 0) {
     s_fail = 0;
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&full[s], gather ? 33 : 1);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -644,72 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles = ceil_div(M, BM) * ntn;
   const int nk = ceil_div(sh.K, BK);
 
-  if (warp == 0 && gather) {
-    // Producer with a gathered A: lane 0 loads B by TMA and arms the stage barrier with B's
-    // bytes; every lane copies its four A rows with cp.async and arrives once they landed
-    // (after a proxy fence, so the tensor cores' reads see them), lagging kLag stages.
-    constexpr int kLag = gather_lag<C::kStages>();
-    int g = 0;
-    bool stop = false;
-    for (int t = blockIdx.x; t < tiles && !stop; t += gridDim.x) {
-      const int m0 = (t / ntn) * BM, n0 = (t % ntn) * BN;
-      long long off[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = m0 + lane + 32 * i;
-        off[i] = row < M ? (long long)__ldg(sh.gidx + row) * sh.gld : -1;
-      }
-      for (int kb = 0; kb < nk; ++kb, ++g) {
-        const int s = g % C::kStages;
-        int bad = 0;
-        if (lane == 0) {
-          if (failed()) bad = 1;
-          else if (g >= C::kStages &&
-                   !mbar_wait_bounded(&empty[s], ((g / C::kStages) - 1) & 1)) {
-            atomicExch(&s_fail, kErrTimeoutEmpty);
-            bad = 1;
-          }
-        }
-        if (__shfl_sync(0xffffffffu, bad, 0)) {
-          stop = true;
-          break;
-        }
-        uint8_t* sa = smem + s * C::kStageBytes;
-        uint8_t* sb = sa + C::kABytes;
-        const int k0 = kb * BK;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], C::kBBytes);
-          if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &ops.b, n0 + 64 * j, k0, &full[s]);
-          } else {
-            tma_load_2d(sb, &ops.b, k0, n0, &full[s]);
-          }
-        }
-        gather_tile_kmajor(sa, sh.gsrc, off, k0, sh.gcols, lane);
-        cp_async_commit();
-        if (g >= kLag) {
-          cp_async_wait<kLag>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full[(g - kLag) % C::kStages]);
-        }
-      }
-    }
-    // the stages still owed an arrival: their copies land, then they are signalled
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    for (int i = max(0, g - kLag); i < g; ++i) mbar_arrive(&full[i % C::kStages]);
-    if (lane == 0) {
-      // let every TMA copy this CTA issued land before the CTA may leave
-      for (int i = max(0, g - C::kStages); i < g; ++i) {
-        const int s = i % C::kStages;
-        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) atomicExch(&s_fail, kErrTimeoutFull);
-      }
-    }
-  } else if (warp == 0) {
+  if (warp == 0) {
     if (lane == 0) {
       int g = 0;  // K blocks issued so far (across tiles)
-
       for (int t = blockIdx.x; t < tiles && !failed(); t += gridDim.x) {
         const int m0 = (t / ntn) * BM, n0 = (t % ntn) * BN;
         for (int kb = 0; kb < nk; ++kb, ++g) {

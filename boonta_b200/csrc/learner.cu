@@ -374,10 +374,6 @@ int allocate_tensor_core(bt_learner* L) {
   BT_TRY(pair(&L->params_b, &L->params_b_lo, L->num_params));
   L->ldx0 = ru8(L->cfg.network.obs_dim + 1);
   BT_TRY(pair(&L->xg, &L->xg_lo, (size_t)R * L->ldx0));
-  if (L->tc_first && !L->x3 && !L->recurrent) {
-    // bf16 operands: the update converts the rollout once and gathers minibatch rows from it
-    BT_TRY(dalloc(L, &L->obs_b, (size_t)L->B * L->ldx0));
-  }
   for (int t = 0; t < L->ntowers; ++t) {
     std::vector<LayerPlan>& layers = L->towers[t].layers;
     for (size_t i = 0; i < layers.size(); ++i) {
@@ -488,12 +484,6 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
     if (lp.tc) {
       umma::GemmShape sh{rows, lp.kout, lp.kin, ceil_div(lp.kin, umma::BK), count, nullptr,
                          L->err_d};
-      if (i == 0 && L->gather_rows && gather) {
-        // the minibatch's rows straight from the bf16 copy of the rollout
-        sh.gsrc = L->obs_b;
-        sh.gidx = gather;
-        sh.gld = sh.gcols = L->ldx0;
-      }
       // The last layer's output is consumed through its pre-activation (the heads apply
       // the activation), so only z is stored for it; the bf16 outputs feed the next layer.
       const bool last = i + 1 == tp.layers.size();
@@ -570,11 +560,6 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
     if (lp.tc) {
       // dW [kin + 1, kout] = [x, 1]^T dz, split-K partials in the parameter layout
       umma::GemmShape sh{lp.kin + 1, lp.kout, rows, lp.dw_kbps, nullptr, count, L->err_d};
-      if (i == 0 && L->gather_rows && idx) {
-        sh.gsrc = L->obs_b;
-        sh.gidx = idx;
-        sh.gld = sh.gcols = L->ldx0;
-      }
       umma::EpiDw ep{lp.dw_part, lp.kout, (size_t)dm * dn};
       if (L->x3) {
         BT_K(L, kProfGemmDw, sw, umma::launch_gemm<128, true, true, true>(lp.dw_ops, sh, ep, lp.dw_splits, sw));
@@ -634,7 +619,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
                cudaStream_t s) {
   const int rows = L->rows_cap;
   const bt_learner_config& c = L->cfg;
-  if (!L->gather_rows) BT_TRY(gather_obs(L, in.obs, in.idx, rows, in.count, s));
+  BT_TRY(gather_obs(L, in.obs, in.idx, rows, in.count, s));
   // separate actor and critic towers run side by side (the critic on a side stream)
   const cudaStream_t sc = side_stream(L, 0, s);
   if (L->ntowers > 1) {
@@ -956,13 +941,6 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
   const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
   const int64_t Bg = L->B * world;
   BT_TRY(bootstrap_and_gae(L, batch, s));
-  if (L->obs_b) {
-    // the rollout's observations as bf16 rows (with the ones column) once per update; every
-    // minibatch's first-layer GEMMs then gather their rows from it
-    BT_K(L, kProfMisc, s, launch_gather_bf16(batch->obs, nullptr, (int)L->B,
-                                             L->cfg.network.obs_dim, L->ldx0, L->obs_b, nullptr,
-                                             nullptr, s));
-  }
   if (world > 1) {
     BT_K(L, kProfMisc, s, launch_local_indices(perm, E * M, L->mb, 0, L->N, L->cfg.rank, L->N * world,
                                 L->rows_cap, L->local_idx, L->local_counts, L->err_d, s));
@@ -985,10 +963,7 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
         in.idx = perm + (size_t)e * Bg + (size_t)m * L->mb;
         in.count = nullptr;
       }
-      L->gather_rows = L->obs_b != nullptr;
-      const int rc = loss_grads(L, in, L->stat_sums + (size_t)i * kNumStatSums, world == 1, s);
-      L->gather_rows = false;
-      BT_TRY(rc);
+      BT_TRY(loss_grads(L, in, L->stat_sums + (size_t)i * kNumStatSums, world == 1, s));
       BT_TRY(optimizer_step(L, i, s));
     }
   }
