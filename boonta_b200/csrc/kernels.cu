@@ -887,6 +887,31 @@ __global__ void gather_bf16_kernel(const float* obs, const int* idx, int rows, i
   }
 }
 
+// Rows idx[r] of a bf16 table [*, ld] (ld a multiple of 8) copied to out [rows, ld], one warp
+// per row in 16-byte chunks; rows past the live count are left as they are.
+__global__ void gather_rows_bf16_kernel(const __nv_bfloat16* src, const int* idx, int rows,
+                                        int ld, __nv_bfloat16* out, const int* count) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
+  if (row >= live_rows(count, rows)) return;
+  const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)idx[row] * ld);
+  uint4* o = reinterpret_cast<uint4*>(out + (size_t)row * ld);
+  const int q8 = ld / 8;
+#pragma unroll 4
+  for (int q = lane; q < q8; q += 32) o[q] = __ldg(s + q);
+}
+
+int launch_gather_rows_bf16(const __nv_bfloat16* src, const int* idx, int rows, int ld,
+                            __nv_bfloat16* out, const int* count, cudaStream_t stream) {
+  if (rows <= 0) return BT_OK;
+  BT_CHECK_ARG(ld % 8 == 0, "gather_rows_bf16: row length %d is not a multiple of 8", ld);
+  BT_CUDA(launch_pdl(gather_rows_bf16_kernel, dim3(ceil_div(rows * 32, 256)), dim3(256), 0,
+                     stream, src, idx, rows, ld, out, count));
+  return BT_OK;
+}
+
 int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
                        __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
                        cudaStream_t stream) {

@@ -120,6 +120,9 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* hi, __nv_bfloat16* l
     *reinterpret_cast<uint2*>(lo + i) = lv;
   }
 }
+// Rows idx[r] of a bf16 table [*, ld] to out [rows, ld] (ld a multiple of 8).
+int launch_gather_rows_bf16(const __nv_bfloat16* src, const int* idx, int rows, int ld,
+                            __nv_bfloat16* out, const int* count, cudaStream_t stream);
 int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
                        __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
                        cudaStream_t stream);

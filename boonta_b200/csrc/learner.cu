@@ -374,6 +374,11 @@ int allocate_tensor_core(bt_learner* L) {
   BT_TRY(pair(&L->params_b, &L->params_b_lo, L->num_params));
   L->ldx0 = ru8(L->cfg.network.obs_dim + 1);
   BT_TRY(pair(&L->xg, &L->xg_lo, (size_t)R * L->ldx0));
+  if (L->tc_first && !L->x3 && !L->recurrent && L->cfg.network.obs_dim >= 1024) {
+    // wide bf16 observations: the update converts the rollout once and gathers each
+    // minibatch's rows from the bf16 copy
+    BT_TRY(dalloc(L, &L->obs_b, (size_t)L->B * L->ldx0));
+  }
   for (int t = 0; t < L->ntowers; ++t) {
     std::vector<LayerPlan>& layers = L->towers[t].layers;
     for (size_t i = 0; i < layers.size(); ++i) {
@@ -467,6 +472,11 @@ int allocate_tensor_core(bt_learner* L) {
 int gather_obs(bt_learner* L, const float* obs, const int* idx, int rows, const int* count,
                cudaStream_t s) {
   if (!L->tc_first) return BT_OK;
+  if (L->gather_rows && idx) {
+    // an update minibatch: its rows from the update's bf16 copy of the rollout
+    BT_K(L, kProfMisc, s, launch_gather_rows_bf16(L->obs_b, idx, rows, L->ldx0, L->xg, count, s));
+    return BT_OK;
+  }
   BT_K(L, kProfMisc, s, launch_gather_bf16(obs, idx, rows, L->cfg.network.obs_dim, L->ldx0, L->xg,
                                            L->xg_lo, count, s));
   return BT_OK;
@@ -941,6 +951,13 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
   const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
   const int64_t Bg = L->B * world;
   BT_TRY(bootstrap_and_gae(L, batch, s));
+  if (L->obs_b) {
+    // the rollout's observations as bf16 rows (with the ones column) once per update: each
+    // epoch reads every row once, so the minibatches then move half the bytes
+    BT_K(L, kProfMisc, s, launch_gather_bf16(batch->obs, nullptr, (int)L->B,
+                                             L->cfg.network.obs_dim, L->ldx0, L->obs_b, nullptr,
+                                             nullptr, s));
+  }
   if (world > 1) {
     BT_K(L, kProfMisc, s, launch_local_indices(perm, E * M, L->mb, 0, L->N, L->cfg.rank, L->N * world,
                                 L->rows_cap, L->local_idx, L->local_counts, L->err_d, s));
@@ -963,7 +980,10 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
         in.idx = perm + (size_t)e * Bg + (size_t)m * L->mb;
         in.count = nullptr;
       }
-      BT_TRY(loss_grads(L, in, L->stat_sums + (size_t)i * kNumStatSums, world == 1, s));
+      L->gather_rows = L->obs_b != nullptr;
+      const int rc = loss_grads(L, in, L->stat_sums + (size_t)i * kNumStatSums, world == 1, s);
+      L->gather_rows = false;
+      BT_TRY(rc);
       BT_TRY(optimizer_step(L, i, s));
     }
   }

@@ -127,6 +127,10 @@ struct bt_learner {
   __nv_bfloat16* params_b = nullptr;  // bf16 shadow of params (written by every Adam step)
   __nv_bfloat16* params_b_lo = nullptr;
   __nv_bfloat16* xg = nullptr;        // gathered minibatch observations [rows, ldx0]
+  // bf16 copy of the rollout's observations [T*N, ldx0] (wide bf16 inputs): each update
+  // minibatch gathers its rows from it (gather_rows, set per minibatch)
+  __nv_bfloat16* obs_b = nullptr;
+  bool gather_rows = false;
   __nv_bfloat16* xg_lo = nullptr;
   int ldx0 = 0;
   // network
