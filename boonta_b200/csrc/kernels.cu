@@ -539,11 +539,8 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
   const uintptr_t a8 = (uintptr_t)p.shadow | (uintptr_t)p.shadow_lo;
   const bool vec = (a16 & 15) == 0 && (a8 & 7) == 0;
   const int64_t n4 = vec ? p.n / 4 : 0;
-  for (int64_t q = first; q < n4; q += stride) {
-    const float4 g = __ldg(reinterpret_cast<const float4*>(p.grads) + q);
-    float4 prm = reinterpret_cast<const float4*>(p.params)[q];
-    float4 m = reinterpret_cast<const float4*>(p.mu)[q];
-    float4 v = reinterpret_cast<const float4*>(p.nu)[q];
+  // two float4 groups per thread and iteration: eight 16-byte loads in flight per thread
+  auto update4 = [&](int64_t q, float4 g, float4 prm, float4 m, float4 v) {
     step(g.x, prm.x, m.x, v.x);
     step(g.y, prm.y, m.y, v.y);
     step(g.z, prm.z, m.z, v.z);
@@ -552,6 +549,25 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
     reinterpret_cast<float4*>(p.mu)[q] = m;
     reinterpret_cast<float4*>(p.nu)[q] = v;
     if (p.shadow) store_bf16x4(p.shadow, p.shadow_lo, 4 * q, prm);
+  };
+  int64_t q = first;
+  for (; q + stride < n4; q += 2 * stride) {
+    const int64_t q2 = q + stride;
+    const float4 g = __ldg(reinterpret_cast<const float4*>(p.grads) + q);
+    const float4 g2 = __ldg(reinterpret_cast<const float4*>(p.grads) + q2);
+    const float4 prm = reinterpret_cast<const float4*>(p.params)[q];
+    const float4 prm2 = reinterpret_cast<const float4*>(p.params)[q2];
+    const float4 m = reinterpret_cast<const float4*>(p.mu)[q];
+    const float4 m2 = reinterpret_cast<const float4*>(p.mu)[q2];
+    const float4 v = reinterpret_cast<const float4*>(p.nu)[q];
+    const float4 v2 = reinterpret_cast<const float4*>(p.nu)[q2];
+    update4(q, g, prm, m, v);
+    update4(q2, g2, prm2, m2, v2);
+  }
+  for (; q < n4; q += stride) {
+    update4(q, __ldg(reinterpret_cast<const float4*>(p.grads) + q),
+            reinterpret_cast<const float4*>(p.params)[q], reinterpret_cast<const float4*>(p.mu)[q],
+            reinterpret_cast<const float4*>(p.nu)[q]);
   }
   for (int64_t i = 4 * n4 + first; i < p.n; i += stride) {
     float prm = p.params[i], m = p.mu[i], v = p.nu[i];
@@ -564,7 +580,7 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
 }
 
 int launch_adam(const AdamParams& p, cudaStream_t stream) {
-  BT_CUDA(launch_pdl(adam_kernel, dim3(2 * kNumSMs), dim3(256), 0, stream, p));
+  BT_CUDA(launch_pdl(adam_kernel, dim3(4 * kNumSMs), dim3(256), 0, stream, p));
   return BT_OK;
 }
 
