@@ -160,6 +160,28 @@ class Learner:
         _lib.check(_lib.lib().bt_learner_get_state(self._h, _ptr(p), _ptr(m), _ptr(v), C.byref(count), _stream()))
         return p, m, v, int(count.value)
 
+    def load_state(self, params: torch.Tensor, mu: torch.Tensor | None = None,
+                   nu: torch.Tensor | None = None, count: torch.Tensor | None = None):
+        """Stream-ordered device copies of a flat state into the handle (no host
+        synchronisation); count is an int32 device scalar. None leaves a part as it is."""
+        cnt = None
+        if count is not None:
+            cnt = count.to(self.device, torch.int32).reshape(1).contiguous()
+        _lib.check(_lib.lib().bt_learner_load_state(
+            self._h, _ptr(params.contiguous()), _ptr(mu.contiguous()) if mu is not None else None,
+            _ptr(nu.contiguous()) if nu is not None else None, _ptr(cnt), _stream()))
+        return cnt  # keeps the source of the asynchronous copy alive for the caller
+
+    def store_state(self):
+        """The handle's state as new device tensors (params, mu, nu, count [int32 scalar]),
+        copied on the current stream without a host synchronisation."""
+        p = torch.empty(self.num_params, dtype=torch.float32, device=self.device)
+        m, v = torch.empty_like(p), torch.empty_like(p)
+        c = torch.empty((), dtype=torch.int32, device=self.device)
+        _lib.check(_lib.lib().bt_learner_store_state(self._h, _ptr(p), _ptr(m), _ptr(v), _ptr(c),
+                                                     _stream()))
+        return p, m, v, c
+
     def params(self) -> dict:
         p, _, _, _ = self.get_state()
         return self.layout.unflatten(p.cpu().numpy())

@@ -15,7 +15,7 @@ is an `OptimizerConfig` describing optax.chain(clip_by_global_norm, adam) instea
 optax object, and arrays are torch CUDA tensors. `PPOState.params` is the flat parameter
 buffer (layout `spec.param_layout`), `optimizer_state` an `AdamState(mu, nu, count)`.
 Keys are integer seeds: the permutations (ppo.py:200) and sampling draws (ppo.py:68) come
-from torch generators seeded by them, not from jax.random (the learner itself is
+from device-side torch generators seeded by them, not from jax.random (the learner itself is
 bit-exact given the same permutations and draws). Anything the learner does not
 implement (auxiliary losses, another advantage estimator, other network modules) raises
 NotImplementedError. Every update and act step runs in the CUDA library; there is no CPU
@@ -67,11 +67,14 @@ class Transition:
 
 @dataclass(frozen=True)
 class AdamState:
-    """optax adam state of the flat parameter buffer (ScaleByAdamState mu, nu, count)."""
+    """optax adam state of the flat parameter buffer (ScaleByAdamState mu, nu, count); count
+    is an int32 device scalar after an update (an int is accepted on the way in). The optax
+    chain's pytree (EmptyState, ScaleByAdamState, EmptyState) is boonta_b200.checkpoint's
+    state_pytree."""
 
     mu: torch.Tensor
     nu: torch.Tensor
-    count: int = 0
+    count: Any = 0
 
 
 @dataclass(frozen=True)
@@ -166,11 +169,22 @@ class PPO:
                                           num_envs, precision=self.precision)
         return self._learners[key]
 
-    def _load(self, lrn, state: PPOState):
+    @staticmethod
+    def _tag(state: PPOState):
         opt = state.optimizer_state
-        tag = (id(state.params), id(opt.mu), id(opt.nu), opt.count)
+        count = opt.count if isinstance(opt.count, int) else id(opt.count)
+        return (id(state.params), id(opt.mu), id(opt.nu), count)
+
+    def _load(self, lrn, state: PPOState):
+        """Brings the handle to `state` unless it already holds it (device copies only)."""
+        tag = self._tag(state)
         if self._loaded.get(id(lrn)) != tag:
-            lrn.set_state(state.params, opt.mu, opt.nu, opt.count)
+            opt = state.optimizer_state
+            count = opt.count
+            if not isinstance(count, torch.Tensor):
+                count = torch.tensor(int(count), dtype=torch.int32)
+            lrn.load_state(state.params.to(lrn.device, torch.float32), opt.mu.to(lrn.device),
+                           opt.nu.to(lrn.device), count.to(lrn.device))
             self._loaded[id(lrn)] = tag
 
     # ---- Algorithm protocol ---------------------------------------------------------------
@@ -211,10 +225,10 @@ class PPO:
         return self._learner(1, n)
 
     def _permutations(self, key, batch: int, device) -> torch.Tensor:
-        g = torch.Generator(device="cpu").manual_seed(_seed(key))
-        perms = torch.stack([torch.randperm(batch, generator=g)
-                             for _ in range(self.cfg.update_epochs)])
-        return perms.to(device=device, dtype=torch.int32)
+        """One permutation of the batch per epoch (ppo.py:199-203), drawn on the device."""
+        g = torch.Generator(device=device).manual_seed(_seed(key))
+        return torch.stack([torch.randperm(batch, generator=g, device=device, dtype=torch.int32)
+                            for _ in range(self.cfg.update_epochs)])
 
     def _batch(self, transitions: Transition) -> dict:
         f, s, aux = transitions.first, transitions.second, transitions.aux
@@ -244,10 +258,12 @@ class PPO:
         batch = self._batch(transitions)
         perms = self._permutations(key, self._perm_size(t, n), batch["reward"].device)
         self.metrics = lrn.update(batch, perms)
-        params, mu, nu, count = lrn.get_state()
-        new = replace(state, params=params, optimizer_state=AdamState(mu, nu, count))
-        opt = new.optimizer_state
-        self._loaded[id(lrn)] = (id(new.params), id(opt.mu), id(opt.nu), opt.count)
+        # the new state in fresh device buffers (the old state stays valid, as in JAX), copied
+        # on the stream with no host synchronisation
+        params, mu, nu, count = lrn.store_state()
+        new = replace(state, step=state.step, params=params,
+                      optimizer_state=AdamState(mu, nu, count))
+        self._loaded[id(lrn)] = self._tag(new)
         return new
 
     def _perm_size(self, t: int, n: int) -> int:
