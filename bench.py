@@ -505,6 +505,9 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-p2p", action="store_true",
+                    help="multi-GPU: NCCL all-reduce + full optimizer step instead of the NVLink "
+                         "peer-memory exchange")
     ap.add_argument("--no-profile", action="store_true",
                     help="skip the per-kernel-class profiled pass (for ncu launch lists)")
     args = ap.parse_args()
@@ -536,6 +539,8 @@ def main():
             uid.copy_(torch.frombuffer(bytearray(Learner.nccl_unique_id()), dtype=torch.uint8))
         dist.broadcast(uid, 0)
         lrn.comm_init(bytes(uid.cpu().numpy()))
+        if args.no_p2p:
+            lrn.use_p2p(False)
     lrn.set_state(init_params(w.network, seed=0, init=w.init))
 
     roll = device_rollout(w, seed=100 + rank, device=device)

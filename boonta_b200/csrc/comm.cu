@@ -22,6 +22,8 @@ struct NcclApi {
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
@@ -43,9 +45,11 @@ static int load_nccl() {
   g_nccl.GetUniqueId = (decltype(g_nccl.GetUniqueId))dlsym(h, "ncclGetUniqueId");
   g_nccl.CommInitRank = (decltype(g_nccl.CommInitRank))dlsym(h, "ncclCommInitRank");
   g_nccl.AllReduce = (decltype(g_nccl.AllReduce))dlsym(h, "ncclAllReduce");
+  g_nccl.AllGather = (decltype(g_nccl.AllGather))dlsym(h, "ncclAllGather");
   g_nccl.CommDestroy = (decltype(g_nccl.CommDestroy))dlsym(h, "ncclCommDestroy");
   g_nccl.GetErrorString = (decltype(g_nccl.GetErrorString))dlsym(h, "ncclGetErrorString");
-  if (!g_nccl.GetUniqueId || !g_nccl.CommInitRank || !g_nccl.AllReduce || !g_nccl.CommDestroy ||
+  if (!g_nccl.GetUniqueId || !g_nccl.CommInitRank || !g_nccl.AllReduce || !g_nccl.AllGather ||
+      !g_nccl.CommDestroy ||
       !g_nccl.GetErrorString) {
     set_error("NCCL library lacks a required symbol");
     return BT_ERR_NCCL;
@@ -81,6 +85,29 @@ int comm_allreduce_f32(Comm* c, float* buf, size_t n, cudaStream_t stream) {
 int comm_allreduce_f64(Comm* c, double* buf, size_t n, cudaStream_t stream) {
   BT_NCCL(g_nccl.AllReduce(buf, buf, n, ncclFloat64, ncclSum, c->comm, stream));
   return BT_OK;
+}
+
+// Blocking all-gather of `bytes` host bytes per rank through the communicator (set-up only).
+static int comm_allgather_host(void* ctx, const void* send, void* recv, size_t bytes) {
+  Comm* c = static_cast<Comm*>(ctx);
+  uint8_t* d = nullptr;
+  BT_CUDA(cudaMalloc(&d, bytes * (c->size + 1)));
+  int rc = BT_OK;
+  if (cudaMemcpy(d, send, bytes, cudaMemcpyHostToDevice) != cudaSuccess) rc = BT_ERR_CUDA;
+  if (rc == BT_OK) {
+    ncclResult_t r = g_nccl.AllGather(d, d + bytes, bytes, ncclUint8, c->comm, 0);
+    if (r != ncclSuccess) {
+      set_error("ncclAllGather failed: %s", g_nccl.GetErrorString(r));
+      rc = BT_ERR_NCCL;
+    }
+  }
+  if (rc == BT_OK && cudaStreamSynchronize(0) != cudaSuccess) rc = BT_ERR_CUDA;
+  if (rc == BT_OK &&
+      cudaMemcpy(recv, d + bytes, bytes * c->size, cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = BT_ERR_CUDA;
+  if (rc == BT_ERR_CUDA) set_error("comm_allgather_host: CUDA copy failed");
+  cudaFree(d);
+  return rc;
 }
 
 void comm_destroy(Comm* c) {
@@ -120,5 +147,6 @@ extern "C" int bt_learner_comm_init(bt_learner* L, const void* unique_id, int32_
     return BT_ERR_NCCL;
   }
   L->comm = c;
-  return BT_OK;
+  // the NVLink peer-memory exchange (exchange.cu) when every rank can map every peer
+  return exchange_create(L, comm_allgather_host, c);
 }

@@ -746,6 +746,7 @@ int bootstrap_and_gae(bt_learner* L, const bt_batch* b, cudaStream_t s) {
 }
 
 int optimizer_step(bt_learner* L, int step, cudaStream_t s) {
+  if (exchange_active(L)) return exchange_optimizer_step(L, step, s);
   const bt_optimizer& o = L->cfg.optimizer;
   AdamParams ap{};
   ap.params = L->params;
@@ -819,6 +820,7 @@ extern "C" void bt_learner_destroy(bt_learner* L) {
   if (!L) return;
   if (L->graph) cudaGraphExecDestroy(L->graph);  // before the communicator it may use
   if (L->cap_stream) cudaStreamDestroy(L->cap_stream);
+  if (L->xchg) exchange_destroy(L->xchg);
   if (L->comm) comm_destroy(L->comm);
   for (cudaEvent_t e : L->prof.pool) cudaEventDestroy(e);
   for (cudaEvent_t e : L->fork_events) cudaEventDestroy(e);
@@ -928,6 +930,11 @@ extern "C" int bt_learner_check(bt_learner* L, void* stream) {
     set_error("a rank's share of a global minibatch exceeded the learner's capacity");
     return BT_ERR_CAPACITY;
   }
+  if (code == 31) {  // kErrExchange (exchange.cu)
+    set_error("a barrier of the NVLink gradient exchange gave up (a peer did not arrive); the "
+              "update's results are invalid");
+    return BT_ERR_TIMEOUT;
+  }
   if (code == 21) {  // kErrGruBarrier (gru_seq.cu)
     set_error("a step barrier of the recurrent sequence kernels gave up; its results are invalid");
     return BT_ERR_TIMEOUT;
@@ -987,6 +994,7 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
       BT_TRY(optimizer_step(L, i, s));
     }
   }
+  if (exchange_active(L)) BT_TRY(exchange_gather_moments(L, s));
   BT_K(L, kProfMisc, s, launch_increment(L->count_d, E * M, s));
   if (L->comm) BT_TRY(comm_allreduce_f64(L->comm, L->stat_sums, (size_t)E * M * kNumStatSums, s));
   if (stats) BT_K(L, kProfStats, s, launch_stat_finalize(L->stat_sums, E * M, 1.0f / (float)L->mb, stats, s));

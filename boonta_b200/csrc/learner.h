@@ -83,7 +83,8 @@ struct TowerPlan {
   int out_dim = 0;
 };
 
-struct Comm;  // NCCL communicator (comm.cu)
+struct Comm;      // NCCL communicator (comm.cu)
+struct Exchange;  // NVLink peer-memory gradient exchange (exchange.cu)
 
 // Kernel classes of the per-class device-time profile (bt_learner_profile_read).
 enum ProfClass {
@@ -183,6 +184,8 @@ struct bt_learner {
   int* local_idx = nullptr;
   int* local_counts = nullptr;
   Comm* comm = nullptr;
+  Exchange* xchg = nullptr;  // set up with the communicator when every peer can be mapped
+  bool use_xchg = true;
   std::vector<void*> allocations;
   Profiler prof;
   // Side streams for independent work inside one update (the critic tower next to the
@@ -250,6 +253,13 @@ int launch_gae_internal(const float* reward, const uint8_t* term, const uint8_t*
 int allocate_gru(bt_learner* L, LayerPlan& lp);
 int recurrent_update(bt_learner* L, const bt_batch* b, const int32_t* perm, float* stats,
                      cudaStream_t s);
+bool exchange_active(const bt_learner* L);
+int exchange_optimizer_step(bt_learner* L, int step, cudaStream_t s);
+int exchange_gather_moments(bt_learner* L, cudaStream_t s);
+int exchange_create(bt_learner* L, int (*allgather)(void* ctx, const void* send, void* recv,
+                                                    size_t bytes),
+                    void* ctx);
+void exchange_destroy(Exchange* x);
 }  // namespace bt
 
 // Enqueue one kernel (or collective) launch `call`, counting it and, when profiling is

@@ -482,6 +482,7 @@ int recurrent_update(bt_learner* L, const bt_batch* b, const int32_t* perm, floa
       BT_TRY(optimizer_step(L, i, s));
     }
   }
+  if (exchange_active(L)) BT_TRY(exchange_gather_moments(L, s));
   BT_K(L, kProfMisc, s, launch_increment(L->count_d, E * M, s));
   if (L->comm) BT_TRY(comm_allreduce_f64(L->comm, L->stat_sums, (size_t)E * M * kNumStatSums, s));
   if (stats) {

@@ -294,6 +294,11 @@ class Learner:
         buf = C.create_string_buffer(bytes(unique_id), 128)
         _lib.check(_lib.lib().bt_learner_comm_init(self._h, buf, 128))
 
+    def use_p2p(self, enable: bool = True):
+        """The NVLink peer-memory gradient exchange fused with the optimizer step (default
+        when available), or the NCCL all-reduce with the full optimizer step (False)."""
+        _lib.check(_lib.lib().bt_learner_use_p2p(self._h, int(enable)))
+
 
 def gae(reward, terminated, truncated, values, bootstrap, gamma: float, gae_lambda: float,
         rho=None, c=None):

@@ -299,6 +299,14 @@ BT_API int bt_clip_adam_noalloc(float* params, float* mu, float* nu, const float
 /* ---- multi-GPU (NCCL over NVLink) -------------------------------------------------------- */
 BT_API int bt_nccl_unique_id(void* out, int32_t size); /* size >= 128 bytes */
 BT_API int bt_learner_comm_init(bt_learner* learner, const void* unique_id, int32_t size);
+/* The per-minibatch gradient mean and optimizer step over NVLink peer memory (on by default
+ * when bt_learner_comm_init could map every peer's buffers): each rank reduces its 1/world
+ * slice of the gradient from its peers' memory, runs clip + Adam on that slice and copies the
+ * other slices' new parameters from their owners; 0 switches back to an NCCL all-reduce and
+ * the full optimizer step on every rank (the same results up to the order of the ranks'
+ * sum). Returns BT_ERR_UNSUPPORTED when enabling it without a mapping. The reference's
+ * counterpart is the all-reduce XLA inserts for anakin.py:165-186. */
+BT_API int bt_learner_use_p2p(bt_learner* learner, int32_t enable);
 
 #ifdef __cplusplus
 }

@@ -18,11 +18,16 @@ WORLD = 2
 def _workload(kind):
     if kind == "c4":
         return configs.c4().scaled(num_steps=8, num_envs=32, num_minibatches=4, update_epochs=2)
+    if kind == "fp32_nccl":
+        return _workload("fp32")
     if kind == "fp32_norm":
         # advantage normalisation over the global batch: the moments are summed across ranks
         # (boonta/algorithms/ppo.py:220-221 over the sharded [T, N_global] advantages)
         w = _workload("fp32")
         return dataclasses.replace(w, ppo=dataclasses.replace(w.ppo, normalize_advantage=True))
+    if kind == "bf16":
+        # C5's network and arithmetic (bf16 GEMMs, the bf16 rollout copy) on a small rollout
+        return configs.c5().scaled(num_steps=8, num_envs=64, num_minibatches=4, update_epochs=2)
     return configs.c2(precision=kind).scaled(num_steps=8, num_envs=64, num_minibatches=4,
                                              update_epochs=2)
 
@@ -48,12 +53,15 @@ def _rank_main(rank, port, kind, q):
     uid = [Learner.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     lrn.comm_init(uid[0])
+    if kind == "fp32_nccl":
+        lrn.use_p2p(False)  # the NCCL all-reduce path instead of the NVLink exchange
     lrn.set_state(init_params(w.network, seed=0, init=w.init))
     roll = _rollouts(w)[rank]
     perms = configs.permutations(w, num_ranks=WORLD)
     st = lrn.update(to_device(roll), torch.as_tensor(perms))
     torch.cuda.synchronize()
-    q.put((rank, lrn.get_state()[0].cpu().numpy(), st.cpu().numpy()))
+    p_, mu, nu, _ = lrn.get_state()
+    q.put((rank, p_.cpu().numpy(), st.cpu().numpy(), mu.cpu().numpy(), nu.cpu().numpy()))
     lrn.close()
     dist.destroy_process_group()
 
@@ -67,7 +75,7 @@ def _global(w):
     return out
 
 
-@pytest.mark.parametrize("kind", ["fp32", "bf16x3", "c4", "fp32_norm"])
+@pytest.mark.parametrize("kind", ["fp32", "bf16x3", "c4", "fp32_norm", "fp32_nccl", "bf16"])
 def test_two_gpu_update_matches_the_global_oracle(kind):
     import multiprocessing as mp
     import socket
@@ -89,13 +97,15 @@ def test_two_gpu_update_matches_the_global_oracle(kind):
         p.start()
     res = {}
     for _ in range(WORLD):
-        r, params, stats = q.get(timeout=300)
-        res[r] = (params, stats)
+        r, params, stats, mu, nu = q.get(timeout=300)
+        res[r] = (params, stats, mu, nu)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     np.testing.assert_array_equal(res[0][0], res[1][0])  # replicas stay bitwise equal
     np.testing.assert_array_equal(res[0][1], res[1][1])
+    np.testing.assert_array_equal(res[0][2], res[1][2])  # Adam's moments replicated too
+    np.testing.assert_array_equal(res[0][3], res[1][3])
 
     w = _workload(kind)
     params = init_params(w.network, seed=0, init=w.init)
@@ -105,6 +115,21 @@ def test_two_gpu_update_matches_the_global_oracle(kind):
     if kind == "c4":
         op, _, ostats, _ = recurrent.update(gw.network, gw.ppo, gw.optimizer, params,
                                             optim.init_state(params), roll, perms)
+    elif kind == "bf16":
+        from _parity import check_params
+
+        from boonta_b200.spec import param_layout
+
+        op64, _, _, _ = oppo.update(gw.network, gw.ppo, gw.optimizer, params,
+                                    optim.init_state(params, np.float64), roll, perms,
+                                    precision="bf16", dtype=np.float64)
+        op32, _, ostats, _ = oppo.update(gw.network, gw.ppo, gw.optimizer, params,
+                                         optim.init_state(params), roll, perms, precision="bf16")
+        got = param_layout(w.network).unflatten(res[0][0])
+        bad = check_params("2-GPU bf16", "bf16", params, got, op64, op32,
+                           w.ppo.update_epochs * w.ppo.num_minibatches, w.optimizer.lr)
+        assert not bad, bad
+        return
     else:
         op, _, ostats, _ = oppo.update(gw.network, gw.ppo, gw.optimizer, params,
                                        optim.init_state(params), roll, perms)
