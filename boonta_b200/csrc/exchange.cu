@@ -25,7 +25,7 @@
 //
 // Barriers: a single thread stores this rank's barrier count into a flag slot of every rank's
 // mailbox (system-scope release) and waits until every slot of its own mailbox has reached that
-// count (system-scope acquire). The wait is bounded (2 s): a rank that gives up records
+// count (system-scope acquire). The wait is bounded (10 s): a rank that gives up records
 // kErrExchange in the learner's error word and returns, and bt_learner_check reports it.
 #include <algorithm>
 #include <vector>
@@ -37,6 +37,9 @@ namespace bt {
 constexpr int kXchgMaxRanks = 8;
 constexpr int kErrExchange = 31;
 constexpr int kXchgBlocks = 4 * kNumSMs;
+// A barrier gives up after 10 s: ranks can start an update seconds apart (process start-up,
+// lazy module loading), far beyond any wait inside a running update.
+constexpr uint64_t kXchgWaitNs = 10000000000ull;
 
 struct XchgBox {
   unsigned long long flag[kXchgMaxRanks];  // the last barrier count rank p reached
@@ -94,7 +97,7 @@ __global__ void xchg_barrier_kernel(XchgBoxes boxes, XchgBox* own, int rank, int
   const uint64_t t0 = global_timer_ns();
   for (int p = 0; p < world; ++p) {
     while (load_acquire_sys(&own->flag[p]) < c) {
-      if (global_timer_ns() - t0 > 2000000000ull) {
+      if (global_timer_ns() - t0 > kXchgWaitNs) {
         atomicExch(err, kErrExchange);
         return;
       }
