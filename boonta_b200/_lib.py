@@ -39,7 +39,7 @@ EXPORTS = (
     "bt_learner_launch_count", "bt_gemm_bf16", "bt_gemm_bf16x3", "bt_clip_adam",
     "bt_clip_adam_noalloc", "bt_learner_use_graphs", "bt_learner_check",
     "bt_selftest_bounded_wait", "bt_learner_load_state", "bt_learner_store_state",
-    "bt_learner_use_p2p",
+    "bt_learner_use_p2p", "bt_learner_exchange_probe",
 )
 
 
@@ -136,6 +136,7 @@ def lib() -> C.CDLL:
         "bt_nccl_unique_id": (C.c_int, [vp, i32]),
         "bt_learner_comm_init": (C.c_int, [vp, vp, i32]),
         "bt_learner_use_p2p": (C.c_int, [vp, i32]),
+        "bt_learner_exchange_probe": (C.c_int, [vp, i32, i32, vp]),
         "bt_learner_profile": (C.c_int, [vp, i32]),
         "bt_learner_profile_read": (C.c_int, [vp, i32, C.c_char_p, i32, C.POINTER(f64),
                                               C.POINTER(i64)]),

@@ -311,6 +311,34 @@ void exchange_destroy(Exchange* x) {
 
 }  // namespace bt
 
+// Diagnostic (no counterpart in the reference): `iters` repetitions of a part of the exchange on
+// the learner's current buffers, enqueued on `stream`, for timing the parts on their own. mode 0:
+// the whole gradient exchange + optimizer step; 1: its three barriers alone; 2: the slice
+// reduction alone; 3: the parameter gather alone. Every rank must make the same calls.
+extern "C" int bt_learner_exchange_probe(bt_learner* L, int32_t mode, int32_t iters,
+                                         void* stream) {
+  BT_CHECK_ARG(L && L->xchg, "bt_learner_exchange_probe: no NVLink exchange on this learner");
+  BT_CHECK_ARG(mode >= 0 && mode <= 3 && iters >= 0, "bt_learner_exchange_probe: mode %d", mode);
+  cudaStream_t s = (cudaStream_t)stream;
+  Exchange* x = L->xchg;
+  const int64_t lo = std::min<int64_t>(x->n, (int64_t)x->rank * x->slice);
+  const int64_t hi = std::min<int64_t>(x->n, lo + x->slice);
+  for (int i = 0; i < iters; ++i) {
+    if (mode == 0) {
+      BT_TRY(exchange_optimizer_step(L, 0, s));
+    } else if (mode == 1) {
+      BT_TRY(launch_barrier(x, nullptr, 0, L->err_d, s));
+      BT_TRY(launch_barrier(x, x->block_sums, kXchgBlocks, L->err_d, s));
+      BT_TRY(launch_barrier(x, nullptr, 0, L->err_d, s));
+    } else if (mode == 2) {
+      BT_TRY(launch_reduce(x, lo, hi, L->grads, s));
+    } else {
+      BT_TRY(launch_gather(x, x->params, L->params, L->params_b, L->params_b_lo, s));
+    }
+  }
+  return BT_OK;
+}
+
 extern "C" int bt_learner_use_p2p(bt_learner* L, int32_t enable) {
   BT_CHECK_ARG(L, "null learner");
   L->use_xchg = enable != 0;

@@ -307,6 +307,12 @@ BT_API int bt_learner_comm_init(bt_learner* learner, const void* unique_id, int3
  * sum). Returns BT_ERR_UNSUPPORTED when enabling it without a mapping. The reference's
  * counterpart is the all-reduce XLA inserts for anakin.py:165-186. */
 BT_API int bt_learner_use_p2p(bt_learner* learner, int32_t enable);
+/* Timing diagnostic of the NVLink exchange (no counterpart in the reference): `iters`
+ * repetitions of one part on the learner's current buffers (mode 0: the whole gradient
+ * exchange + optimizer step; 1: its three barriers; 2: the slice reduction; 3: the parameter
+ * gather). Every rank must make the same calls; the buffers' contents become meaningless. */
+BT_API int bt_learner_exchange_probe(bt_learner* learner, int32_t mode, int32_t iters,
+                                     void* stream);
 
 #ifdef __cplusplus
 }
