@@ -311,6 +311,8 @@ void exchange_destroy(Exchange* x) {
 
 }  // namespace bt
 
+using namespace bt;
+
 // Diagnostic (no counterpart in the reference): `iters` repetitions of a part of the exchange on
 // the learner's current buffers, enqueued on `stream`, for timing the parts on their own. mode 0:
 // the whole gradient exchange + optimizer step; 1: its three barriers alone; 2: the slice
