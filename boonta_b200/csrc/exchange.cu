@@ -12,13 +12,13 @@
 //      squares;
 //   3. publishes the sum of squares into every peer's mailbox, barrier; every rank now holds
 //      the G partial sums and adds them in rank order (the same global norm everywhere);
-//   4. runs clip + Adam on its slice only (1/G of the optimizer's memory traffic);
-//   5. barrier: every slice is updated;
-//   6. copies the other G - 1 updated parameter slices from their owners (NVLink loads) and
-//      writes their bf16 shadow locally.
+//   4. runs clip + Adam on its slice only (1/G of the optimizer's memory traffic), storing each
+//      new parameter and its bf16 shadow into its own buffers and into every peer's (NVLink
+//      stores, fenced system-wide by each thread);
+//   5. barrier: every slice is updated everywhere.
 // The gradient crosses NVLink once inbound per rank ((G-1)/G of it) and the parameters once
-// ((G-1)/G), the volume of one all-reduce, with the optimizer step on 1/G of the parameters in
-// between. Adam's moments stay sharded during the update (each rank owns its slice's mu / nu)
+// outbound ((G-1)/G), the volume of one all-reduce, with the optimizer step on 1/G of the
+// parameters in between. Adam's moments stay sharded during the update (each rank owns its slice's mu / nu)
 // and are gathered the same way once the update ends, so every rank holds the full state
 // between updates. The mailboxes and the peers' buffers are CUDA IPC mappings set up when the
 // communicator is created (bt_learner_comm_init).
@@ -61,6 +61,8 @@ struct Exchange {
   int rank = 0, world = 1;
   int64_t n = 0, slice = 0;
   bt::XchgPeers grads{}, params{}, mu{}, nu{};
+  __nv_bfloat16* shadow[bt::kXchgMaxRanks] = {};     // peers' bf16 parameter copies
+  __nv_bfloat16* shadow_lo[bt::kXchgMaxRanks] = {};  // (and low halves, split mode)
   bt::XchgBoxes boxes{};
   bt::XchgBox* own = nullptr;
   double* block_sums = nullptr;
@@ -80,29 +82,34 @@ __device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned lo
   return v;
 }
 
-// One thread. With `sums` set, first adds the block partial sums of squares in block order and
-// stores the total into every rank's mailbox slot `rank`. Then the barrier.
+// One warp; lane p < world talks to rank p. With `sums` set, the warp first adds the block
+// partial sums of squares and lane p stores the total into rank p's mailbox slot `rank`. Then the barrier: lane p stores this rank's barrier count into rank
+// p's flag slot (release, system scope: ordered after the lane's own stores) and waits until
+// rank p's slot in this rank's mailbox has reached it (acquire). The data the peers read next
+// (gradients, or parameters pushed by an earlier kernel that fenced its stores) was complete
+// when this kernel started.
 __global__ void xchg_barrier_kernel(XchgBoxes boxes, XchgBox* own, int rank, int world,
                                     const double* sums, int nsums, int* err) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  if (sums) {
-    double t = 0.0;
-    for (int i = 0; i < nsums; ++i) t += sums[i];
-    for (int p = 0; p < world; ++p) boxes.box[p]->sums[rank] = t;
-  }
+  const int p = threadIdx.x;
   const unsigned long long c = own->count + 1;
-  own->count = c;
-  __threadfence_system();  // this GPU's earlier writes are visible to the peers
-  for (int p = 0; p < world; ++p) store_release_sys(&boxes.box[p]->flag[rank], c);
-  const uint64_t t0 = global_timer_ns();
-  for (int p = 0; p < world; ++p) {
+  double t = 0.0;
+  if (sums) {  // fixed lane order and tree: the same total on every launch
+    for (int i = p; i < nsums; i += 32) t += sums[i];
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  if (p < world) {
+    if (sums) boxes.box[p]->sums[rank] = t;
+    store_release_sys(&boxes.box[p]->flag[rank], c);
+    const uint64_t t0 = global_timer_ns();
     while (load_acquire_sys(&own->flag[p]) < c) {
       if (global_timer_ns() - t0 > kXchgWaitNs) {
         atomicExch(err, kErrExchange);
-        return;
+        break;
       }
     }
   }
+  __syncwarp();
+  if (p == 0) own->count = c;
 }
 
 // The rank's slice [lo, hi) of the gradient summed over the ranks (rank order), written over
@@ -215,10 +222,15 @@ int exchange_optimizer_step(bt_learner* L, int step, cudaStream_t s) {
   ap.eps_root = o.eps_root;
   ap.shadow = L->params_b ? L->params_b + lo : nullptr;
   ap.shadow_lo = L->params_b_lo ? L->params_b_lo + lo : nullptr;
+  for (int p = 0; p < x->world; ++p) {
+    if (p == x->rank) continue;
+    ap.push_params[ap.npush] = x->params.buf[p] + lo;
+    ap.push_shadow[ap.npush] = x->shadow[p] ? x->shadow[p] + lo : nullptr;
+    ap.push_shadow_lo[ap.npush] = x->shadow_lo[p] ? x->shadow_lo[p] + lo : nullptr;
+    ++ap.npush;
+  }
   if (hi > lo) BT_K(L, kProfAdam, s, launch_adam(ap, s));
   BT_K(L, kProfAllreduce, s, launch_barrier(x, nullptr, 0, L->err_d, s));
-  BT_K(L, kProfAllreduce, s,
-       launch_gather(x, x->params, L->params, L->params_b, L->params_b_lo, s));
   return BT_OK;
 }
 
@@ -252,11 +264,11 @@ int exchange_create(bt_learner* L, int (*allgather)(void* ctx, const void* send,
   if (rc == BT_OK) rc = dalloc(L, &x->block_sums, kXchgBlocks);
   if (rc == BT_OK && cudaMemset(x->own, 0, sizeof(XchgBox)) != cudaSuccess) rc = BT_ERR_CUDA;
   if (rc == BT_OK && cudaDeviceSynchronize() != cudaSuccess) rc = BT_ERR_CUDA;
-  constexpr int kBufs = 5;
-  void* local[kBufs] = {L->grads, L->params, L->mu, L->nu, x->own};
+  constexpr int kBufs = 7;
+  void* local[kBufs] = {L->grads, L->params, L->mu, L->nu, x->own, L->params_b, L->params_b_lo};
   std::vector<cudaIpcMemHandle_t> mine(kBufs), all((size_t)kBufs * world);
   for (int i = 0; i < kBufs && rc == BT_OK; ++i)
-    if (cudaIpcGetMemHandle(&mine[i], local[i]) != cudaSuccess) rc = BT_ERR_CUDA;
+    if (local[i] && cudaIpcGetMemHandle(&mine[i], local[i]) != cudaSuccess) rc = BT_ERR_CUDA;
   // every rank takes part in the all-gather, mapped or not (a failed handle is sent as zeros
   // and makes every rank fall back together)
   int ok = rc == BT_OK ? 1 : 0;
@@ -271,6 +283,7 @@ int exchange_create(bt_learner* L, int (*allgather)(void* ctx, const void* send,
   for (int p = 0; p < world && ok; ++p) {
     for (int i = 0; i < kBufs; ++i) {
       void* ptr = local[i];
+      if (!ptr) continue;  // no bf16 shadow (fp32 learner) or no low halves
       if (p != rank) {
         if (cudaIpcOpenMemHandle(&ptr, all[(size_t)p * kBufs + i],
                                  cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
@@ -286,7 +299,9 @@ int exchange_create(bt_learner* L, int (*allgather)(void* ctx, const void* send,
         case 1: x->params.buf[p] = f; break;
         case 2: x->mu.buf[p] = f; break;
         case 3: x->nu.buf[p] = f; break;
-        default: x->boxes.box[p] = static_cast<XchgBox*>(ptr); break;
+        case 4: x->boxes.box[p] = static_cast<XchgBox*>(ptr); break;
+        case 5: x->shadow[p] = static_cast<__nv_bfloat16*>(ptr); break;
+        default: x->shadow_lo[p] = static_cast<__nv_bfloat16*>(ptr); break;
       }
     }
   }
@@ -336,7 +351,7 @@ extern "C" int bt_learner_exchange_probe(bt_learner* L, int32_t mode, int32_t it
       BT_TRY(launch_reduce(x, lo, hi, L->grads, s));
     } else {
       BT_TRY(launch_gather(x, x->params, L->params, L->params_b, L->params_b_lo, s));
-    }
+    }  // (mode 3 times the pull-based parameter gather, for comparison with the push)
   }
   return BT_OK;
 }

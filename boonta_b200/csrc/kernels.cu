@@ -549,6 +549,10 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
     reinterpret_cast<float4*>(p.mu)[q] = m;
     reinterpret_cast<float4*>(p.nu)[q] = v;
     if (p.shadow) store_bf16x4(p.shadow, p.shadow_lo, 4 * q, prm);
+    for (int r = 0; r < p.npush; ++r) {
+      reinterpret_cast<float4*>(p.push_params[r])[q] = prm;
+      if (p.push_shadow[r]) store_bf16x4(p.push_shadow[r], p.push_shadow_lo[r], 4 * q, prm);
+    }
   };
   int64_t q = first;
   for (; q + stride < n4; q += 2 * stride) {
@@ -576,7 +580,13 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
     p.mu[i] = m;
     p.nu[i] = v;
     if (p.shadow) store_bf16(p.shadow, p.shadow_lo, i, prm);
+    for (int r = 0; r < p.npush; ++r) {
+      p.push_params[r][i] = prm;
+      if (p.push_shadow[r]) store_bf16(p.push_shadow[r], p.push_shadow_lo[r], i, prm);
+    }
   }
+  // the pushed parameters reach the peers' memory before this thread is done
+  if (p.npush) __threadfence_system();
 }
 
 int launch_adam(const AdamParams& p, cudaStream_t stream) {

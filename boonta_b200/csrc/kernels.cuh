@@ -179,6 +179,13 @@ struct AdamParams {
   float lr, max_norm, b1, b2, eps, eps_root;
   __nv_bfloat16* shadow;     // nullable bf16 copy of params
   __nv_bfloat16* shadow_lo;  // nullable low halves (split bf16 pairs)
+  // Other GPUs' copies of the same elements (NVLink peer memory, already offset like params):
+  // every new parameter (and its bf16 shadow) is also stored there, and each thread fences its
+  // stores system-wide before it finishes. npush = 0: none.
+  int npush;
+  float* push_params[7];
+  __nv_bfloat16* push_shadow[7];
+  __nv_bfloat16* push_shadow_lo[7];
 };
 int launch_adam(const AdamParams& p, cudaStream_t stream);
 
