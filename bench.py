@@ -510,10 +510,18 @@ def main():
                          "peer-memory exchange")
     ap.add_argument("--no-profile", action="store_true",
                     help="skip the per-kernel-class profiled pass (for ncu launch lists)")
+    ap.add_argument("--num-envs", type=int, default=None,
+                    help="fewer environments per GPU (a small case for profiler captures; with "
+                         "--minibatches, the same minibatch shape on a smaller rollout)")
+    ap.add_argument("--minibatches", type=int, default=None)
     args = ap.parse_args()
 
     kw = {"precision": args.precision} if args.precision else {}
     w = configs.make(args.config, **kw)
+    scale = {k: v for k, v in (("num_envs", args.num_envs),
+                               ("num_minibatches", args.minibatches)) if v}
+    if scale:
+        w = w.scaled(**scale)
     if args.impl == "reference":
         return run_reference(args, w)
 
