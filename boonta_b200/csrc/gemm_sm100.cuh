@@ -339,6 +339,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (nk == 0) mma_commit(&acc_full[0]);  // nothing to accumulate: release the epilogue
     }
+  } else if constexpr (Epi::kRowWise) {
+    // Row-wise epilogue (BN = 64, K within one accumulation chunk): the four warps of column
+    // half 0 (warps 2..5, one per TMEM lane quarter) read their rows whole, thread = row; the
+    // other four only release the buffer.
+    static_assert(BN == 64, "row-wise epilogues take 64-column tiles");
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const bool ok = mbar_wait_bounded(&acc_full[0], 0);
+    if (!ok && lane == 0) atomicExch(&s_fail, kErrTimeoutAcc);
+    fence_after_sync();
+    float v[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) v[j] = 0.f;
+    if (ok && half == 0 && nk > 0) {
+      float a[32], b[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16), a);
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + 32u, b);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = a[j];
+        v[32 + j] = b[j];
+      }
+    }
+    fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&acc_empty[0]);
+    if (half == 0) epi.apply_row(m0 + q * 32 + lane, M, v, smem, q * 32 + lane);
   } else {
     // Epilogue warps 2..9: TMEM lane quarter = warp % 4 (the hardware's access rule), column
     // half = (warp - 2) / 4. After the final commit the stage ring is idle, so each warp
@@ -807,6 +834,7 @@ struct EpiDx {
 // into out[split][n][m] (the [K_in + 1, N_out] kernel+bias layout); coalesced across the
 // warp's rows.
 struct EpiDwT {
+  static constexpr bool kRowWise = false;
   static constexpr bool kStaged = false;
   static constexpr bool kDeep = true;
   static constexpr bool kTma = false;
@@ -827,6 +855,7 @@ struct EpiDwT {
 
 // Plain fp32 store of the tile (diagnostics and tests).
 struct EpiStore {
+  static constexpr bool kRowWise = false;
   static constexpr bool kStaged = true;
   static constexpr bool kDeep = false;
   static constexpr bool kTma = false;
@@ -844,6 +873,7 @@ struct EpiStore {
 // feature] stored as split-K partial out[split][m][n] (the [K_in + 1, N_out] kernel+bias
 // layout), staged so that a warp writes 32 consecutive outputs of a row at a time.
 struct EpiDw {
+  static constexpr bool kRowWise = false;
   static constexpr bool kStaged = true;
   static constexpr bool kDeep = true;
   static constexpr bool kTma = false;

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "mma_sync.cuh"
+#include "ppo_row.cuh"
 
 namespace bt {
 
@@ -637,40 +638,13 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
         lp = group8_sum(acc);
         ent = group8_sum(e);
       }
-      // Surrogate (ppo.py:90-103), with JAX's balanced tie rule for min/max/clip.
+      // Surrogate and value loss (ppo.py:90-115), JAX's balanced tie rule for min/max/clip.
       const float eps = p.clip;
-      const float ratio = expf(lp - lp_old);
-      const float lo = 1.f - eps, hi = 1.f + eps;
-      const float u = fmaxf(ratio, lo);
-      const float du = (ratio == u) ? ((lo == u) ? 0.5f : 1.f) : 0.f;
-      const float clipped = fminf(u, hi);
-      const float dm = (u == clipped) ? ((hi == clipped) ? 0.5f : 1.f) : 0.f;
-      const float s1 = ratio * adv, s2 = clipped * adv;
-      const float mn = fminf(s1, s2);
-      const float t1 = (s1 == mn) ? ((s2 == mn) ? 0.5f : 1.f) : 0.f;
-      const float t2 = (s2 == mn) ? ((s1 == mn) ? 0.5f : 1.f) : 0.f;
-      const float g_lp = -((t1 * adv + t2 * adv * (dm * du)) * ratio) * p.inv_mb;
+      const RowLoss rl = ppo_row_loss(lp, lp_old, adv, ret, v_old, value, on, eps, p.clip_value,
+                                      p.inv_mb, p.vf_coef);
+      const float g_lp = rl.g_lp;
       const float g_ent = -p.ent_coef * p.inv_mb;
-      // Value loss (ppo.py:105-115).
-      const float c1 = 0.5f * ((value - ret) * (value - ret));
-      float crit, dcrit;
-      if (p.clip_value) {
-        const float dv = value - v_old;
-        const float uu = fmaxf(dv, -eps);
-        const float duu = (dv == uu) ? ((-eps == uu) ? 0.5f : 1.f) : 0.f;
-        const float cl = fminf(uu, eps);
-        const float dcl = (uu == cl) ? ((eps == cl) ? 0.5f : 1.f) : 0.f;
-        const float vc = v_old + cl;
-        const float c2 = 0.5f * ((vc - ret) * (vc - ret));
-        crit = fmaxf(c1, c2);
-        const float w1 = (c1 == crit) ? ((c2 == crit) ? 0.5f : 1.f) : 0.f;
-        const float w2 = (c2 == crit) ? ((c1 == crit) ? 0.5f : 1.f) : 0.f;
-        dcrit = w1 * (value - ret) + w2 * (vc - ret) * (dcl * duu);
-      } else {
-        crit = c1;
-        dcrit = value - ret;
-      }
-      const float d_value = on ? p.vf_coef * p.inv_mb * dcrit : 0.f;
+      const float d_value = rl.d_value;
 #pragma unroll
       for (int jj = 0; jj < JJ; ++jj) {
         const int j = sub + 8 * jj;
@@ -690,19 +664,7 @@ __global__ void __launch_bounds__(kHeadThreads, (FUSE && MMA) ? 1 : 2)
       }
       if (sub == 0 && on) {
         if (p.d_val) p.d_val[row] = d_value;
-        st[0] += (double)mn;
-        st[1] += (double)ent;
-        st[2] += (double)(lp_old - lp);
-        st[3] += (fabsf(ratio - 1.f) > eps) ? 1.0 : 0.0;
-        st[4] += (double)adv;
-        st[5] += (double)crit;
-        const double res = (double)ret - (double)value;
-        st[6] += res;
-        st[7] += res * res;
-        st[8] += (double)ret;
-        st[9] += (double)ret * (double)ret;
-        st[10] += (double)value;
-        st[11] += 1.0;
+        add_row_stats(st, rl, ent, lp, lp_old, adv, ret, value, eps);
       }
     }
     __syncthreads();

@@ -22,6 +22,7 @@
 
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
+#include "heads_tc.cuh"
 #include "learner.h"
 
 namespace bt {
@@ -298,11 +299,25 @@ int allocate(bt_learner* L) {
     const int rounds = ceil_div(tiles, kNumSMs * per_sm);
     L->heads_blocks = ceil_div(tiles, rounds);
   }
-  L->heads_fused_dw = heads_fuse_dw(L->F_pi, L->F_v, A, L->shared);
+  {
+    const LayerPlan* last = L->towers[0].layers.empty() ? nullptr : &L->towers[0].layers.back();
+    L->tc_heads = last && last->kind == BT_LAYER_DENSE &&
+                  heads_tc_eligible(c.network.head, L->shared, L->recurrent, last->tc, L->F_pi, A);
+  }
+  L->heads_fused_dw = !L->tc_heads && heads_fuse_dw(L->F_pi, L->F_v, A, L->shared);
   // act and the bootstrap evaluate the heads with the update's product arithmetic
-  L->split_pi = heads_split_products(L->F_pi, L->F_v, A, L->shared);
+  L->split_pi = L->tc_heads || heads_split_products(L->F_pi, L->F_v, A, L->shared);
   L->split_v = L->split_pi && L->shared;
-  if (L->heads_fused_dw) {
+  if (L->tc_heads) {
+    // tensor-core heads: one statistic partial per 128-row tile; the head dW GEMM split over
+    // the rows to fill one wave of CTAs with at least 8 K blocks per split
+    L->heads_blocks = ceil_div(L->rows_cap, umma::BM);
+    const int tiles = ceil_div(L->F_pi + 1, umma::BM);
+    const int nkb = ceil_div(L->rows_cap, umma::BK);
+    const int splits = std::max(1, std::min(kNumSMs / tiles, nkb / 8));
+    L->head_dw_kbps = ceil_div(nkb, splits);
+    L->head_pi_splits = L->head_v_splits = ceil_div(nkb, L->head_dw_kbps);
+  } else if (L->heads_fused_dw) {
     // the heads kernel accumulates the head weight gradients, one partial per block
     L->head_pi_splits = L->head_v_splits = L->heads_blocks;
   } else {
@@ -388,6 +403,11 @@ int allocate_tensor_core(bt_learner* L) {
       lp.ldh = ru8(lp.kout + 1);
       BT_TRY(pair(&lp.hb, &lp.hb_lo, (size_t)R * lp.ldh));
       BT_TRY(launch_ones_column(lp.hb, R, lp.kout, lp.ldh, 1.f, 0));
+      if (L->tc_heads && t == 0 && i + 1 == layers.size() && !lp.hb_lo) {
+        // the tensor-core heads read the torso output as split bf16 pairs
+        BT_TRY(dalloc(L, &lp.hb_lo, (size_t)R * lp.ldh));
+        BT_CUDA(cudaMemset(lp.hb_lo, 0, (size_t)R * lp.ldh * 2));
+      }
       BT_TRY(pair(&lp.dzb, &lp.dzb_lo, (size_t)R * lp.kout));
       if (i == 0) {
         lp.xin_b = L->xg;
@@ -444,9 +464,11 @@ int allocate_tensor_core(bt_learner* L) {
                                    (uint64_t)lp.kout * 2, 64));
       lp.map_hb_lo = lp.map_hb;
       lp.map_dzb_lo = lp.map_dzb;
-      if (L->x3) {
+      if (lp.hb_lo) {
         BT_TRY(umma::encode_tile_map(&lp.map_hb_lo, lp.hb_lo, false, lp.kout, rows,
                                      (uint64_t)lp.ldh * 2, 64));
+      }
+      if (L->x3) {
         BT_TRY(umma::encode_tile_map(&lp.map_dzb_lo, lp.dzb_lo, false, lp.kout, rows,
                                      (uint64_t)lp.kout * 2, 64));
       }
@@ -458,6 +480,35 @@ int allocate_tensor_core(bt_learner* L) {
         lp.dw_ops.a_lo = lp.dw_ops.a;
         lp.dw_ops.b_lo = lp.dw_ops.b;
       }
+    }
+  }
+  if (L->tc_heads) {
+    // maps of the three head GEMMs (heads_tc.cuh); every operand is a split bf16 pair
+    const LayerPlan& last = L->towers[0].layers.back();
+    const int F = L->F_pi, H = umma::kHeadCols;
+    BT_TRY(dalloc(L, &L->whb, (size_t)F * H));
+    BT_TRY(dalloc(L, &L->whb_lo, (size_t)F * H));
+    BT_TRY(dalloc(L, &L->dhb, (size_t)R * H));
+    BT_TRY(dalloc(L, &L->dhb_lo, (size_t)R * H));
+    BT_CUDA(cudaMemset(L->dhb, 0, (size_t)R * H * 2));
+    BT_CUDA(cudaMemset(L->dhb_lo, 0, (size_t)R * H * 2));
+    const uint64_t hld = (uint64_t)last.ldh * 2, dld = (uint64_t)H * 2;
+    for (int part = 0; part < 2; ++part) {
+      const __nv_bfloat16* h = part ? last.hb_lo : last.hb;
+      const __nv_bfloat16* w = part ? L->whb_lo : L->whb;
+      const __nv_bfloat16* d = part ? L->dhb_lo : L->dhb;
+      umma::Operands& o = L->head_o_ops;
+      umma::Operands& x = L->head_dx_ops;
+      umma::Operands& g = L->head_dw_ops;
+      // outputs O = h W_h: A = h (K-major, K = F), B = W_h (MN-major, [K = F][N = 64])
+      BT_TRY(umma::encode_map(part ? &o.a_lo : &o.a, h, F, R, hld, 64, 128));
+      BT_TRY(umma::encode_map(part ? &o.b_lo : &o.b, w, H, F, dld, 64, 64));
+      // dL/dy = D W_h^T: A = D (K-major, K = 64), B = W_h (K-major, [N = F][K = 64])
+      BT_TRY(umma::encode_map(part ? &x.a_lo : &x.a, d, H, R, dld, 64, 128));
+      BT_TRY(umma::encode_map(part ? &x.b_lo : &x.b, w, H, F, dld, 64, 128));
+      // head dW = [h, 1]^T D: A = h with its ones column (MN-major over F + 1), B = D (MN-major)
+      BT_TRY(umma::encode_map(part ? &g.a_lo : &g.a, h, F + 1, R, hld, 64, 64));
+      BT_TRY(umma::encode_map(part ? &g.b_lo : &g.b, d, H, R, dld, 64, 64));
     }
   }
   BT_CUDA(cudaDeviceSynchronize());
@@ -497,6 +548,8 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       // The last layer's output is consumed through its pre-activation (the heads apply
       // the activation), so only z is stored for it; the bf16 outputs feed the next layer.
       const bool last = i + 1 == tp.layers.size();
+      // (the tensor-core heads read the last layer's output as split bf16 pairs)
+      const bool out_b = !last || (L->tc_heads && &tp == &L->towers[0]);
       umma::EpiFwd ep;
       ep.f32_map = lp.map_z;
       ep.hi_map = lp.map_hb;
@@ -504,8 +557,8 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       ep.bias = w + (size_t)lp.kin * lp.kout;
       ep.act = lp.act;
       ep.has_f32 = true;
-      ep.has_hi = !lp.ln && !last;
-      ep.has_lo = ep.has_hi && L->x3;
+      ep.has_hi = !lp.ln && out_b;
+      ep.has_lo = ep.has_hi && lp.hb_lo != nullptr;
       if (L->x3) {
         BT_K(L, kProfGemmFwd, s, umma::launch_gemm<128, false, true, true>(lp.fwd_ops, sh, ep, 1, s));
       } else if (lp.fwd_bn == 256) {
@@ -515,8 +568,8 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       }
       if (lp.ln) {
         BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act,
-                                                 lp.y, nullptr, last ? nullptr : lp.hb,
-                                                 last ? nullptr : lp.hb_lo, lp.ldh, lp.mean,
+                                                 lp.y, nullptr, out_b ? lp.hb : nullptr,
+                                                 out_b ? lp.hb_lo : nullptr, lp.ldh, lp.mean,
                                                  lp.rstd, count, s));
       }
     } else if (lp.kind == BT_LAYER_CONV3X3) {
@@ -642,6 +695,50 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   TowerPlan& tv = L->towers[L->ntowers - 1];
   LayerPlan& last_pi = t0.layers.back();
   LayerPlan& last_v = tv.layers.back();
+  cudaStream_t sh = side_stream(L, 3, s);
+  if (L->tc_heads) {
+    // head outputs + loss + dL/dO (one 128-row tile per block), then on a side stream the
+    // statistics and the head weight gradient next to dL/dy and the torso's backward
+    BT_K(L, kProfHeads, s, launch_heads_pack(L->params + L->head_pi_off, L->params + L->head_v_off,
+                                             L->F_pi, L->A, L->whb, L->whb_lo, s));
+    umma::EpiHeadsLoss eh{};
+    eh.A = L->A;
+    eh.count = in.count;
+    eh.idx = in.idx;
+    eh.b_pi = L->params + L->head_pi_off + (size_t)L->F_pi * L->A;
+    eh.b_v = L->params + L->head_v_off + L->F_v;
+    eh.action = static_cast<const int*>(in.action);
+    eh.lp_old = in.lp_old;
+    eh.v_old = in.v_old;
+    eh.adv = in.adv;
+    eh.ret = in.ret;
+    eh.inv_mb = in.inv_mb;
+    eh.clip = c.ppo.clip_coefficient;
+    eh.clip_value = c.ppo.clip_value_loss;
+    eh.ent_coef = c.ppo.entropy_coefficient;
+    eh.vf_coef = c.ppo.value_coefficient;
+    eh.d_hi = L->dhb;
+    eh.d_lo = L->dhb_lo;
+    eh.stat_partials = L->stat_part;
+    BT_K(L, kProfHeads, s, launch_heads_tc_loss(L->head_o_ops, rows, L->F_pi, eh, L->err_d, s));
+    BT_TRY(stream_dep(L, s, sh));
+    BT_K(L, kProfStats, sh, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, sh));
+    umma::EpiHeadsDw ed{L->head_pi_part, L->head_v_part, L->A, L->F_pi};
+    BT_K(L, kProfHeadDw, sh, launch_heads_tc_dw(L->head_dw_ops, L->F_pi, rows, L->head_dw_kbps,
+                                                L->head_pi_splits, in.count, ed, L->err_d, sh));
+    umma::GemmShape shx{rows, L->F_pi, umma::kHeadCols, 1, in.count, nullptr, L->err_d};
+    umma::EpiDx epx;
+    epx.in_map = last_pi.map_pre;
+    epx.f32_map = last_pi.map_dpre;
+    epx.hi_map = last_pi.map_dzb;
+    epx.lo_map = last_pi.map_dzb_lo;
+    epx.act = last_pi.act;
+    epx.has_f32 = last_pi.ln;
+    epx.has_hi = !epx.has_f32;
+    epx.has_lo = epx.has_hi && L->x3;
+    BT_K(L, kProfHeads, s,
+         umma::launch_gemm<128, false, false, true>(L->head_dx_ops, shx, epx, 1, s));
+  } else {
   HeadsParams hp{};
   hp.rows = rows;
   hp.count = in.count;
@@ -687,7 +784,6 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   // [f, 1]^T d_out and [F + 1, 1] = [f, 1]^T d_value) run on a side stream next to the
   // towers' backward; it joins the caller's stream before the gradient reduction, so the
   // next minibatch's heads kernel finds the partial sums consumed.
-  cudaStream_t sh = side_stream(L, 3, s);
   BT_TRY(stream_dep(L, s, sh));
   BT_K(L, kProfStats, sh, launch_stat_reduce(L->stat_part, L->heads_blocks, stat_slot, sh));
   if (!L->heads_fused_dw) {
@@ -697,6 +793,7 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
     BT_K(L, kProfHeadDw, sh, launch_skinny_dw(last_v.pre(), L->F_v, last_v.act, L->d_val, 1,
                                               rows, in.count, L->head_v_splits,
                                               L->head_v_part, sh));
+  }
   }
   // Padded minibatches (multi-GPU, bt_learner_loss_grads): the tensor-core dW GEMMs read whole
   // 64-row blocks up to the live count, and the kernels writing their bf16 dz operands (the

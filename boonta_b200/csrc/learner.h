@@ -166,6 +166,13 @@ struct bt_learner {
   int heads_blocks = 0;
   bool heads_fused_dw = false;  // the heads kernel writes the head weight-gradient partials
   bool split_pi = false, split_v = false;  // heads evaluated with split-bf16 products
+  // tensor-core heads (heads_tc.cuh): packed head kernels W_h [F, 64], the head-output
+  // gradient D [act_rows, 64] (split bf16 pairs), the maps of the three head GEMMs
+  bool tc_heads = false;
+  __nv_bfloat16 *whb = nullptr, *whb_lo = nullptr;
+  __nv_bfloat16 *dhb = nullptr, *dhb_lo = nullptr;
+  bt::umma::Operands head_o_ops{}, head_dx_ops{}, head_dw_ops{};
+  int head_dw_kbps = 1;
   // targets
   float* adv = nullptr;
   float* ret = nullptr;

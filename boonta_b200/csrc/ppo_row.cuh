@@ -1,0 +1,78 @@
+// Per-row PPO loss terms (boonta/algorithms/ppo.py:90-115) shared by the heads kernels.
+#pragma once
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace bt {
+
+// The surrogate, value and entropy terms of one row (ppo.py:90-115) and the gradient factors of
+// the log-prob and the value, with JAX's balanced tie rule for min / max / clip.
+struct RowLoss {
+  float g_lp;     // dL / d log_prob (before the 1 / minibatch factor is applied: included)
+  float d_value;  // dL / d value (zero for dead rows)
+  float mn;       // min(ratio * adv, clip(ratio) * adv)
+  float crit;     // the row's value loss
+  float ratio;
+};
+
+__device__ __forceinline__ RowLoss ppo_row_loss(float lp, float lp_old, float adv, float ret,
+                                                float v_old, float value, bool on, float eps,
+                                                int clip_value, float inv_mb, float vf_coef) {
+  RowLoss o;
+  const float ratio = expf(lp - lp_old);
+  const float lo = 1.f - eps, hi = 1.f + eps;
+  const float u = fmaxf(ratio, lo);
+  const float du = (ratio == u) ? ((lo == u) ? 0.5f : 1.f) : 0.f;
+  const float clipped = fminf(u, hi);
+  const float dm = (u == clipped) ? ((hi == clipped) ? 0.5f : 1.f) : 0.f;
+  const float s1 = ratio * adv, s2 = clipped * adv;
+  const float mn = fminf(s1, s2);
+  const float t1 = (s1 == mn) ? ((s2 == mn) ? 0.5f : 1.f) : 0.f;
+  const float t2 = (s2 == mn) ? ((s1 == mn) ? 0.5f : 1.f) : 0.f;
+  o.g_lp = -((t1 * adv + t2 * adv * (dm * du)) * ratio) * inv_mb;
+  const float c1 = 0.5f * ((value - ret) * (value - ret));
+  float crit, dcrit;
+  if (clip_value) {
+    const float dv = value - v_old;
+    const float uu = fmaxf(dv, -eps);
+    const float duu = (dv == uu) ? ((-eps == uu) ? 0.5f : 1.f) : 0.f;
+    const float cl = fminf(uu, eps);
+    const float dcl = (uu == cl) ? ((eps == cl) ? 0.5f : 1.f) : 0.f;
+    const float vc = v_old + cl;
+    const float c2 = 0.5f * ((vc - ret) * (vc - ret));
+    crit = fmaxf(c1, c2);
+    const float w1 = (c1 == crit) ? ((c2 == crit) ? 0.5f : 1.f) : 0.f;
+    const float w2 = (c2 == crit) ? ((c1 == crit) ? 0.5f : 1.f) : 0.f;
+    dcrit = w1 * (value - ret) + w2 * (vc - ret) * (dcl * duu);
+  } else {
+    crit = c1;
+    dcrit = value - ret;
+  }
+  o.d_value = on ? vf_coef * inv_mb * dcrit : 0.f;
+  o.mn = mn;
+  o.crit = crit;
+  o.ratio = ratio;
+  return o;
+}
+
+// The twelve statistic sums of one live row (order of the heads kernels' partials).
+__device__ __forceinline__ void add_row_stats(double (&st)[kNumStatSums], const RowLoss& r,
+                                              float ent, float lp, float lp_old, float adv,
+                                              float ret, float value, float eps) {
+  st[0] += (double)r.mn;
+  st[1] += (double)ent;
+  st[2] += (double)(lp_old - lp);
+  st[3] += (fabsf(r.ratio - 1.f) > eps) ? 1.0 : 0.0;
+  st[4] += (double)adv;
+  st[5] += (double)r.crit;
+  const double res = (double)ret - (double)value;
+  st[6] += res;
+  st[7] += res * res;
+  st[8] += (double)ret;
+  st[9] += (double)ret * (double)ret;
+  st[10] += (double)value;
+  st[11] += 1.0;
+}
+
+}  // namespace bt
