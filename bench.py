@@ -238,6 +238,46 @@ def gae_bandwidth(w, device, rounds: int = 4) -> dict:
 
 
 # ---- synthetic inputs on the device ----------------------------------------------------------
+def act_timing(w, lrn, roll, device, calls: int = 32) -> dict:
+    """The act step (PPO.step, ppo.py:57-74) through the public Learner.act /
+    Learner.act_recurrent over the N envs of one rollout step, as the rollout loop of
+    anakin.py:46-76 calls it: device time per call (CUDA events around `calls` back-to-back
+    calls, after 3 untimed ones) cycling over the rollout's T observation slices, with uniform
+    (categorical) or normal (gaussian) noise drawn on the device beforehand."""
+    import torch
+
+    t, n, a = w.num_steps, w.num_envs, w.network.action_dim
+    g = torch.Generator(device=device)
+    g.manual_seed(11)
+    noise = (torch.rand((calls, n, a), generator=g, device=device).clamp_(min=1e-30)
+             if w.network.head == "categorical"
+             else torch.randn((calls, n, a), generator=g, device=device))
+    obs = roll["obs"]
+    if w.network.recurrent:
+        h = w.network.towers()[0][-1].features
+        carry = torch.zeros((n, h), device=device)
+        reset = torch.zeros(n, dtype=torch.uint8, device=device)
+        call = lambda i: lrn.act_recurrent(obs[i % t], reset, carry, noise[i])
+    else:
+        call = lambda i: lrn.act(obs[i % t], noise[i])
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize()
+    l0 = lrn.launch_count()
+    stream = torch.cuda.current_stream()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(calls):
+        call(i)
+    e.record(stream)
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / calls
+    return {"ms_per_call": ms, "env_steps_per_s": n / (ms / 1000.0), "rows": n,
+            "gpu_launches_per_call": (lrn.launch_count() - l0) / calls,
+            "note": "device time of Learner.act over one rollout step's N envs (network "
+                    "forward, heads, sampling fused into the heads kernel)"}
+
+
 def device_rollout(w, seed: int, device):
     import torch
 
@@ -651,6 +691,7 @@ def main():
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "e2e": e2e,
+        "act": act_timing(w, lrn, roll, device),
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w)

@@ -39,7 +39,8 @@ EXPORTS = (
     "bt_learner_launch_count", "bt_gemm_bf16", "bt_gemm_bf16x3", "bt_clip_adam",
     "bt_clip_adam_noalloc", "bt_learner_use_graphs", "bt_learner_check",
     "bt_selftest_bounded_wait", "bt_learner_load_state", "bt_learner_store_state",
-    "bt_learner_use_p2p", "bt_learner_exchange_probe",
+    "bt_learner_use_p2p", "bt_learner_exchange_probe", "bt_linear_scan",
+    "bt_linear_scan_backward",
 )
 
 
@@ -113,6 +114,9 @@ def lib() -> C.CDLL:
         "bt_last_error": (C.c_char_p, []),
         "bt_version": (C.c_char_p, []),
         "bt_gae": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f64, f64, vp, vp, vp]),
+        "bt_linear_scan": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+        "bt_linear_scan_backward": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
+                                              i32, vp]),
         "bt_learner_create": (C.c_int, [C.POINTER(LearnerConfig), C.POINTER(vp)]),
         "bt_learner_destroy": (None, [vp]),
         "bt_learner_num_params": (i64, [vp]),

@@ -34,7 +34,6 @@ namespace bt {
 constexpr int kHeadThreads = 256;
 constexpr int kHeadWarps = kHeadThreads / 32;
 constexpr int kTileRows = 32;
-constexpr float kLog2Pi = 1.8378770664093453f;
 
 // Shared-memory layout of the heads kernel, in floats (every region 16-byte aligned).
 struct HeadsLayout {
@@ -890,64 +889,64 @@ int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, con
 
 namespace bt {
 
-// a14: action sampling of PPO.step (boonta/algorithms/ppo.py:57-74) for a row of head
-// outputs. Categorical (boonta/networks/distributions.py:8-23): logits = out / temperature
-// (greedy one-hot of argmax at temperature 0), normalised by log_softmax; the action is
-// argmax(log_softmax(logits) + gumbel) with gumbel = -log(-log(u)). The noise and the
-// log_softmax are evaluated in double and rounded once to float32, and the sum is a
-// float32 add with the first index winning ties, so the index is a deterministic
-// function of (logits, u): the CPU oracle reproduces it bit for bit.
-// Gaussian: action = mean + temperature * sigma * noise, log-prob of that action.
+// a14: the sampling of PPO.step (sample_row, ppo_row.cuh) over rows of head outputs.
 __global__ void sample_kernel(const float* out, const float* scale, int head, int A, int rows,
                               const float* noise, float temperature, void* action,
                               float* log_prob) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
-  const float* o = out + (size_t)r * A;
-  if (head == BT_HEAD_CATEGORICAL) {
-    int* act = reinterpret_cast<int*>(action);
-    if (!(temperature > 0.f)) {
-      int best = 0;
-      for (int j = 1; j < A; ++j)
-        if (o[j] > o[best]) best = j;
-      act[r] = best;
-      log_prob[r] = 0.f;
-      return;
+  sample_row(out + (size_t)r * A, scale, head, A, r, noise, temperature, action, log_prob);
+}
+
+// Fused act step for the CUDA-core heads: one warp per row evaluates the head outputs (as
+// heads_forward_kernel) into the warp's shared-memory row, then lane 0 samples from it (as
+// sample_kernel). Shared memory: (A + 1) floats per warp.
+__global__ void heads_act_kernel(const float* f_pi, int F, const float* f_v, int Fv,
+                                 const float* w_pi, const float* w_v, const float* scale,
+                                 int head, int A, int rows, int act_pi, int act_v,
+                                 bool split_pi, bool split_v, const float* noise,
+                                 float temperature, void* action, float* log_prob, float* value) {
+  extern __shared__ float o_s[];
+  const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + wib;
+  if (row >= rows) return;
+  float* o = o_s + (size_t)wib * (A + 1);
+  const float* f = f_pi + (size_t)row * F;
+  for (int j = 0; j < A; ++j) {
+    float acc = 0.f;
+    for (int k = lane; k < F; k += 32) {
+      const float x = act_forward(f[k], act_pi), w = w_pi[(size_t)k * A + j];
+      acc = split_pi ? split_fma(x, w, acc) : fmaf(x, w, acc);
     }
-    double mx = -INFINITY;
-    for (int j = 0; j < A; ++j) mx = fmax(mx, (double)(o[j] / temperature));
-    double se = 0.0;
-    for (int j = 0; j < A; ++j) se += exp((double)(o[j] / temperature) - mx);
-    const double lse = log(se) + mx;
-    int best = 0;
-    float best_v = -INFINITY;
-    for (int j = 0; j < A; ++j) {
-      const float lj = (float)((double)(o[j] / temperature) - lse);
-      float v = lj;
-      if (noise) {
-        const double u = (double)noise[(size_t)r * A + j];
-        v = lj + (float)(-log(-log(u)));
-      }
-      if (v > best_v || j == 0) {
-        best_v = v;
-        best = j;
-      }
-    }
-    act[r] = best;
-    log_prob[r] = (float)((double)(o[best] / temperature) - lse);
-  } else {
-    float* act = reinterpret_cast<float*>(action);
-    float lp = 0.f;
-    for (int j = 0; j < A; ++j) {
-      const float s = scale[j];
-      const float sig = temperature * ((fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)))) + 1e-3f);
-      const float eps = noise ? noise[(size_t)r * A + j] : 0.f;
-      const float a = o[j] + sig * eps;
-      act[(size_t)r * A + j] = a;
-      if (sig > 0.f) lp += -0.5f * eps * eps - logf(sig) - 0.5f * kLog2Pi;
-    }
-    log_prob[r] = lp;
+    acc = warp_sum(acc);
+    if (lane == 0) o[j] = acc + w_pi[(size_t)F * A + j];
   }
+  const float* fv = f_v + (size_t)row * Fv;
+  float acc = 0.f;
+  for (int k = lane; k < Fv; k += 32) {
+    const float x = act_forward(fv[k], act_v), w = w_v[k];
+    acc = split_v ? split_fma(x, w, acc) : fmaf(x, w, acc);
+  }
+  acc = warp_sum(acc);
+  __syncwarp();
+  if (lane == 0) {
+    if (value) value[row] = acc + w_v[Fv];
+    sample_row(o, scale, head, A, row, noise, temperature, action, log_prob);
+  }
+}
+
+int launch_heads_act(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
+                     const float* w_v, const float* scale, int head, int A, int rows, int act_pi,
+                     int act_v, bool split_pi, bool split_v, const float* noise,
+                     float temperature, void* action, float* log_prob, float* value,
+                     cudaStream_t stream) {
+  if (rows <= 0) return BT_OK;
+  constexpr int kWarps = 8;
+  heads_act_kernel<<<ceil_div(rows, kWarps), 32 * kWarps, kWarps * (A + 1) * sizeof(float),
+                     stream>>>(f_pi, F, f_v, Fv, w_pi, w_v, scale, head, A, rows, act_pi, act_v,
+                               split_pi, split_v, noise, temperature, action, log_prob, value);
+  BT_LAUNCH_CHECK("heads_act_kernel");
+  return BT_OK;
 }
 
 int launch_sample(const float* out, const float* scale, int head, int A, int rows,

@@ -29,6 +29,12 @@ int launch_heads_tc_loss(const umma::Operands& ops, int rows, int F,
   return umma::launch_gemm<umma::kHeadCols, false, true, true>(ops, sh, ep, 1, stream);
 }
 
+int launch_heads_tc_act(const umma::Operands& ops, int rows, int F, const umma::EpiHeadsAct& ep,
+                        int* err, cudaStream_t stream) {
+  umma::GemmShape sh{rows, umma::kHeadCols, F, ceil_div(F, umma::BK), nullptr, nullptr, err};
+  return umma::launch_gemm<umma::kHeadCols, false, true, true>(ops, sh, ep, 1, stream);
+}
+
 int launch_heads_tc_dw(const umma::Operands& ops, int F, int rows, int kblocks_per_split,
                        int splits, const int* count, const umma::EpiHeadsDw& ep, int* err,
                        cudaStream_t stream) {

@@ -130,6 +130,39 @@ struct EpiHeadsLoss {
   }
 };
 
+// Row-wise epilogue of the act step's head-output GEMM: thread = row adds the biases, stores
+// the value and samples the action from the logits (sample_row, through a padded shared-memory
+// row), so the act step needs no separate heads or sampling kernel. The logits are the same
+// accumulations the update's loss epilogue sees for the same row and parameters.
+struct EpiHeadsAct {
+  static constexpr bool kStaged = false;
+  static constexpr bool kDeep = true;
+  static constexpr bool kTma = false;
+  static constexpr bool kRowWise = true;
+  int A;
+  const float* b_pi;
+  const float* b_v;
+  const float* noise;  // nullable: [rows, A] uniforms
+  float temperature;
+  int* action;
+  float* log_prob;
+  float* value;  // nullable
+  __device__ __forceinline__ void apply_row(int row, int M, float (&v)[kHeadCols], uint8_t* scr,
+                                            int trow) const {
+    float* o = reinterpret_cast<float*>(scr) + trow * (kHeadCols + 1);
+    float val = *b_v;
+#pragma unroll
+    for (int j = 0; j < kHeadCols; ++j) {
+      if (j < A) o[j] = v[j] + __ldg(b_pi + j);
+      else if (j == A) val += v[j];
+    }
+    if (row < M) {
+      if (value) value[row] = val;
+      sample_row(o, nullptr, BT_HEAD_CATEGORICAL, A, row, noise, temperature, action, log_prob);
+    }
+  }
+};
+
 // Head weight-gradient tile [F + 1, 64] (row m = feature, the bias last; column j = output):
 // columns j < A go to the actor partials [split][F + 1][A], column A to the critic partials
 // [split][F + 1].
@@ -164,6 +197,9 @@ int launch_heads_pack(const float* w_pi, const float* w_v, int F, int A, __nv_bf
 // Head outputs + loss over `rows` rows (grid: ceil(rows / 128) blocks = statistic partials).
 int launch_heads_tc_loss(const umma::Operands& ops, int rows, int F,
                          const umma::EpiHeadsLoss& ep, int* err, cudaStream_t stream);
+// Act step: head outputs, value and sampled action of `rows` rows.
+int launch_heads_tc_act(const umma::Operands& ops, int rows, int F, const umma::EpiHeadsAct& ep,
+                        int* err, cudaStream_t stream);
 // Head weight gradient over the live rows, split-K partials.
 int launch_heads_tc_dw(const umma::Operands& ops, int F, int rows, int kblocks_per_split,
                        int splits, const int* count, const umma::EpiHeadsDw& ep, int* err,

@@ -65,6 +65,13 @@ bool heads_split_products(int F_pi, int F_v, int A, bool shared);
 int launch_heads_forward(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
                          const float* w_v, int A, int rows, int act_pi, int act_v, float* out,
                          float* value, bool split_pi, bool split_v, cudaStream_t stream);
+// Fused act step (CUDA-core heads): head outputs and the sample of PPO.step in one kernel;
+// action / log_prob per row, value nullable.
+int launch_heads_act(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
+                     const float* w_v, const float* scale, int head, int A, int rows, int act_pi,
+                     int act_v, bool split_pi, bool split_v, const float* noise,
+                     float temperature, void* action, float* log_prob, float* value,
+                     cudaStream_t stream);
 
 // Conv 3x3 SAME stride 1 on NHWC rows (conv.cu): forward z = conv + bias, h = act(z)
 // ([rows, H*W*Cout]); weight gradient as per-block partials [blocks][(9C + 1) * Cout].

@@ -1253,9 +1253,6 @@ extern "C" int bt_learner_loss_grads(bt_learner* L, const bt_batch* batch, const
 }
 
 namespace bt {
-int launch_sample(const float* out, const float* scale, int head, int A, int rows,
-                  const float* noise, float temperature, void* action, float* log_prob,
-                  cudaStream_t stream);
 }
 
 namespace bt {
@@ -1298,13 +1295,31 @@ extern "C" int bt_learner_act(bt_learner* L, const float* obs, int32_t num, cons
     BT_TRY(forward_tower(L, L->towers[t], obs, nullptr, num, nullptr, s));
   TowerPlan& t0 = L->towers[0];
   TowerPlan& tv = L->towers[L->ntowers - 1];
-  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(t0.layers.back().pre(), L->F_pi, tv.layers.back().pre(), L->F_v,
-                              L->params + L->head_pi_off, L->params + L->head_v_off, L->A, num,
-                              t0.layers.back().act, tv.layers.back().act, L->act_out,
-                              value ? value : L->act_val, L->split_pi, L->split_v, s));
-  BT_K(L, kProfMisc, s, launch_sample(L->act_out,
-                       L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr,
-                       L->cfg.network.head, L->A, num, noise, temperature, action, log_prob, s));
+  if (L->tc_heads) {
+    // head outputs on the tensor cores (the update's arithmetic), sampled in the epilogue
+    BT_K(L, kProfHeadsFwd, s, launch_heads_pack(L->params + L->head_pi_off,
+                                                L->params + L->head_v_off, L->F_pi, L->A,
+                                                L->whb, L->whb_lo, s));
+    umma::EpiHeadsAct ea{};
+    ea.A = L->A;
+    ea.b_pi = L->params + L->head_pi_off + (size_t)L->F_pi * L->A;
+    ea.b_v = L->params + L->head_v_off + L->F_v;
+    ea.noise = noise;
+    ea.temperature = temperature;
+    ea.action = static_cast<int*>(action);
+    ea.log_prob = log_prob;
+    ea.value = value;
+    BT_K(L, kProfHeadsFwd, s, launch_heads_tc_act(L->head_o_ops, num, L->F_pi, ea, L->err_d, s));
+    return BT_OK;
+  }
+  // head outputs and the sample in one kernel
+  BT_K(L, kProfHeadsFwd, s,
+       launch_heads_act(t0.layers.back().pre(), L->F_pi, tv.layers.back().pre(), L->F_v,
+                        L->params + L->head_pi_off, L->params + L->head_v_off,
+                        L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr,
+                        L->cfg.network.head, L->A, num, t0.layers.back().act,
+                        tv.layers.back().act, L->split_pi, L->split_v, noise, temperature,
+                        action, log_prob, value, s));
   return BT_OK;
 }
 

@@ -75,4 +75,63 @@ __device__ __forceinline__ void add_row_stats(double (&st)[kNumStatSums], const 
   st[11] += 1.0;
 }
 
+constexpr float kLog2Pi = 1.8378770664093453f;
+
+// a14: action sampling of PPO.step (boonta/algorithms/ppo.py:57-74) for row r of head outputs
+// o[0..A). Categorical (boonta/networks/distributions.py:8-23): logits = o / temperature
+// (greedy argmax at temperature 0), normalised by log_softmax; the action is
+// argmax(log_softmax(logits) + gumbel) with gumbel = -log(-log(u)). The noise and the
+// log_softmax are evaluated in double and rounded once to float32, and the sum is a float32
+// add with the first index winning ties, so the index is a deterministic function of
+// (logits, u): the CPU oracle reproduces it bit for bit. Gaussian: action = mean +
+// temperature * sigma * noise, and the log-prob of that action.
+__device__ inline void sample_row(const float* o, const float* scale, int head, int A, int r,
+                                  const float* noise, float temperature, void* action,
+                                  float* log_prob) {
+  if (head == BT_HEAD_CATEGORICAL) {
+    int* act = reinterpret_cast<int*>(action);
+    if (!(temperature > 0.f)) {
+      int best = 0;
+      for (int j = 1; j < A; ++j)
+        if (o[j] > o[best]) best = j;
+      act[r] = best;
+      log_prob[r] = 0.f;
+      return;
+    }
+    double mx = -INFINITY;
+    for (int j = 0; j < A; ++j) mx = fmax(mx, (double)(o[j] / temperature));
+    double se = 0.0;
+    for (int j = 0; j < A; ++j) se += exp((double)(o[j] / temperature) - mx);
+    const double lse = log(se) + mx;
+    int best = 0;
+    float best_v = -INFINITY;
+    for (int j = 0; j < A; ++j) {
+      const float lj = (float)((double)(o[j] / temperature) - lse);
+      float v = lj;
+      if (noise) {
+        const double u = (double)noise[(size_t)r * A + j];
+        v = lj + (float)(-log(-log(u)));
+      }
+      if (v > best_v || j == 0) {
+        best_v = v;
+        best = j;
+      }
+    }
+    act[r] = best;
+    log_prob[r] = (float)((double)(o[best] / temperature) - lse);
+  } else {
+    float* act = reinterpret_cast<float*>(action);
+    float lp = 0.f;
+    for (int j = 0; j < A; ++j) {
+      const float s = scale[j];
+      const float sig = temperature * ((fmaxf(s, 0.f) + log1pf(expf(-fabsf(s)))) + 1e-3f);
+      const float eps = noise ? noise[(size_t)r * A + j] : 0.f;
+      const float a = o[j] + sig * eps;
+      act[(size_t)r * A + j] = a;
+      if (sig > 0.f) lp += -0.5f * eps * eps - logf(sig) - 0.5f * kLog2Pi;
+    }
+    log_prob[r] = lp;
+  }
+}
+
 }  // namespace bt

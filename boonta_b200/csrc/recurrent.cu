@@ -492,9 +492,6 @@ int recurrent_update(bt_learner* L, const bt_batch* b, const int32_t* perm, floa
   return BT_OK;
 }
 
-int launch_sample(const float* out, const float* scale, int head, int A, int rows,
-                  const float* noise, float temperature, void* action, float* log_prob,
-                  cudaStream_t stream);
 
 // a14 for GRU networks (RecurrentPPO.step, boonta/algorithms/recurrent_ppo.py:72-96): one
 // time step of the network on `num` envs from the caller's carry (zero where reset, the
@@ -511,17 +508,13 @@ int recurrent_act(bt_learner* L, const float* obs, const uint8_t* reset, const f
   BT_K(L, kProfMisc, s, launch_elementwise(set_int_kernel, 1, s, L->rnn_rows, num));
   BT_TRY(forward_tower(L, tp, obs, nullptr, num, L->rnn_rows, s));
   BT_TRY(gru_forward(L, g, prev.h, carry, nullptr, nullptr, L->rnn_rows, num, 1, s));
-  BT_K(L, kProfHeadsFwd, s, launch_heads_forward(g.h, L->F_pi, g.h, L->F_v,
-                                                 L->params + L->head_pi_off,
-                                                 L->params + L->head_v_off, L->A, num,
-                                                 BT_ACT_NONE, BT_ACT_NONE, L->act_out,
-                                                 value ? value : L->act_val, L->split_pi,
-                                                 L->split_v, s));
-  BT_K(L, kProfMisc, s, launch_sample(L->act_out,
-                                      L->head_scale_off >= 0 ? L->params + L->head_scale_off
-                                                             : nullptr,
-                                      L->cfg.network.head, L->A, num, noise, temperature, action,
-                                      log_prob, s));
+  // head outputs and the sample in one kernel
+  BT_K(L, kProfHeadsFwd, s,
+       launch_heads_act(g.h, L->F_pi, g.h, L->F_v, L->params + L->head_pi_off,
+                        L->params + L->head_v_off,
+                        L->head_scale_off >= 0 ? L->params + L->head_scale_off : nullptr,
+                        L->cfg.network.head, L->A, num, BT_ACT_NONE, BT_ACT_NONE, L->split_pi,
+                        L->split_v, noise, temperature, action, log_prob, value, s));
   // rows are env-major with T = 1, so the step's outputs are the carry rows in env order
   BT_CUDA(cudaMemcpyAsync(carry_out, g.h, (size_t)num * H * sizeof(float),
                           cudaMemcpyDeviceToDevice, s));

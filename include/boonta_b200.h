@@ -26,6 +26,9 @@
  *   bt_learner_set_state /
  *   bt_learner_get_state    the PPOState pytree (ppo.py:30-34): params and the optax
  *                           chain state (clip: empty; adam: count, mu, nu)
+ *   bt_linear_scan /
+ *   bt_linear_scan_backward boonta/networks/kernels/scan.py:13-89 (the SSM torso's linear
+ *                           recurrence and its custom VJP; the Pallas Mosaic-GPU kernel)
  *   bt_learner_comm_init    the NCCL communicator behind jax.distributed / XLA's
  *                           all-reduce (hangar/train.py:17-18, anakin.py:165-186)
  *
@@ -154,6 +157,22 @@ BT_API int bt_gae(const float* reward, const uint8_t* terminated, const uint8_t*
            const float* values, const float* bootstrap, const float* rho, const float* c,
            int32_t num_steps, int32_t num_envs, double gamma, double gae_lambda,
            float* advantages, float* returns, void* stream);
+
+/* ---- linear recurrence scan (boonta/networks/kernels/scan.py:13-89) -----------------------
+ * h[b, t, f] = a[b, t, f] * h[b, t-1, f] + bx[b, t, f] with h[b, -1, f] = init[b, f], over
+ * [batch, steps, features] arrays (features contiguous), accumulated in float32 and stored in
+ * `dtype` (the dtype of a; BT_DTYPE_*); init in `init_dtype`. The backward is the reference's
+ * custom VJP: db = reverse scan of the cotangent with multipliers a[t+1], da = db * h[t-1]
+ * (init at t = 0), dinit = db[:, 0] * a[:, 0]. batch <= 65535. Device pointers. */
+#define BT_DTYPE_F32 0
+#define BT_DTYPE_BF16 1
+BT_API int bt_linear_scan(const void* a, const void* b, const void* init, void* out,
+                   int32_t batch, int32_t steps, int32_t features, int32_t dtype,
+                   int32_t init_dtype, void* stream);
+BT_API int bt_linear_scan_backward(const void* a, const void* h, const void* init,
+                            const void* cotangent, void* da, void* db, void* dinit,
+                            int32_t batch, int32_t steps, int32_t features, int32_t dtype,
+                            int32_t init_dtype, void* stream);
 
 /* ---- learner ---------------------------------------------------------------------------- */
 BT_API int bt_learner_create(const bt_learner_config* cfg, bt_learner** out);
