@@ -366,6 +366,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&acc_empty[0]);
     if (half == 0) epi.apply_row(m0 + q * 32 + lane, M, v, smem, q * 32 + lane);
+    if constexpr (Epi::kCoop) {
+      // then all eight epilogue warps work on the tile's rows together
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      epi.coop(smem, m0, M, warp - 2, lane);
+    }
   } else {
     // Epilogue warps 2..9: TMEM lane quarter = warp % 4 (the hardware's access rule), column
     // half = (warp - 2) / 4. After the final commit the stage ring is idle, so each warp

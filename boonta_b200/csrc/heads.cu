@@ -899,18 +899,20 @@ __global__ void sample_kernel(const float* out, const float* scale, int head, in
 }
 
 // Fused act step for the CUDA-core heads: one warp per row evaluates the head outputs (as
-// heads_forward_kernel) into the warp's shared-memory row, then lane 0 samples from it (as
-// sample_kernel). Shared memory: (A + 1) floats per warp.
+// heads_forward_kernel) into the warp's shared-memory row, then samples from it
+// (sample_row_warp, bit-identical to sample_kernel).
 __global__ void heads_act_kernel(const float* f_pi, int F, const float* f_v, int Fv,
                                  const float* w_pi, const float* w_v, const float* scale,
                                  int head, int A, int rows, int act_pi, int act_v,
                                  bool split_pi, bool split_v, const float* noise,
                                  float temperature, void* action, float* log_prob, float* value) {
-  extern __shared__ float o_s[];
+  extern __shared__ double act_s[];  // per warp: 64 doubles of sampling scratch, A + 1 floats
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + wib;
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + wib;
   if (row >= rows) return;
-  float* o = o_s + (size_t)wib * (A + 1);
+  double* es = act_s + (size_t)wib * 64;
+  float* o = reinterpret_cast<float*>(act_s + (size_t)warps * 64) + (size_t)wib * (A + 1);
   const float* f = f_pi + (size_t)row * F;
   for (int j = 0; j < A; ++j) {
     float acc = 0.f;
@@ -928,11 +930,9 @@ __global__ void heads_act_kernel(const float* f_pi, int F, const float* f_v, int
     acc = split_v ? split_fma(x, w, acc) : fmaf(x, w, acc);
   }
   acc = warp_sum(acc);
+  if (lane == 0 && value) value[row] = acc + w_v[Fv];
   __syncwarp();
-  if (lane == 0) {
-    if (value) value[row] = acc + w_v[Fv];
-    sample_row(o, scale, head, A, row, noise, temperature, action, log_prob);
-  }
+  sample_row_warp(o, scale, head, A, row, noise, temperature, action, log_prob, es, lane);
 }
 
 int launch_heads_act(const float* f_pi, int F, const float* f_v, int Fv, const float* w_pi,
@@ -942,8 +942,8 @@ int launch_heads_act(const float* f_pi, int F, const float* f_v, int Fv, const f
                      cudaStream_t stream) {
   if (rows <= 0) return BT_OK;
   constexpr int kWarps = 8;
-  heads_act_kernel<<<ceil_div(rows, kWarps), 32 * kWarps, kWarps * (A + 1) * sizeof(float),
-                     stream>>>(f_pi, F, f_v, Fv, w_pi, w_v, scale, head, A, rows, act_pi, act_v,
+  const size_t smem = kWarps * (64 * sizeof(double) + (A + 1) * sizeof(float));
+  heads_act_kernel<<<ceil_div(rows, kWarps), 32 * kWarps, smem, stream>>>(f_pi, F, f_v, Fv, w_pi, w_v, scale, head, A, rows, act_pi, act_v,
                                split_pi, split_v, noise, temperature, action, log_prob, value);
   BT_LAUNCH_CHECK("heads_act_kernel");
   return BT_OK;

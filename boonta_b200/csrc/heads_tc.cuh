@@ -23,12 +23,19 @@ namespace umma {
 constexpr int kHeadCols = 64;  // packed head outputs (A actor outputs + the value, padded)
 
 // Row-wise epilogue of the head-output GEMM (split-K kernel, BN = 64, one accumulation chunk):
-// thread = row, holding the row's 64 accumulators.
+// thread = row first parks the row's 64 accumulators plus biases in shared memory (rows of
+// kLd floats); then the 256 threads of the eight epilogue warps take the tile's 128 rows, two
+// adjacent lanes per row, each on 32 of the outputs: max, softmax sum, entropy and log-prob
+// combined across the pair by one shuffle (the same value on both), the PPO loss terms, D =
+// dL/dO stored as split bf16 pairs (16-byte stores), and the statistics summed over the warp
+// by a fixed shuffle tree and over the eight warps in order (deterministic).
 struct EpiHeadsLoss {
   static constexpr bool kStaged = false;
   static constexpr bool kDeep = true;
   static constexpr bool kTma = false;
   static constexpr bool kRowWise = true;
+  static constexpr bool kCoop = true;
+  static constexpr int kLd = kHeadCols + 1;
   int A;
   const int* count;  // nullable: live rows
   const int* idx;    // nullable: flat sample index of each row
@@ -45,100 +52,128 @@ struct EpiHeadsLoss {
   __nv_bfloat16* d_lo;
   double* stat_partials;  // [gridDim.x][kNumStatSums]
 
-  // All 128 threads of the four row warps call this, also after a failed accumulator wait
-  // (they meet at named barrier 1).
-  __device__ __forceinline__ void apply_row(int row, int M, float (&v)[kHeadCols], uint8_t* scr,
+  __device__ __forceinline__ void apply_row(int, int, float (&v)[kHeadCols], uint8_t* scr,
                                             int trow) const {
+    float* o = reinterpret_cast<float*>(scr) + trow * kLd;
+    const float bv = *b_v;
+#pragma unroll
+    for (int j = 0; j < kHeadCols; ++j) {
+      if (j < A) o[j] = v[j] + __ldg(b_pi + j);
+      else if (j == A) o[j] = bv + v[j];  // the value
+    }
+  }
+
+  __device__ __forceinline__ void coop(uint8_t* scr, int m0, int M, int ew, int lane) const {
+    // two threads per row (adjacent lanes), thread half h on outputs 32h .. 32h + 31
+    const float* rows_s = reinterpret_cast<const float*>(scr);
+    double* st_s = reinterpret_cast<double*>(scr + BM * kLd * sizeof(float) + 1024);
+    const int t = ew * 32 + lane, r = t >> 1, h = t & 1, jb = 32 * h;
+    const int row = m0 + r;
     const int live = count ? min(M, *count) : M;
     const bool on = row < live;
+    const float* o = rows_s + r * kLd;
     const int flat = on ? (idx ? idx[row] : row) : 0;
     const int act = on ? action[flat] : 0;
-    float mx = -INFINITY, value = *b_v;
-#pragma unroll
-    for (int j = 0; j < kHeadCols; ++j) {
-      if (j < A) {
-        v[j] += __ldg(b_pi + j);
-        mx = fmaxf(mx, v[j]);
-      } else if (j == A) {
-        value += v[j];
-      }
-    }
-    float se = 0.f;
-#pragma unroll
-    for (int j = 0; j < kHeadCols; ++j)
-      if (j < A) se += expf(v[j] - mx);
-    const float lse = logf(se);
-    float ent = 0.f, lp = 0.f;
-#pragma unroll
-    for (int j = 0; j < kHeadCols; ++j) {
-      if (j < A) {
-        const float l = (v[j] - mx) - lse;
-        ent -= expf(l) * l;
-        if (j == act) lp = l;
-      }
-    }
     const float lpo = on ? lp_old[flat] : 0.f;
     const float ad = on ? adv[flat] : 0.f;
     const float rt = on ? ret[flat] : 0.f;
     const float vo = on ? v_old[flat] : 0.f;
+    const float value = o[A];
+    float x[32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      x[j] = jb + j < A ? o[jb + j] : -INFINITY;
+      mx = fmaxf(mx, x[j]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    float se = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      x[j] = x[j] - mx;  // z_j
+      se += jb + j < A ? expf(x[j]) : 0.f;
+    }
+    se = se + __shfl_xor_sync(0xffffffffu, se, 1);  // the pair's two halves, same sum on both
+    const float lse = logf(se);
+    float ent = 0.f, mine = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (jb + j < A) {
+        const float l = x[j] - lse;
+        ent -= expf(l) * l;
+        if (jb + j == act) mine = l;
+      }
+    }
+    ent = ent + __shfl_xor_sync(0xffffffffu, ent, 1);
+    const float lp = mine + __shfl_xor_sync(0xffffffffu, mine, 1);
     const RowLoss rl = ppo_row_loss(lp, lpo, ad, rt, vo, value, on, clip, clip_value, inv_mb,
                                     vf_coef);
     const float g_ent = -ent_coef * inv_mb;
-    // D = dL/dO: the categorical log-prob and entropy gradients, the value gradient in column A
-#pragma unroll
-    for (int j = 0; j < kHeadCols; ++j) {
-      float g = 0.f;
-      if (on && j < A) {
-        const float l = (v[j] - mx) - lse;
-        const float p = expf(l);
-        g = rl.g_lp * (((j == act) ? 1.f : 0.f) - p) + g_ent * (-p * (l + ent));
-      } else if (j == A) {
-        g = rl.d_value;
-      }
-      v[j] = g;
-    }
     if (row < M) {
+      __nv_bfloat16* dh = d_hi + (size_t)row * kHeadCols + jb;
+      __nv_bfloat16* dl = d_lo + (size_t)row * kHeadCols + jb;
 #pragma unroll
-      for (int j = 0; j < kHeadCols; j += 8) {
-        uint32_t h[4], l[4];
+      for (int q = 0; q < 4; ++q) {
+        uint32_t hw[4], lw[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const __nv_bfloat162 hp = __floats2bfloat162_rn(v[j + 2 * i], v[j + 2 * i + 1]);
-          h[i] = *reinterpret_cast<const uint32_t*>(&hp);
-          const __nv_bfloat162 lq = __floats2bfloat162_rn(v[j + 2 * i] - __low2float(hp),
-                                                          v[j + 2 * i + 1] - __high2float(hp));
-          l[i] = *reinterpret_cast<const uint32_t*>(&lq);
+          float g[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = jb + 8 * q + 2 * i + e;
+            float gj = 0.f;
+            if (j == A) {
+              gj = rl.d_value;
+            } else if (on && j < A) {
+              const float l = x[8 * q + 2 * i + e] - lse;
+              const float p = expf(l);
+              gj = rl.g_lp * (((j == act) ? 1.f : 0.f) - p) + g_ent * (-p * (l + ent));
+            }
+            g[e] = gj;
+          }
+          const __nv_bfloat162 hp = __floats2bfloat162_rn(g[0], g[1]);
+          const __nv_bfloat162 lq = __floats2bfloat162_rn(g[0] - __low2float(hp),
+                                                          g[1] - __high2float(hp));
+          hw[i] = *reinterpret_cast<const uint32_t*>(&hp);
+          lw[i] = *reinterpret_cast<const uint32_t*>(&lq);
         }
-        *reinterpret_cast<uint4*>(d_hi + (size_t)row * kHeadCols + j) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(d_lo + (size_t)row * kHeadCols + j) = make_uint4(l[0], l[1], l[2], l[3]);
+        *reinterpret_cast<uint4*>(dh + 8 * q) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(dl + 8 * q) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
     }
-    // block statistic partials: rows in tile order, then thread s < 12 adds the 128 rows
+    // the row's statistics on its h = 0 thread, summed over the warp by a fixed shuffle tree,
+    // then the eight warp sums in warp order by threads 0..11
     double st[kNumStatSums];
 #pragma unroll
-    for (int s = 0; s < kNumStatSums; ++s) st[s] = 0.0;
-    if (on) add_row_stats(st, rl, ent, lp, lpo, ad, rt, value, clip);
-    double* sd = reinterpret_cast<double*>(scr);
+    for (int k = 0; k < kNumStatSums; ++k) st[k] = 0.0;
+    if (on && h == 0) add_row_stats(st, rl, ent, lp, lpo, ad, rt, value, clip);
 #pragma unroll
-    for (int s = 0; s < kNumStatSums; ++s) sd[trow * kNumStatSums + s] = st[s];
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (trow < kNumStatSums) {
-      double t = 0.0;
-      for (int r = 0; r < BM; ++r) t += sd[r * kNumStatSums + trow];
-      stat_partials[(size_t)blockIdx.x * kNumStatSums + trow] = t;
+    for (int k = 0; k < kNumStatSums; ++k) st[k] = warp_sum_d(st[k]);
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < kNumStatSums; ++k) st_s[ew * kNumStatSums + k] = st[k];
+    }
+    asm volatile("bar.sync 3, 256;" ::: "memory");
+    if (t < kNumStatSums) {
+      double sum = 0.0;
+      for (int w = 0; w < kEpiWarps; ++w) sum += st_s[w * kNumStatSums + t];
+      stat_partials[(size_t)blockIdx.x * kNumStatSums + t] = sum;
     }
   }
 };
 
 // Row-wise epilogue of the act step's head-output GEMM: thread = row adds the biases, stores
-// the value and samples the action from the logits (sample_row, through a padded shared-memory
-// row), so the act step needs no separate heads or sampling kernel. The logits are the same
-// accumulations the update's loss epilogue sees for the same row and parameters.
+// the value and the row's logits (padded shared-memory rows); then the eight epilogue warps
+// sample the tile's rows, one warp per row (sample_row_warp), so the act step needs no
+// separate heads or sampling kernel. The logits are the same accumulations the update's loss
+// epilogue sees for the same row and parameters.
 struct EpiHeadsAct {
   static constexpr bool kStaged = false;
   static constexpr bool kDeep = true;
   static constexpr bool kTma = false;
   static constexpr bool kRowWise = true;
+  static constexpr bool kCoop = true;
+  static constexpr int kLd = kHeadCols + 1;  // shared row stride (floats)
   int A;
   const float* b_pi;
   const float* b_v;
@@ -149,17 +184,22 @@ struct EpiHeadsAct {
   float* value;  // nullable
   __device__ __forceinline__ void apply_row(int row, int M, float (&v)[kHeadCols], uint8_t* scr,
                                             int trow) const {
-    float* o = reinterpret_cast<float*>(scr) + trow * (kHeadCols + 1);
+    float* o = reinterpret_cast<float*>(scr) + trow * kLd;
     float val = *b_v;
 #pragma unroll
     for (int j = 0; j < kHeadCols; ++j) {
       if (j < A) o[j] = v[j] + __ldg(b_pi + j);
       else if (j == A) val += v[j];
     }
-    if (row < M) {
-      if (value) value[row] = val;
-      sample_row(o, nullptr, BT_HEAD_CATEGORICAL, A, row, noise, temperature, action, log_prob);
-    }
+    if (row < M && value) value[row] = val;
+  }
+  // after apply_row on every row of the tile (rows m0 .. m0 + 127): epilogue warp ew of 8
+  __device__ __forceinline__ void coop(uint8_t* scr, int m0, int M, int ew, int lane) const {
+    const float* rows_s = reinterpret_cast<const float*>(scr);
+    double* es = reinterpret_cast<double*>(scr + BM * kLd * sizeof(float) + 1024) + ew * 64;
+    for (int r = ew; r < BM && m0 + r < M; r += kEpiWarps)
+      sample_row_warp(rows_s + r * kLd, nullptr, BT_HEAD_CATEGORICAL, A, m0 + r, noise,
+                      temperature, action, log_prob, es, lane);
   }
 };
 

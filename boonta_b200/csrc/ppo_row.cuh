@@ -134,4 +134,68 @@ __device__ inline void sample_row(const float* o, const float* scale, int head, 
   }
 }
 
+// sample_row for one row by a whole warp (every lane calls it; A <= 64): the categorical case
+// evaluates the per-action terms (the scaled logits, their exponentials, the Gumbel noise) on
+// lanes j and j + 32 in parallel, adds the exponentials in index order on lane 0 (the order of
+// sample_row) and picks the first maximal index with a warp reduction, so the action and the
+// log-prob are bit-identical to sample_row's (for non-NaN outputs). `es`: 64 doubles of the
+// warp's scratch. Other
+// heads and temperature 0 fall back to sample_row on lane 0.
+__device__ inline void sample_row_warp(const float* o, const float* scale, int head, int A, int r,
+                                       const float* noise, float temperature, void* action,
+                                       float* log_prob, double* es, int lane) {
+  if (head != BT_HEAD_CATEGORICAL || !(temperature > 0.f) || A > 64) {
+    if (lane == 0) sample_row(o, scale, head, A, r, noise, temperature, action, log_prob);
+    return;
+  }
+  const int j0 = lane, j1 = lane + 32;
+  const double x0 = j0 < A ? (double)(o[j0] / temperature) : -INFINITY;
+  const double x1 = j1 < A ? (double)(o[j1] / temperature) : -INFINITY;
+  double mx = fmax(x0, x1);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+  if (j0 < A) es[j0] = exp(x0 - mx);
+  if (j1 < A) es[j1] = exp(x1 - mx);
+  __syncwarp();
+  double lse = 0.0;
+  if (lane == 0) {
+    double se = 0.0;
+    for (int j = 0; j < A; ++j) se += es[j];
+    lse = log(se) + mx;
+  }
+  lse = __shfl_sync(0xffffffffu, lse, 0);
+  float v0 = -INFINITY, v1 = -INFINITY;
+  if (j0 < A) {
+    v0 = (float)(x0 - lse);
+    if (noise) v0 = v0 + (float)(-log(-log((double)noise[(size_t)r * A + j0])));
+  }
+  if (j1 < A) {
+    v1 = (float)(x1 - lse);
+    if (noise) v1 = v1 + (float)(-log(-log((double)noise[(size_t)r * A + j1])));
+  }
+  // first maximal index (sample_row's `v > best_v || j == 0` scan)
+  float bv = v0;
+  int bj = j0;
+  if (v1 > v0) {
+    bv = v1;
+    bj = j1;
+  }
+  if (j0 >= A) bj = 1 << 30;
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+    const int oj = __shfl_xor_sync(0xffffffffu, bj, d);
+    if (ov > bv || (ov == bv && oj < bj)) {
+      bv = ov;
+      bj = oj;
+    }
+  }
+  if (bj >= A) bj = 0;  // every value -inf or NaN: sample_row keeps index 0
+  __syncwarp();
+  if (lane == 0) {
+    reinterpret_cast<int*>(action)[r] = bj;
+    log_prob[r] = (float)((double)(o[bj] / temperature) - lse);
+  }
+}
+
 }  // namespace bt

@@ -242,8 +242,11 @@ def test_full_size_update_one_epoch(name):
     other = [i for i in range(stats.shape[-1]) if i != clip]
     if w.precision == "bf16":
         # each statistic within the bf16 noise: BF16_NOISE times the float32 oracle's own
-        # distance from the float64 one, plus 2e-3 (the clip fraction: 1 % of the rows)
-        noise = np.abs(ostats32 - ostats)
+        # distance from the float64 one, plus 2e-3 (the clip fraction: 1 % of the rows). The
+        # distance at one minibatch is a single draw of a trajectory's divergence (the float32
+        # oracle's value mean moves 5e-4 at one minibatch and 5e-3 at another), so each
+        # statistic's noise scale is its largest distance over the epoch.
+        noise = np.abs(ostats32 - ostats).max(axis=(0, 1), keepdims=True)
         dev = np.abs(stats - ostats)
         allowed = BF16_NOISE * noise + 2e-3
         allowed[..., clip] = BF16_NOISE * noise[..., clip] + 1e-2
