@@ -26,7 +26,8 @@ constexpr int kHeadCols = 64;  // packed head outputs (A actor outputs + the val
 // thread = row first parks the row's 64 accumulators plus biases in shared memory (rows of
 // kLd floats); then the 256 threads of the eight epilogue warps take the tile's 128 rows, two
 // adjacent lanes per row, each on 32 of the outputs: max, softmax sum, entropy and log-prob
-// combined across the pair by one shuffle (the same value on both), the PPO loss terms, D =
+// combined across the pair by one shuffle (the same value on both; one exponential per output,
+// the probabilities as exp(z_j) / sum), the PPO loss terms, D =
 // dL/dO stored as split bf16 pairs (16-byte stores), and the statistics summed over the warp
 // by a fixed shuffle tree and over the eight warps in order (deterministic).
 struct EpiHeadsLoss {
@@ -87,20 +88,23 @@ struct EpiHeadsLoss {
       mx = fmaxf(mx, x[j]);
     }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    float e[32];  // exp(z_j), each evaluated once
     float se = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       x[j] = x[j] - mx;  // z_j
-      se += jb + j < A ? expf(x[j]) : 0.f;
+      e[j] = jb + j < A ? expf(x[j]) : 0.f;
+      se += e[j];
     }
     se = se + __shfl_xor_sync(0xffffffffu, se, 1);  // the pair's two halves, same sum on both
-    const float lse = logf(se);
+    const float lse = logf(se), inv_se = 1.f / se;
     float ent = 0.f, mine = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
+      e[j] *= inv_se;  // p_j
       if (jb + j < A) {
         const float l = x[j] - lse;
-        ent -= expf(l) * l;
+        ent -= e[j] * l;
         if (jb + j == act) mine = l;
       }
     }
@@ -119,17 +123,17 @@ struct EpiHeadsLoss {
         for (int i = 0; i < 4; ++i) {
           float g[2];
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int j = jb + 8 * q + 2 * i + e;
+          for (int k = 0; k < 2; ++k) {
+            const int j = jb + 8 * q + 2 * i + k;
             float gj = 0.f;
             if (j == A) {
               gj = rl.d_value;
             } else if (on && j < A) {
-              const float l = x[8 * q + 2 * i + e] - lse;
-              const float p = expf(l);
+              const float l = x[8 * q + 2 * i + k] - lse;
+              const float p = e[8 * q + 2 * i + k];
               gj = rl.g_lp * (((j == act) ? 1.f : 0.f) - p) + g_ent * (-p * (l + ent));
             }
-            g[e] = gj;
+            g[k] = gj;
           }
           const __nv_bfloat162 hp = __floats2bfloat162_rn(g[0], g[1]);
           const __nv_bfloat162 lq = __floats2bfloat162_rn(g[0] - __low2float(hp),

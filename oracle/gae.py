@@ -44,3 +44,49 @@ def gae(reward, terminated, truncated, values, bootstrap, gamma, gae_lambda,
         advantages[t] = advantage
         next_value = values[t]
     return advantages, advantages + values
+
+
+CHUNKS = 8
+
+
+def gae_chunked(reward, terminated, truncated, values, bootstrap, gamma, gae_lambda,
+                rho=None, c=None):
+    """float32 GAE in the CUDA kernel's order (boonta_b200/csrc/gae.cu, gae_chunked_kernel):
+    the same per-step terms delta_t, k_t (A_t = delta_t + k_t A_{t+1}), the T steps in 8 chunks
+    of ceil(T / 8), each chunk folded from its last step into the map A = M * A_entering + C
+    from a zero carry, the maps of the later chunks composed onto the zero advantage past the
+    last step, then each chunk rescanned. Every product and sum rounded to float32."""
+    f = np.float32
+    reward = np.asarray(reward, f)
+    values = np.asarray(values, f)
+    bootstrap = np.asarray(bootstrap, f)
+    term = (1.0 - np.asarray(terminated, f)).astype(f)
+    trunc = (1.0 - np.asarray(truncated, f)).astype(f)
+    rho = np.ones_like(values) if rho is None else np.asarray(rho, f)
+    c = np.ones_like(values) if c is None else np.asarray(c, f)
+    g = f(gamma)
+    gl = f(float(gamma) * float(gae_lambda))
+    T = values.shape[0]
+    nxt = np.concatenate([values[1:], bootstrap[None]], axis=0) if T else values
+    delta = (rho * (reward + g * term * nxt - values)) * trunc
+    k = gl * c * term * trunc
+    L = -(-T // CHUNKS) if T else 0
+    spans = [(min(T, w * L), min(T, w * L + L)) for w in range(CHUNKS)]
+    maps = []
+    for t0, t1 in spans:
+        M = np.ones_like(bootstrap)
+        C = np.zeros_like(bootstrap)
+        for t in range(t1 - 1, t0 - 1, -1):
+            C = (delta[t] + k[t] * C).astype(f)
+            M = (k[t] * M).astype(f)
+        maps.append((M, C))
+    adv_out = np.zeros_like(values)
+    for w, (t0, t1) in enumerate(spans):
+        a = np.zeros_like(bootstrap)
+        for cc in range(CHUNKS - 1, w, -1):
+            M, C = maps[cc]
+            a = (M * a + C).astype(f)
+        for t in range(t1 - 1, t0 - 1, -1):
+            a = (delta[t] + k[t] * a).astype(f)
+            adv_out[t] = a
+    return adv_out, (adv_out + values).astype(f)

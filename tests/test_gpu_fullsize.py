@@ -128,8 +128,9 @@ def test_full_size_targets(name):
     # the scan itself, on the learner's own bootstrap values
     oadv, oret = ogae.gae(roll["reward"], roll["terminated"], roll["truncated"], roll["value"],
                           boot, w.ppo.gamma, w.ppo.gae_lambda)
-    np.testing.assert_allclose(adv, oadv, rtol=1e-5, atol=1e-6)
-    np.testing.assert_allclose(ret, oret, rtol=1e-5, atol=1e-6)
+    scale = max(1.0, float(np.abs(oadv).max()))  # the chunked scan's rounding scale
+    np.testing.assert_allclose(adv, oadv, rtol=1e-5, atol=1e-6 * scale)
+    np.testing.assert_allclose(ret, oret, rtol=1e-5, atol=1e-6 * scale)
 
 
 def _flat_minibatch(w, rows, seed):

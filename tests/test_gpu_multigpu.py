@@ -1,6 +1,8 @@
-"""Multi-GPU learner (NCCL all-reduce per minibatch) on 2 GPUs, one process per GPU: the
-ranks end bitwise identical and equal to the single-process oracle update of the global
-batch (global permutation, boonta/algorithms/ppo.py:200). Skipped with fewer than 2 GPUs."""
+"""Multi-GPU learner on 2 GPUs (BT_TEST_WORLD=N for another rank count), one process per GPU:
+the NVLink peer-memory gradient exchange fused with the optimizer step (and, for one case, the
+NCCL all-reduce path); the ranks end bitwise identical and equal to the single-process oracle
+update of the global batch (global permutation, boonta/algorithms/ppo.py:200). Skipped with
+fewer GPUs than ranks."""
 import dataclasses
 import os
 
@@ -12,7 +14,7 @@ from boonta_b200.spec import init_params
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+WORLD = int(os.environ.get("BT_TEST_WORLD", "2"))
 
 
 def _workload(kind):
