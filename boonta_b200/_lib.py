@@ -40,7 +40,8 @@ EXPORTS = (
     "bt_clip_adam_noalloc", "bt_learner_use_graphs", "bt_learner_check",
     "bt_selftest_bounded_wait", "bt_learner_load_state", "bt_learner_store_state",
     "bt_learner_use_p2p", "bt_learner_exchange_probe", "bt_linear_scan",
-    "bt_linear_scan_backward",
+    "bt_linear_scan_backward", "bt_threefry2x32_host", "bt_threefry2x32", "bt_random_split",
+    "bt_random_fill", "bt_random_permutation_workspace", "bt_random_permutation",
 )
 
 
@@ -115,6 +116,14 @@ def lib() -> C.CDLL:
         "bt_version": (C.c_char_p, []),
         "bt_gae": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f64, f64, vp, vp, vp]),
         "bt_linear_scan": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+        "bt_threefry2x32_host": (None, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                        C.POINTER(C.c_uint32)]),
+        "bt_threefry2x32": (C.c_int, [C.c_uint32, C.c_uint32, vp, vp, vp, vp, i64, vp]),
+        "bt_random_split": (C.c_int, [C.POINTER(C.c_uint32), i32, i32, C.POINTER(C.c_uint32)]),
+        "bt_random_fill": (C.c_int, [C.POINTER(C.c_uint32), i64, i32, C.c_float, C.c_float, i32,
+                                     vp, vp]),
+        "bt_random_permutation_workspace": (i64, [i64]),
+        "bt_random_permutation": (C.c_int, [C.POINTER(C.c_uint32), i64, i32, vp, vp, i64, vp]),
         "bt_linear_scan_backward": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
                                               i32, vp]),
         "bt_learner_create": (C.c_int, [C.POINTER(LearnerConfig), C.POINTER(vp)]),

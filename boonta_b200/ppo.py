@@ -14,9 +14,11 @@ MLP / conv / GRU families the learner implements) instead of a flax module, `opt
 is an `OptimizerConfig` describing optax.chain(clip_by_global_norm, adam) instead of an
 optax object, and arrays are torch CUDA tensors. `PPOState.params` is the flat parameter
 buffer (layout `spec.param_layout`), `optimizer_state` an `AdamState(mu, nu, count)`.
-Keys are integer seeds: the permutations (ppo.py:200) and sampling draws (ppo.py:68) come
-from device-side torch generators seeded by them, not from jax.random (the learner itself is
-bit-exact given the same permutations and draws). Anything the learner does not
+Keys are threefry keys (two uint32 words, as jax.random.key_data returns; an integer seed is
+taken as jax.random.PRNGKey(seed)): the permutations (ppo.py:200, 230) and the sampling draws
+(ppo.py:68, distributions.py:21-23) are drawn from them on the device in jax.random's
+conventions (boonta_b200.random; csrc/random.cu). Parameter initialisation (init) stays a
+seeded host draw. Anything the learner does not
 implement (auxiliary losses, another advantage estimator, other network modules) raises
 NotImplementedError. Every update and act step runs in the CUDA library; there is no CPU
 path.
@@ -28,6 +30,7 @@ from typing import Any, Callable
 
 import torch
 
+from . import random as trandom
 from .spec import NetworkSpec, OptimizerConfig, PPOConfig, init_params, param_layout
 
 RecurrentPPOConfig = PPOConfig  # recurrent_ppo.py:18-28 has the same fields and defaults
@@ -110,6 +113,16 @@ def generalized_advantage_estimator(transitions: Transition, values, bootstrap, 
 
 def _u8(x):
     return (x if x.dtype == torch.uint8 else x.to(torch.uint8)).contiguous()
+
+
+def _act_noise(key, network, n: int, device) -> torch.Tensor:
+    """The draws behind the act step's sample, from the step key on the device: the uniforms
+    of jax.random.gumbel (minval = the smallest normal float32) for a categorical head
+    (distributions.py:21-23), standard normals for a gaussian one, [n, action_dim]."""
+    a = network.action_dim
+    if network.head == "categorical":
+        return trandom.uniform(key, (n, a), torch.finfo(torch.float32).tiny, 1.0, device)
+    return trandom.normal(key, (n, a), device)
 
 
 def _seed(key) -> int:
@@ -208,13 +221,7 @@ class PPO:
         n = obs.shape[0]
         lrn = self._act_learner(n)
         self._load(lrn, state)
-        g = torch.Generator(device=obs.device).manual_seed(_seed(key))
-        a = self.network.action_dim
-        if self.network.head == "categorical":
-            tiny = torch.finfo(torch.float32).tiny
-            noise = torch.rand((n, a), generator=g, device=obs.device).clamp_(min=tiny)
-        else:
-            noise = torch.randn((n, a), generator=g, device=obs.device)
+        noise = _act_noise(key, self.network, n, obs.device)
         action, log_prob, value = lrn.act(obs, noise, temperature)
         return state, carry, action, {"log_prob": log_prob, "value": value}
 
@@ -225,10 +232,11 @@ class PPO:
         return self._learner(1, n)
 
     def _permutations(self, key, batch: int, device) -> torch.Tensor:
-        """One permutation of the batch per epoch (ppo.py:199-203), drawn on the device."""
-        g = torch.Generator(device=device).manual_seed(_seed(key))
-        return torch.stack([torch.randperm(batch, generator=g, device=device, dtype=torch.int32)
-                            for _ in range(self.cfg.update_epochs)])
+        """One permutation of the batch per epoch, drawn on the device from the update key as
+        the reference does: keys = split(key, update_epochs), permutation(keys[e], batch)
+        (ppo.py:199-203, 230)."""
+        keys = trandom.split(key, self.cfg.update_epochs)
+        return torch.stack([trandom.permutation(k, batch, device) for k in keys])
 
     def _batch(self, transitions: Transition) -> dict:
         f, s, aux = transitions.first, transitions.second, transitions.aux
@@ -299,13 +307,7 @@ class RecurrentPPO(PPO):
         for flag in (timestep.terminated, timestep.truncated):
             if flag is not None:
                 reset |= torch.as_tensor(flag, device=obs.device).reshape(n).to(torch.uint8)
-        g = torch.Generator(device=obs.device).manual_seed(_seed(key))
-        a = self.network.action_dim
-        if self.network.head == "categorical":
-            tiny = torch.finfo(torch.float32).tiny
-            noise = torch.rand((n, a), generator=g, device=obs.device).clamp_(min=tiny)
-        else:
-            noise = torch.randn((n, a), generator=g, device=obs.device)
+        noise = _act_noise(key, self.network, n, obs.device)
         action, log_prob, value, new_carry = lrn.act_recurrent(obs, reset, carry, noise,
                                                                temperature)
         return state, new_carry, action, {"log_prob": log_prob, "value": value}

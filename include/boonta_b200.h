@@ -29,6 +29,8 @@
  *   bt_linear_scan /
  *   bt_linear_scan_backward boonta/networks/kernels/scan.py:13-89 (the SSM torso's linear
  *                           recurrence and its custom VJP; the Pallas Mosaic-GPU kernel)
+ *   bt_random_*             jax.random's threefry key operations behind ppo.py:200, 230
+ *                           (permutation, split) and distributions.py:21-23 (uniform draws)
  *   bt_learner_comm_init    the NCCL communicator behind jax.distributed / XLA's
  *                           all-reduce (hangar/train.py:17-18, anakin.py:165-186)
  *
@@ -173,6 +175,28 @@ BT_API int bt_linear_scan_backward(const void* a, const void* h, const void* ini
                             const void* cotangent, void* da, void* db, void* dinit,
                             int32_t batch, int32_t steps, int32_t features, int32_t dtype,
                             int32_t init_dtype, void* stream);
+
+/* ---- counter-based random numbers in JAX's threefry conventions ---------------------------
+ * (jax.random with threefry2x32 keys; boonta/algorithms/ppo.py:200, 230,
+ * boonta/networks/distributions.py:21-23). Keys are two uint32 words (jax.random.key_data);
+ * `partitionable` selects JAX's counter layout (1: jax_threefry_partitionable, the default of
+ * current JAX; 0: the original layout).
+ *   bt_threefry2x32_host / bt_threefry2x32: the raw block cipher (Random123 threefry2x32-20) on
+ *     one counter pair (host) or n pairs (device arrays).
+ *   bt_random_split: jax.random.split(key, num) on the host: out[2*i], out[2*i+1].
+ *   bt_random_fill: n values of jax.random.bits (kind 0, uint32), uniform(minval, maxval)
+ *     (kind 1, float32) or normal (kind 2, float32) into device memory.
+ *   bt_random_permutation: jax.random.permutation(key, n) as int32 (device), with a device
+ *     workspace of bt_random_permutation_workspace(n) bytes (-1: n unsupported). */
+BT_API void bt_threefry2x32_host(uint32_t k0, uint32_t k1, uint32_t c0, uint32_t c1, uint32_t* y);
+BT_API int bt_threefry2x32(uint32_t k0, uint32_t k1, const uint32_t* c0, const uint32_t* c1,
+                    uint32_t* y0, uint32_t* y1, int64_t n, void* stream);
+BT_API int bt_random_split(const uint32_t* key, int32_t num, int32_t partitionable, uint32_t* out);
+BT_API int bt_random_fill(const uint32_t* key, int64_t n, int32_t kind, float minval,
+                   float maxval, int32_t partitionable, void* out, void* stream);
+BT_API int64_t bt_random_permutation_workspace(int64_t n);
+BT_API int bt_random_permutation(const uint32_t* key, int64_t n, int32_t partitionable,
+                          int32_t* out, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---- learner ---------------------------------------------------------------------------- */
 BT_API int bt_learner_create(const bt_learner_config* cfg, bt_learner** out);
