@@ -182,8 +182,9 @@ extern "C" int64_t bt_random_permutation_workspace(int64_t n) {
 extern "C" int bt_random_permutation(const uint32_t* key, int64_t n, int32_t partitionable,
                                      int32_t* out, void* workspace, int64_t workspace_bytes,
                                      void* stream) {
-  BT_CHECK_ARG(key && out && n >= 0 && n <= INT32_MAX, "bt_random_permutation: bad argument");
+  BT_CHECK_ARG(key && n >= 0 && n <= INT32_MAX, "bt_random_permutation: bad argument");
   if (n == 0) return BT_OK;
+  BT_CHECK_ARG(out, "bt_random_permutation: null output");
   const cudaStream_t s = (cudaStream_t)stream;
   const int rounds = bt::permutation_rounds(n);
   bt::iota_kernel<<<bt::fill_grid(n), 256, 0, s>>>(out, n);
