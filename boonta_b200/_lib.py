@@ -42,6 +42,7 @@ EXPORTS = (
     "bt_learner_use_p2p", "bt_learner_exchange_probe", "bt_linear_scan",
     "bt_linear_scan_backward", "bt_threefry2x32_host", "bt_threefry2x32", "bt_random_split",
     "bt_random_fill", "bt_random_permutation_workspace", "bt_random_permutation",
+    "bt_selftest_gru_barrier",
 )
 
 
@@ -116,6 +117,7 @@ def lib() -> C.CDLL:
         "bt_version": (C.c_char_p, []),
         "bt_gae": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, i32, i32, f64, f64, vp, vp, vp]),
         "bt_linear_scan": (C.c_int, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
+        "bt_selftest_gru_barrier": (C.c_int, [i32, vp]),
         "bt_threefry2x32_host": (None, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                         C.POINTER(C.c_uint32)]),
         "bt_threefry2x32": (C.c_int, [C.c_uint32, C.c_uint32, vp, vp, vp, vp, i64, vp]),

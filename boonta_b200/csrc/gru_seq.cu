@@ -24,10 +24,13 @@
 //
 // The barrier: thread 0 of every CTA adds one to a device counter (zeroed before the launch)
 // and spins until it reaches (step + 1) * CTAs. All CTAs must be resident at once: the host
-// launches at most one CTA per SM with an occupancy check, and the spin is bounded (2 s of
-// %globaltimer), after which the CTA records kErrGruBarrier in the learner's error word
-// and leaves; the others then time out at their next barrier.
+// launches at most one CTA per SM with an occupancy check, the recurrent path issues all its
+// kernels on the caller's stream (no side stream of the learner runs beside these), and the spin
+// is bounded (2 s of %globaltimer), after which the CTA records kErrGruBarrier in the learner's
+// error word and leaves; the others then time out at their next barrier
+// (bt_selftest_gru_barrier makes every barrier give up, on purpose).
 #include "common.cuh"
+#include "gru_seq.cuh"
 #include "kernels.cuh"
 #include "mma_sync.cuh"
 #include "ptx.cuh"
@@ -37,27 +40,6 @@ namespace bt {
 constexpr int kGruSeqThreads = 256;
 constexpr int kGruSeqEnvs = 32;   // envs per CTA
 constexpr int kGruSeqUnits = 16;  // hidden units per CTA
-constexpr int kErrGruBarrier = 21;
-
-struct GruSeqParams {
-  int T, H, envs;
-  const int* env_count;  // nullable: live envs
-  const float* xp;       // [envs * T, 3H] input projections (+ input bias)
-  const float* wh;       // [H, 3H]
-  const float* bhn;      // [H]
-  const uint8_t* reset;  // [envs * T] (row = env * T + t)
-  float* hin;            // [envs * T, H] carry entering each step
-  float* h;              // [envs * T, H] outputs
-  float* gr;
-  float* gz;
-  float* gn;
-  float* ghn;
-  const float* dhs;  // [envs * T, H] dL/dh_t from the heads (backward)
-  float* dxp;        // [envs * T, 3H] (backward)
-  float* dhp;        // [envs * T, 3H] (backward)
-  unsigned int* bar;  // zeroed before the launch
-  int* err;
-};
 
 // Grid-wide step barrier; returns false (after recording the failure) if it gave up.
 __device__ __forceinline__ bool gru_grid_barrier(const GruSeqParams& p, unsigned int target,
@@ -70,8 +52,8 @@ __device__ __forceinline__ bool gru_grid_barrier(const GruSeqParams& p, unsigned
     while (true) {
       unsigned int v;
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.bar) : "memory");
-      if (v >= target) break;
-      if (global_timer_ns() - t0 > 2000000000ull) {
+      if (v >= target + p.bar_offset) break;
+      if (global_timer_ns() - t0 > (p.limit_ns ? p.limit_ns : 2000000000ull)) {
         *s_fail = 1;
         if (p.err) atomicExch(p.err, kErrGruBarrier);
         break;
@@ -356,3 +338,55 @@ int launch_gru_seq_backward(const GruSeqParams& p, cudaStream_t s) {
 }
 
 }  // namespace bt
+
+extern "C" int bt_selftest_gru_barrier(int32_t limit_us, void* stream) {
+  using namespace bt;
+  BT_CHECK_ARG(limit_us > 0 && limit_us <= 2000000, "limit %d us outside (0, 2 s]", limit_us);
+  cudaStream_t s = (cudaStream_t)stream;
+  // a 2-step sequence of 32 envs x 64 units (4 CTAs) on zeroed buffers, with every barrier
+  // target one above what the grid can reach
+  constexpr int kH = 64, kEnvs = 32, kT = 2;
+  const size_t rows = (size_t)kEnvs * kT;
+  const size_t floats = rows * 3 * kH * 3 + rows * kH * 8 + (size_t)kH * 3 * kH + kH;
+  float* buf = nullptr;
+  BT_CUDA(cudaMallocAsync(&buf, floats * sizeof(float) + rows + 64, s));
+  BT_CUDA(cudaMemsetAsync(buf, 0, floats * sizeof(float) + rows + 64, s));
+  float* f = buf;
+  auto take = [&](size_t n) { float* q = f; f += n; return q; };
+  GruSeqParams p{};
+  p.T = kT;
+  p.H = kH;
+  p.envs = kEnvs;
+  p.xp = take(rows * 3 * kH);
+  p.dxp = take(rows * 3 * kH);
+  p.dhp = take(rows * 3 * kH);
+  p.hin = take(rows * kH);
+  p.h = take(rows * kH);
+  p.gr = take(rows * kH);
+  p.gz = take(rows * kH);
+  p.gn = take(rows * kH);
+  p.ghn = take(rows * kH);
+  p.dhs = take(rows * kH);
+  p.wh = take((size_t)kH * 3 * kH);
+  p.bhn = take(kH);
+  take(rows * kH);
+  uint8_t* tail = reinterpret_cast<uint8_t*>(f);
+  p.reset = tail;
+  p.bar = reinterpret_cast<unsigned int*>(tail + ((rows + 15) / 16) * 16);
+  p.err = reinterpret_cast<int*>(p.bar + 4);
+  p.limit_ns = (unsigned long long)limit_us * 1000ull;
+  p.bar_offset = 1;
+  bool ok = false;
+  BT_TRY(gru_seq_supported(kEnvs, kH, &ok));
+  BT_CHECK_ARG(ok, "gru sequence kernel does not fit this device");
+  BT_TRY(launch_gru_seq_forward(p, s));
+  int code = 0;
+  BT_CUDA(cudaMemcpyAsync(&code, p.err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  BT_CUDA(cudaFreeAsync(buf, s));
+  BT_CUDA(cudaStreamSynchronize(s));
+  if (code == kErrGruBarrier) {
+    set_error("gru step barrier gave up after %d us (the expected outcome)", limit_us);
+    return BT_ERR_TIMEOUT;
+  }
+  return code ? BT_ERR_CUDA : BT_OK;
+}

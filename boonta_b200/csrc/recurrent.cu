@@ -20,35 +20,13 @@
 #include <algorithm>
 
 #include "gemm_simt.cuh"
+#include "gru_seq.cuh"
 #include "learner.h"
 
 namespace bt {
 
 int comm_allreduce_f64(Comm* c, double* buf, size_t n, cudaStream_t stream);
 
-// gru_seq.cu
-struct GruSeqParams {
-  int T, H, envs;
-  const int* env_count;
-  const float* xp;
-  const float* wh;
-  const float* bhn;
-  const uint8_t* reset;
-  float* hin;
-  float* h;
-  float* gr;
-  float* gz;
-  float* gn;
-  float* ghn;
-  const float* dhs;
-  float* dxp;
-  float* dhp;
-  unsigned int* bar;
-  int* err;
-};
-int gru_seq_supported(int envs, int H, bool* ok);
-int launch_gru_seq_forward(const GruSeqParams& p, cudaStream_t s);
-int launch_gru_seq_backward(const GruSeqParams& p, cudaStream_t s);
 
 namespace {
 

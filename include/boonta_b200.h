@@ -242,6 +242,10 @@ BT_API int bt_learner_check(bt_learner* learner, void* stream);
  * the failure; returns BT_ERR_TIMEOUT when it did (the expected result) with the context still
  * usable. No counterpart in the reference. */
 BT_API int bt_selftest_bounded_wait(int32_t limit_us, void* stream);
+/* The GRU sequence kernels' grid-wide step barrier with an unreachable target and the given
+ * limit (microseconds, at most 2 s): returns BT_ERR_TIMEOUT when every CTA gave up, as designed.
+ * Synchronises the stream. */
+BT_API int bt_selftest_gru_barrier(int32_t limit_us, void* stream);
 
 /* CUDA-graph replay of bt_learner_update (on by default; no counterpart in the reference,
  * where XLA compiles the update into one program). The first update with a given set of
