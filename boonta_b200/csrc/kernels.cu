@@ -913,6 +913,37 @@ __global__ void gather_bf16_kernel(const float* obs, const int* idx, int rows, i
   }
 }
 
+// fp32 rows [rows, d] (row stride d) as split bf16 pairs [rows, d]: rows below the live count
+// converted, rows from it to the next 64-row boundary zero (the tensor-core dW GEMMs read whole
+// 64-row blocks). One warp per row.
+__global__ void split_rows_bf16_kernel(const float* src, int rows, int d, __nv_bfloat16* out,
+                                       __nv_bfloat16* out_lo, const int* count) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
+  const int live = live_rows(count, rows);
+  if (row >= dz_rows_end(live, rows)) return;
+  const bool on = row < live;
+  const float* r = src + (size_t)row * d;
+  if ((d & 3) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    for (int q = lane; q < d / 4; q += 32)
+      store_bf16x4(out, out_lo, (size_t)row * d + 4 * q,
+                   on ? __ldg(r4 + q) : make_float4(0.f, 0.f, 0.f, 0.f));
+  } else {
+    for (int k = lane; k < d; k += 32) store_bf16(out, out_lo, (size_t)row * d + k, on ? r[k] : 0.f);
+  }
+}
+
+int launch_split_rows_bf16(const float* src, int rows, int d, __nv_bfloat16* out,
+                           __nv_bfloat16* out_lo, const int* count, cudaStream_t stream) {
+  if (rows <= 0) return BT_OK;
+  BT_CUDA(launch_pdl(split_rows_bf16_kernel, dim3(ceil_div(rows * 32, 256)), dim3(256), 0,
+                     stream, src, rows, d, out, out_lo, count));
+  return BT_OK;
+}
+
 // Rows idx[r] of a bf16 table [*, ld] (ld a multiple of 8) copied to out [rows, ld], one warp
 // per row in 16-byte chunks; rows past the live count are left as they are.
 __global__ void gather_rows_bf16_kernel(const __nv_bfloat16* src, const int* idx, int rows,

@@ -194,6 +194,7 @@ int pick_splits(int M, int N, int K) {
 }  // namespace
 
 int allocate_tensor_core(bt_learner* L);
+int allocate_gru_tc(bt_learner* L);
 
 int allocate(bt_learner* L) {
   const bt_learner_config& c = L->cfg;
@@ -363,7 +364,8 @@ int allocate(bt_learner* L) {
     BT_TRY(dalloc(L, &L->local_idx, (size_t)E * M * L->units_cap));
     BT_TRY(dalloc(L, &L->local_counts, (size_t)E * M));
   }
-  return allocate_tensor_core(L);
+  BT_TRY(allocate_tensor_core(L));
+  return allocate_gru_tc(L);
 }
 
 // ---- tensor-core (bf16) operand buffers and TMA tensor maps -------------------------------

@@ -74,6 +74,16 @@ struct LayerPlan {
   float* wh_part = nullptr;
   float* bhn_part = nullptr;
   int wi_splits = 1, wh_splits = 1, bhn_splits = 1;
+  // GRU projections on the tcgen05 GEMM in split bf16 (tc_proj): the input x, the carries and
+  // the projection gradients as split bf16 pairs, the maps of the four GEMMs
+  bool tc_proj = false;
+  int ldxg = 0, wi_kbps = 1, wh_kbps = 1;
+  __nv_bfloat16 *xb = nullptr, *xb_lo = nullptr;      // [rows, ldxg], ones column at kin
+  __nv_bfloat16 *hinb = nullptr, *hinb_lo = nullptr;  // [rows, H]
+  __nv_bfloat16 *dxpb = nullptr, *dxpb_lo = nullptr;  // [rows, 3H]
+  __nv_bfloat16 *dhpb = nullptr, *dhpb_lo = nullptr;  // [rows, 3H]
+  bt::umma::Operands proj_ops{}, wi_ops{}, wh_ops{}, gdx_ops{};
+  CUtensorMap map_xp;
   const float* pre() const { return ln ? y : z; }
 };
 

@@ -188,7 +188,21 @@ int gru_forward(bt_learner* L, LayerPlan& g, const float* x, const float* carry,
                 const int* env_count, const int* rows_live, int envs, int T, cudaStream_t s) {
   const int H = g.hidden, rows = envs * T;
   // xp = [x, 1] [W_i; b_i]
-  {
+  if (g.tc_proj) {
+    BT_K(L, kProfMisc, s, launch_gather_bf16(x, nullptr, rows, g.kin, g.ldxg, g.xb, g.xb_lo,
+                                             rows_live, s));
+    umma::GemmShape sh{rows, 3 * H, g.kin, ceil_div(g.kin, umma::BK), rows_live, nullptr,
+                       L->err_d};
+    umma::EpiFwd ep;
+    ep.f32_map = g.map_xp;
+    ep.hi_map = g.map_xp;
+    ep.lo_map = g.map_xp;
+    ep.bias = L->params + g.wi_off + (size_t)g.kin * 3 * H;
+    ep.act = BT_ACT_NONE;
+    ep.has_f32 = true;
+    ep.has_hi = ep.has_lo = false;
+    BT_K(L, kProfGemmFwd, s, umma::launch_gemm<128, false, true, true>(g.proj_ops, sh, ep, 1, s));
+  } else {
     ARows a{x, nullptr, g.kin, g.kin};
     BRows b{L->params + g.wi_off, 3 * H, g.kin + 1};
     EpiForward ep{g.xp, nullptr, 3 * H, BT_ACT_NONE};
@@ -258,6 +272,44 @@ int gru_backward_steps(bt_learner* L, LayerPlan& g, const int* env_count, int en
 int gru_weight_grads(bt_learner* L, LayerPlan& g, LayerPlan& prev, const int* rows_live,
                      int rows, cudaStream_t s) {
   const int H = g.hidden;
+  if (g.tc_proj) {
+    // the projection gradients and the carries as split bf16 pairs (the x operand is still
+    // in place from the forward), then three tcgen05 GEMMs
+    const int H3 = 3 * H;
+    BT_K(L, kProfMisc, s, launch_split_rows_bf16(g.dxp, rows, H3, g.dxpb, g.dxpb_lo, rows_live, s));
+    BT_K(L, kProfMisc, s, launch_split_rows_bf16(g.dhp, rows, H3, g.dhpb, g.dhpb_lo, rows_live, s));
+    BT_K(L, kProfMisc, s, launch_split_rows_bf16(g.hin, rows, H, g.hinb, g.hinb_lo, rows_live, s));
+    {
+      umma::GemmShape sh{g.kin + 1, H3, rows, g.wi_kbps, nullptr, rows_live, L->err_d};
+      umma::EpiDw ep{g.wi_part, H3, (size_t)(g.kin + 1) * H3};
+      BT_K(L, kProfGemmDw, s, umma::launch_gemm<128, true, true, true>(g.wi_ops, sh, ep, g.wi_splits, s));
+    }
+    {
+      umma::GemmShape sh{H, H3, rows, g.wh_kbps, nullptr, rows_live, L->err_d};
+      umma::EpiDw ep{g.wh_part, H3, (size_t)H * H3};
+      BT_K(L, kProfGemmDw, s, umma::launch_gemm<128, true, true, true>(g.wh_ops, sh, ep, g.wh_splits, s));
+    }
+    {
+      ACols a{g.hin, nullptr, H, 0};  // ones row only: column sums of dhp's n part -> b_hn
+      BRows b{g.dhp + 2 * H, 3 * H, rows};
+      EpiPartial ep{g.bhn_part, H, (size_t)H};
+      BT_K(L, kProfGemmDw, s, launch_gemm_simt(a, b, ep, 1, H, rows, g.bhn_splits, s, nullptr,
+                                               rows_live));
+    }
+    {
+      umma::GemmShape sh{rows, g.kin, H3, ceil_div(H3, umma::BK), rows_live, nullptr, L->err_d};
+      umma::EpiDx epx;
+      epx.in_map = prev.map_pre;
+      epx.f32_map = prev.map_dpre;
+      epx.hi_map = prev.map_dpre;
+      epx.lo_map = prev.map_dpre;
+      epx.act = prev.act;
+      epx.has_f32 = true;
+      epx.has_hi = epx.has_lo = false;
+      BT_K(L, kProfGemmDx, s, umma::launch_gemm<128, false, false, true>(g.gdx_ops, sh, epx, 1, s));
+    }
+    return BT_OK;
+  }
   // weight gradients over all live rows
   {
     ACols a{prev.h, nullptr, g.kin, g.kin};  // [x, 1]^T dxp -> [W_i; b_i]
@@ -364,6 +416,25 @@ int allocate_gru(bt_learner* L, LayerPlan& g) {
   const int rows = L->rows_cap;
   g.wi_splits = pick_splits_k(g.kin + 1, 3 * H, rows);
   g.wh_splits = pick_splits_k(H, 3 * H, rows);
+  {
+    // the input projection, the GRU weight gradients and the dX into the previous (Dense)
+    // layer on the tcgen05 GEMM in split bf16, the recurrence's own arithmetic
+    std::vector<LayerPlan>& layers = L->towers[0].layers;
+    const LayerPlan* prev = layers.size() >= 2 ? &layers[layers.size() - 2] : nullptr;
+    g.tc_proj = prev && prev->kind == BT_LAYER_DENSE && !prev->tc && prev->kout == g.kin &&
+                g.kin % 32 == 0 && H % 64 == 0;
+    if (g.tc_proj) {
+      const int nkb = ceil_div(rows, umma::BK);
+      auto split_k = [&](int M, int* kbps, int* splits) {
+        const int tiles = ceil_div(M, umma::BM) * ceil_div(3 * H, 128);
+        const int sp = std::max(1, std::min(kNumSMs / tiles, nkb / 8));
+        *kbps = ceil_div(nkb, sp);
+        *splits = ceil_div(nkb, *kbps);
+      };
+      split_k(g.kin + 1, &g.wi_kbps, &g.wi_splits);
+      split_k(H, &g.wh_kbps, &g.wh_splits);
+    }
+  }
   g.bhn_splits = pick_splits_k(1, H, rows);
   BT_TRY(dalloc(L, &g.wi_part, (size_t)g.wi_splits * (g.kin + 1) * 3 * H));
   BT_TRY(dalloc(L, &g.wh_part, (size_t)g.wh_splits * H * 3 * H));
@@ -381,6 +452,62 @@ int allocate_gru(bt_learner* L, LayerPlan& g) {
   BT_TRY(dalloc(L, &L->rnn_reset, R));
   BT_TRY(dalloc(L, &L->rnn_rows, 1));
   BT_TRY(dalloc(L, &L->tail_obs, (size_t)2 * L->N * L->cfg.network.obs_dim));
+  return BT_OK;
+}
+
+// Buffers and tensor maps of the GRU's tensor-core projections (after the parameter layout and
+// the tensor-core path of the other layers are set up).
+int allocate_gru_tc(bt_learner* L) {
+  if (!L->recurrent) return BT_OK;
+  std::vector<LayerPlan>& layers = L->towers[0].layers;
+  LayerPlan& g = layers.back();
+  if (!g.tc_proj) return BT_OK;
+  LayerPlan& prev = layers[layers.size() - 2];
+  const int H = g.hidden, K = g.kin, H3 = 3 * H, R = L->act_rows;
+  auto pair = [&](__nv_bfloat16** hi, __nv_bfloat16** lo, size_t n) -> int {
+    BT_TRY(dalloc(L, hi, n));
+    BT_TRY(dalloc(L, lo, n));
+    BT_CUDA(cudaMemset(*hi, 0, n * 2));
+    BT_CUDA(cudaMemset(*lo, 0, n * 2));
+    return BT_OK;
+  };
+  // the bf16 shadow of the parameters (refreshed when an update starts, written by every Adam
+  // step) serves W_i
+  if (!L->params_b) BT_TRY(pair(&L->params_b, &L->params_b_lo, L->num_params));
+  g.ldxg = (K + 1 + 7) / 8 * 8;
+  BT_TRY(pair(&g.xb, &g.xb_lo, (size_t)R * g.ldxg));
+  BT_TRY(pair(&g.hinb, &g.hinb_lo, (size_t)R * H));
+  BT_TRY(pair(&g.dxpb, &g.dxpb_lo, (size_t)R * H3));
+  BT_TRY(pair(&g.dhpb, &g.dhpb_lo, (size_t)R * H3));
+  const uint64_t ldx = (uint64_t)g.ldxg * 2, l3 = (uint64_t)H3 * 2, lh = (uint64_t)H * 2;
+  for (int part = 0; part < 2; ++part) {
+    const __nv_bfloat16* w = (part ? L->params_b_lo : L->params_b) + g.wi_off;
+    const __nv_bfloat16* x = part ? g.xb_lo : g.xb;
+    const __nv_bfloat16* hin = part ? g.hinb_lo : g.hinb;
+    const __nv_bfloat16* dx = part ? g.dxpb_lo : g.dxpb;
+    const __nv_bfloat16* dh = part ? g.dhpb_lo : g.dhpb;
+    umma::Operands& pj = g.proj_ops;
+    umma::Operands& wi = g.wi_ops;
+    umma::Operands& wh = g.wh_ops;
+    umma::Operands& gx = g.gdx_ops;
+    // xp = x W_i (+ b_i in the epilogue): A = x (K-major over the K inputs), B = W_i ([K][3H])
+    BT_TRY(umma::encode_map(part ? &pj.a_lo : &pj.a, x, K, R, ldx, 64, 128));
+    BT_TRY(umma::encode_map(part ? &pj.b_lo : &pj.b, w, H3, K, l3, 64, 64));
+    // [W_i; b_i] gradient = [x, 1]^T dxp: both MN-major over the rows
+    BT_TRY(umma::encode_map(part ? &wi.a_lo : &wi.a, x, K + 1, R, ldx, 64, 64));
+    BT_TRY(umma::encode_map(part ? &wi.b_lo : &wi.b, dx, H3, R, l3, 64, 64));
+    // W_h gradient = hin^T dhp
+    BT_TRY(umma::encode_map(part ? &wh.a_lo : &wh.a, hin, H, R, lh, 64, 64));
+    BT_TRY(umma::encode_map(part ? &wh.b_lo : &wh.b, dh, H3, R, l3, 64, 64));
+    // dL/dx = dxp W_i^T: A = dxp (K-major over 3H), B = W_i as [N = K][K = 3H]
+    BT_TRY(umma::encode_map(part ? &gx.a_lo : &gx.a, dx, H3, R, l3, 64, 128));
+    BT_TRY(umma::encode_map(part ? &gx.b_lo : &gx.b, w, H3, K, l3, 64, 128));
+  }
+  BT_TRY(umma::encode_tile_map(&g.map_xp, g.xp, true, H3, R, (uint64_t)H3 * 4, 128));
+  const uint64_t lp4 = (uint64_t)prev.kout * 4;
+  BT_TRY(umma::encode_tile_map(&prev.map_pre, prev.pre(), true, prev.kout, R, lp4, 128));
+  BT_TRY(umma::encode_tile_map(&prev.map_dpre, prev.d_pre, true, prev.kout, R, lp4, 128));
+  BT_CUDA(cudaDeviceSynchronize());
   return BT_OK;
 }
 
