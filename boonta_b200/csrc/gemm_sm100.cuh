@@ -678,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           pending = false;
         }
         if (load_in && lane == 0) {
-          mbar_arrive_expect_tx(ibar, 32 * 32 * 4);
+          mbar_arrive_expect_tx(ibar, epi.in_bytes());
           tma_load_2d(wbuf, &epi.in_map, col0, row0, ibar);
         }
         float v[32];
@@ -768,6 +768,7 @@ struct EpiFwd {
   int act;
   bool has_f32, has_hi, has_lo;
   __device__ __forceinline__ bool uses_in() const { return false; }
+  __device__ __forceinline__ uint32_t in_bytes() const { return 0; }
   // v = acc + bias (zero for rows past the live count): the fp32 output z
   __device__ __forceinline__ void prep(float (&v)[32], const uint8_t*, int, int col0, bool live,
                                        int N) const {
@@ -799,8 +800,10 @@ struct EpiFwd {
 };
 
 // dX of a layer: g = acc * act'(pre) of the previous layer, from its pre-activation alone
-// (loaded as a TMA tile through in_map: fp32, box 32 x 32, 128-byte swizzle); stores g as
-// fp32 (LayerNorm previous layer, has_f32) or bf16 (hi/lo halves when has_lo).
+// (loaded as a TMA tile through in_map: fp32, box 32 x 32, 128-byte swizzle) or, for a ReLU
+// previous layer with in_bf16, from its bf16 output h (box 32 x 32, 64-byte swizzle: relu'(y) =
+// [h > 0]); stores g as fp32 (LayerNorm previous layer, has_f32) or bf16 (hi/lo halves when
+// has_lo).
 struct EpiDx {
   static constexpr bool kStaged = false;
   static constexpr bool kDeep = false;
@@ -810,23 +813,40 @@ struct EpiDx {
   CUtensorMap f32_map, hi_map, lo_map;
   int act;
   bool has_f32, has_hi, has_lo;
+  bool in_bf16 = false;
   __device__ __forceinline__ bool uses_in() const { return act != BT_ACT_NONE; }
+  __device__ __forceinline__ uint32_t in_bytes() const { return in_bf16 ? 32 * 32 * 2 : 32 * 32 * 4; }
   // g = acc * act'(pre) with pre from the input tile (zero for rows past the live count)
   __device__ __forceinline__ void prep(float (&v)[32], const uint8_t* in, int lane, int,
                                        bool live, int) const {
-    with_act(act, [&](auto tag) {
-      constexpr int A = decltype(tag)::value;
-      if constexpr (A != BT_ACT_NONE) {
+    if (in_bf16) {
+      // the row's four 16-byte chunks of 8 bf16 outputs, 64-byte swizzle (stage_row_bf16)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 p = load_row_f32(in, lane, j);
-          v[4 * j] *= act_dz<A>(p.x);
-          v[4 * j + 1] *= act_dz<A>(p.y);
-          v[4 * j + 2] *= act_dz<A>(p.z);
-          v[4 * j + 3] *= act_dz<A>(p.w);
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(in + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __nv_bfloat162 hp = *reinterpret_cast<const __nv_bfloat162*>(&ws[i]);
+          v[8 * j + 2 * i] *= act_dz_from_out<BT_ACT_RELU>(__low2float(hp));
+          v[8 * j + 2 * i + 1] *= act_dz_from_out<BT_ACT_RELU>(__high2float(hp));
         }
       }
-    });
+    } else {
+      with_act(act, [&](auto tag) {
+        constexpr int A = decltype(tag)::value;
+        if constexpr (A != BT_ACT_NONE) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 p = load_row_f32(in, lane, j);
+            v[4 * j] *= act_dz<A>(p.x);
+            v[4 * j + 1] *= act_dz<A>(p.y);
+            v[4 * j + 2] *= act_dz<A>(p.z);
+            v[4 * j + 3] *= act_dz<A>(p.w);
+          }
+        }
+      });
+    }
     if (!live) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = 0.f;

@@ -39,7 +39,7 @@ __global__ void ln_forward_kernel(const float* z, const float* sb, int rows, int
   with_act(act, [&](auto tag) {
     for (int k = lane; k < n; k += 32) {
       const float yv = (zr[k] - mean) * (r * sb[k]) + sb[n + k];
-      y[(size_t)row * n + k] = yv;
+      if (y) y[(size_t)row * n + k] = yv;
       const float hv = act_fwd<decltype(tag)::value>(yv);
       if (h) h[(size_t)row * n + k] = hv;
       if (hb) store_bf16(hb, hb_lo, (size_t)row * ldhb + k, hv);
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(256) ln_forward_vec_kernel(
       yv.y = (v[i].y - mean) * (r * a.y) + b.y;
       yv.z = (v[i].z - mean) * (r * a.z) + b.z;
       yv.w = (v[i].w - mean) * (r * a.w) + b.w;
-      reinterpret_cast<float4*>(y + (size_t)row * n)[q] = yv;
+      if (y) reinterpret_cast<float4*>(y + (size_t)row * n)[q] = yv;
       const float4 hv = make_float4(act_fwd<A>(yv.x), act_fwd<A>(yv.y), act_fwd<A>(yv.z),
                                     act_fwd<A>(yv.w));
       if (h) reinterpret_cast<float4*>(h + (size_t)row * n)[q] = hv;
@@ -362,8 +362,9 @@ void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out
   *count = n;
 }
 
-// Wide chunks: each thread sums the splits of 4 elements spaced by the block size, eight
-// splits at a time (32 independent loads in flight per thread), in split order.
+// Wide chunks (one or more 1024-element pieces): per piece, each thread sums the splits of 4
+// elements spaced by the block size, eight splits at a time (32 independent loads in flight
+// per thread), in split order.
 // Tall chunks (many splits, kTallChunk elements): warp w sums splits w, w + 8, ... of the
 // lane's element, then the eight warp sums are added in warp order.
 // Narrow segments (fewer elements than a warp has lanes per split pass, e.g. the per-block
@@ -417,41 +418,45 @@ __global__ void __launch_bounds__(256, 4) reduce_segments_kernel(const Segment* 
       sq = (double)s * (double)s;
     }
   } else {
+    // one kReduceChunk piece at a time (a block may own several consecutive pieces)
     constexpr int kPer = kReduceChunk / 256;
-    float acc[kPer];
+    for (int c0 = ch.begin; c0 < ch.end; c0 += kReduceChunk) {
+      const int c1 = min(ch.end, c0 + kReduceChunk);
+      float acc[kPer];
 #pragma unroll
-    for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
-    int k = 0;
-    for (; k + 8 <= sg.nsplit; k += 8) {
-      float v[8][kPer];
+      for (int e = 0; e < kPer; ++e) acc[e] = 0.f;
+      int k = 0;
+      for (; k + 8 <= sg.nsplit; k += 8) {
+        float v[8][kPer];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float* src = sg.src + (size_t)(k + u) * sg.stride;
+        for (int u = 0; u < 8; ++u) {
+          const float* src = sg.src + (size_t)(k + u) * sg.stride;
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) {
+            const int i = c0 + threadIdx.x + e * 256;
+            v[u][e] = (i < c1) ? __ldg(src + i) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) acc[e] += v[u][e];
+      }
+      for (; k < sg.nsplit; ++k) {
+        const float* src = sg.src + (size_t)k * sg.stride;
 #pragma unroll
         for (int e = 0; e < kPer; ++e) {
-          const int i = ch.begin + threadIdx.x + e * 256;
-          v[u][e] = (i < ch.end) ? __ldg(src + i) : 0.f;
+          const int i = c0 + threadIdx.x + e * 256;
+          if (i < c1) acc[e] += __ldg(src + i);
         }
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-#pragma unroll
-        for (int e = 0; e < kPer; ++e) acc[e] += v[u][e];
-    }
-    for (; k < sg.nsplit; ++k) {
-      const float* src = sg.src + (size_t)k * sg.stride;
-#pragma unroll
       for (int e = 0; e < kPer; ++e) {
-        const int i = ch.begin + threadIdx.x + e * 256;
-        if (i < ch.end) acc[e] += __ldg(src + i);
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-      const int i = ch.begin + threadIdx.x + e * 256;
-      if (i < ch.end) {
-        grads[sg.dst + i] = acc[e];
-        sq += (double)acc[e] * (double)acc[e];
+        const int i = c0 + threadIdx.x + e * 256;
+        if (i < c1) {
+          grads[sg.dst + i] = acc[e];
+          sq += (double)acc[e] * (double)acc[e];
+        }
       }
     }
   }

@@ -163,8 +163,13 @@ constexpr int kReduceChunk = 1024;
 // per thread is nsplit / 8 long instead of nsplit).
 constexpr int kTallSplits = 64;
 constexpr int kTallChunk = 32;
+// Wide segments with few partials take several kReduceChunk pieces per block (up to 8, about
+// 16 partial rows of a piece per block), so a block moves enough bytes to pay for its start
+// and its norm reduction.
 __host__ __device__ inline int reduce_chunk_len(int len, int nsplit) {
-  return (len >= 256 && nsplit >= kTallSplits) ? kTallChunk : kReduceChunk;
+  if (len >= 256 && nsplit >= kTallSplits) return kTallChunk;
+  const int reps = nsplit >= 16 ? 1 : (16 / (nsplit < 1 ? 1 : nsplit) > 8 ? 8 : 16 / nsplit);
+  return kReduceChunk * reps;
 }
 // Builds the chunk table of a segment list (host side).
 void build_reduce_chunks(const Segment* segs, int num_segments, ReduceChunk* out, int* count);

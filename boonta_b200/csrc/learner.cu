@@ -484,6 +484,16 @@ int allocate_tensor_core(bt_learner* L) {
       }
     }
   }
+  // LayerNorm + ReLU tensor-core layers whose every consumer of y takes relu'(y) from hb
+  for (int t = 0; t < L->ntowers; ++t) {
+    std::vector<LayerPlan>& layers = L->towers[t].layers;
+    for (size_t i = 0; i < layers.size(); ++i) {
+      LayerPlan& lp = layers[i];
+      const bool last = i + 1 == layers.size();
+      lp.relu_from_hb = lp.tc && lp.ln && lp.act == BT_ACT_RELU &&
+                        (last ? (L->tc_heads && t == 0) : layers[i + 1].tc);
+    }
+  }
   if (L->tc_heads) {
     // maps of the three head GEMMs (heads_tc.cuh); every operand is a split bf16 pair
     const LayerPlan& last = L->towers[0].layers.back();
@@ -535,8 +545,10 @@ int gather_obs(bt_learner* L, const float* obs, const int* idx, int rows, const 
   return BT_OK;
 }
 
+// keep_pre = false (the update's minibatch forward): layers whose y is read only through
+// relu'(y) (relu_from_hb) skip writing it.
 int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
-                  const int* count, cudaStream_t s) {
+                  const int* count, cudaStream_t s, bool keep_pre) {
   const float* in = obs;
   const int* gather = idx;
   int in_ld = tp.in_dim;
@@ -570,7 +582,8 @@ int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx
       }
       if (lp.ln) {
         BT_K(L, kProfLnFwd, s, launch_ln_forward(lp.z, L->params + lp.ln_off, rows, lp.kout, lp.act,
-                                                 lp.y, nullptr, out_b ? lp.hb : nullptr,
+                                                 (keep_pre || !lp.relu_from_hb) ? lp.y : nullptr,
+                                                 nullptr, out_b ? lp.hb : nullptr,
                                                  out_b ? lp.hb_lo : nullptr, lp.ldh, lp.mean,
                                                  lp.rstd, count, s));
       }
@@ -638,7 +651,8 @@ int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* id
         umma::GemmShape shx{rows, lp.kin, lp.kout, ceil_div(lp.kout, umma::BK), count, nullptr,
                             L->err_d};
         umma::EpiDx epx;
-        epx.in_map = prev.map_pre;
+        epx.in_map = prev.relu_from_hb ? prev.map_hb : prev.map_pre;
+        epx.in_bf16 = prev.relu_from_hb;
         epx.f32_map = prev.map_dpre;
         epx.hi_map = prev.map_dzb;
         epx.lo_map = prev.map_dzb_lo;
@@ -689,9 +703,9 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
   const cudaStream_t sc = side_stream(L, 0, s);
   if (L->ntowers > 1) {
     BT_TRY(stream_dep(L, s, sc));
-    BT_TRY(forward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, sc));
+    BT_TRY(forward_tower(L, L->towers[1], in.obs, in.idx, rows, in.count, sc, false));
   }
-  BT_TRY(forward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s));
+  BT_TRY(forward_tower(L, L->towers[0], in.obs, in.idx, rows, in.count, s, false));
   if (L->ntowers > 1) BT_TRY(stream_dep(L, sc, s));
   TowerPlan& t0 = L->towers[0];
   TowerPlan& tv = L->towers[L->ntowers - 1];
@@ -730,7 +744,8 @@ int loss_grads(bt_learner* L, const MinibatchInputs& in, double* stat_slot, bool
                                                 L->head_pi_splits, in.count, ed, L->err_d, sh));
     umma::GemmShape shx{rows, L->F_pi, umma::kHeadCols, 1, in.count, nullptr, L->err_d};
     umma::EpiDx epx;
-    epx.in_map = last_pi.map_pre;
+    epx.in_map = last_pi.relu_from_hb ? last_pi.map_hb : last_pi.map_pre;
+    epx.in_bf16 = last_pi.relu_from_hb;
     epx.f32_map = last_pi.map_dpre;
     epx.hi_map = last_pi.map_dzb;
     epx.lo_map = last_pi.map_dzb_lo;

@@ -84,6 +84,10 @@ struct LayerPlan {
   __nv_bfloat16 *dhpb = nullptr, *dhpb_lo = nullptr;  // [rows, 3H]
   bt::umma::Operands proj_ops{}, wi_ops{}, wh_ops{}, gdx_ops{};
   CUtensorMap map_xp;
+  // LayerNorm + ReLU tensor-core layer whose consumers take relu'(y) from the bf16 output hb
+  // (the next layer's dX epilogue, or the tensor-core heads): the update's minibatch forward
+  // does not write y
+  bool relu_from_hb = false;
   const float* pre() const { return ln ? y : z; }
 };
 
@@ -260,7 +264,7 @@ namespace bt {
 // Make `to` wait for all work enqueued so far on `from`.
 int stream_dep(bt_learner* L, cudaStream_t from, cudaStream_t to);
 int forward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
-                  const int* count, cudaStream_t s);
+                  const int* count, cudaStream_t s, bool keep_pre = true);
 int backward_tower(bt_learner* L, TowerPlan& tp, const float* obs, const int* idx, int rows,
                    const int* count, cudaStream_t s, int top, cudaStream_t s_dw = nullptr);
 int optimizer_step(bt_learner* L, int step, cudaStream_t s);
