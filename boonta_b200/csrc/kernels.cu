@@ -893,28 +893,37 @@ int launch_skinny_dw(const float* f, int F, int act, const float* d, int n, int 
 // ---- bf16 operand buffers of the tensor-core path ------------------------------------------
 // Minibatch gather of observation rows into a bf16 [rows, ld] operand: columns [0, d) the
 // observation, column d = 1 (the bias column of the dW GEMM), (d, ld) zero. One warp per
-// row (coalesced along the row).
+// row (coalesced along the row). With `table` set, each gathered bf16 row is also stored at
+// its own index in the table [*, ld] (the update's bf16 copy of the rollout, filled by the
+// first epoch's minibatches, which together read every row once).
 __global__ void gather_bf16_kernel(const float* obs, const int* idx, int rows, int d, int ld,
-                                   __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count) {
+                                   __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
+                                   __nv_bfloat16* table) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   pdl_trigger();
   pdl_wait();
   if (row >= live_rows(count, rows)) return;
-  const float* src = obs + (size_t)(idx ? idx[row] : row) * d;
+  const int r = idx ? idx[row] : row;
+  const float* src = obs + (size_t)r * d;
+  __nv_bfloat16* trow = table ? table + (size_t)r * ld : nullptr;
   int k0 = 0;
   if ((d & 3) == 0 && (ld & 3) == 0) {
     // float4 loads and 8-byte bf16 stores, four chunks in flight per lane
     const int q4 = d / 4;
     const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll 4
-    for (int q = lane; q < q4; q += 32)
-      store_bf16x4(out, out_lo, (size_t)row * ld + 4 * q, __ldg(s4 + q));
+    for (int q = lane; q < q4; q += 32) {
+      const float4 v = __ldg(s4 + q);
+      store_bf16x4(out, out_lo, (size_t)row * ld + 4 * q, v);
+      if (trow) store_bf16x4(trow, nullptr, 4 * q, v);
+    }
     k0 = d;
   }
   for (int k = k0 + lane; k < ld; k += 32) {
     const float v = k < d ? src[k] : (k == d ? 1.f : 0.f);
     store_bf16(out, out_lo, (size_t)row * ld + k, v);
+    if (trow) store_bf16(trow, nullptr, k, v);
   }
 }
 
@@ -976,10 +985,10 @@ int launch_gather_rows_bf16(const __nv_bfloat16* src, const int* idx, int rows, 
 
 int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
                        __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, __nv_bfloat16* table) {
   if (rows <= 0) return BT_OK;
   BT_CUDA(launch_pdl(gather_bf16_kernel, dim3(ceil_div(rows * 32, 256)), dim3(256), 0, stream,
-                     obs, idx, rows, d, ld, out, out_lo, count));
+                     obs, idx, rows, d, ld, out, out_lo, count, table));
   return BT_OK;
 }
 

@@ -132,7 +132,7 @@ int launch_gather_rows_bf16(const __nv_bfloat16* src, const int* idx, int rows, 
                             __nv_bfloat16* out, const int* count, cudaStream_t stream);
 int launch_gather_bf16(const float* obs, const int* idx, int rows, int d, int ld,
                        __nv_bfloat16* out, __nv_bfloat16* out_lo, const int* count,
-                       cudaStream_t stream);
+                       cudaStream_t stream, __nv_bfloat16* table = nullptr);
 // fp32 [rows, d] -> split bf16 pairs [rows, d]; rows from the live count to the next 64-row
 // boundary written as zeros.
 int launch_split_rows_bf16(const float* src, int rows, int d, __nv_bfloat16* out,

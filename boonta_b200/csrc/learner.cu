@@ -536,7 +536,15 @@ int gather_obs(bt_learner* L, const float* obs, const int* idx, int rows, const 
                cudaStream_t s) {
   if (!L->tc_first) return BT_OK;
   if (L->gather_rows && idx) {
-    // an update minibatch: its rows from the update's bf16 copy of the rollout
+    if (L->fill_obs_b) {
+      // a first-epoch minibatch: its fp32 rows to the GEMM operand, and (when later epochs
+      // follow) into the update's bf16 copy of the rollout at their own indices
+      BT_K(L, kProfMisc, s, launch_gather_bf16(obs, idx, rows, L->cfg.network.obs_dim, L->ldx0,
+                                               L->xg, nullptr, count, s,
+                                               L->cfg.ppo.update_epochs > 1 ? L->obs_b : nullptr));
+      return BT_OK;
+    }
+    // a later epoch: its rows from the update's bf16 copy of the rollout
     BT_K(L, kProfMisc, s, launch_gather_rows_bf16(L->obs_b, idx, rows, L->ldx0, L->xg, count, s));
     return BT_OK;
   }
@@ -1072,13 +1080,8 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
   const int E = L->cfg.ppo.update_epochs, M = L->cfg.ppo.num_minibatches;
   const int64_t Bg = L->B * world;
   BT_TRY(bootstrap_and_gae(L, batch, s));
-  if (L->obs_b) {
-    // the rollout's observations as bf16 rows (with the ones column) once per update: each
-    // epoch reads every row once, so the minibatches then move half the bytes
-    BT_K(L, kProfMisc, s, launch_gather_bf16(batch->obs, nullptr, (int)L->B,
-                                             L->cfg.network.obs_dim, L->ldx0, L->obs_b, nullptr,
-                                             nullptr, s));
-  }
+  // (with a bf16 copy of the rollout, the first epoch's minibatch gathers fill it: an epoch
+  // reads every row once, so the later epochs' gathers move half the bytes)
   if (world > 1) {
     BT_K(L, kProfMisc, s, launch_local_indices(perm, E * M, L->mb, 0, L->N, L->cfg.rank, L->N * world,
                                 L->rows_cap, L->local_idx, L->local_counts, L->err_d, s));
@@ -1102,6 +1105,7 @@ int update_body(bt_learner* L, const bt_batch* batch, const int32_t* perm, float
         in.count = nullptr;
       }
       L->gather_rows = L->obs_b != nullptr;
+      L->fill_obs_b = e == 0;
       const int rc = loss_grads(L, in, L->stat_sums + (size_t)i * kNumStatSums, world == 1, s);
       L->gather_rows = false;
       BT_TRY(rc);

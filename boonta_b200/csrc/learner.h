@@ -146,6 +146,7 @@ struct bt_learner {
   // minibatch gathers its rows from it (gather_rows, set per minibatch)
   __nv_bfloat16* obs_b = nullptr;
   bool gather_rows = false;
+  bool fill_obs_b = false;  // first epoch: gather from the fp32 rollout and fill obs_b
   __nv_bfloat16* xg_lo = nullptr;
   int ldx0 = 0;
   // network
