@@ -14,12 +14,14 @@
 //      the G partial sums and adds them in rank order (the same global norm everywhere);
 //   4. runs clip + Adam on its slice only (1/G of the optimizer's memory traffic), storing each
 //      new parameter and its bf16 shadow into its own buffers and into every peer's (NVLink
-//      stores, fenced system-wide by each thread);
+//      stores, fenced system-wide by each thread); the tensor-core layers' weight matrices,
+//      which the peers read only through the shadow during the update, go as the shadow alone;
 //   5. barrier: every slice is updated everywhere.
 // The gradient crosses NVLink once inbound per rank ((G-1)/G of it) and the parameters once
 // outbound ((G-1)/G), the volume of one all-reduce, with the optimizer step on 1/G of the
 // parameters in between. Adam's moments stay sharded during the update (each rank owns its slice's mu / nu)
-// and are gathered the same way once the update ends, so every rank holds the full state
+// and are gathered the same way once the update ends (with those weights' fp32 values), so every
+// rank holds the full state
 // between updates. The mailboxes and the peers' buffers are CUDA IPC mappings set up when the
 // communicator is created (bt_learner_comm_init).
 //
@@ -222,6 +224,23 @@ int exchange_optimizer_step(bt_learner* L, int step, cudaStream_t s) {
   ap.eps_root = o.eps_root;
   ap.shadow = L->params_b ? L->params_b + lo : nullptr;
   ap.shadow_lo = L->params_b_lo ? L->params_b_lo + lo : nullptr;
+  // the tensor-core layers' weight matrices are read through the bf16 shadow alone while the
+  // update runs: their fp32 values are not pushed (exchange_gather_moments copies them at the
+  // update's end)
+  if (L->params_b) {
+    for (int t = 0; t < L->ntowers; ++t) {
+      for (const LayerPlan& lp : L->towers[t].layers) {
+        if (!lp.tc || lp.kind != BT_LAYER_DENSE || ap.nskip == 8) continue;
+        const int64_t a = std::max<int64_t>(lp.w_off, lo);
+        const int64_t b = std::min<int64_t>(lp.w_off + (int64_t)lp.kin * lp.kout, hi);
+        if (a < b) {
+          ap.skip_lo[ap.nskip] = a - lo;
+          ap.skip_hi[ap.nskip] = b - lo;
+          ++ap.nskip;
+        }
+      }
+    }
+  }
   for (int p = 0; p < x->world; ++p) {
     if (p == x->rank) continue;
     ap.push_params[ap.npush] = x->params.buf[p] + lo;
@@ -235,12 +254,14 @@ int exchange_optimizer_step(bt_learner* L, int step, cudaStream_t s) {
 }
 
 // After the update's last minibatch: every rank gathers the other ranks' slices of Adam's
-// moments, so the full optimizer state is replicated between updates.
+// moments and of the fp32 parameters (the weights pushed only as their bf16 shadow), so the full
+// state is replicated between updates.
 int exchange_gather_moments(bt_learner* L, cudaStream_t s) {
   Exchange* x = L->xchg;
   BT_K(L, kProfAllreduce, s, launch_barrier(x, nullptr, 0, L->err_d, s));
   BT_K(L, kProfAllreduce, s, launch_gather(x, x->mu, L->mu, nullptr, nullptr, s));
   BT_K(L, kProfAllreduce, s, launch_gather(x, x->nu, L->nu, nullptr, nullptr, s));
+  BT_K(L, kProfAllreduce, s, launch_gather(x, x->params, L->params, nullptr, nullptr, s));
   // no rank's moments change again before every rank has finished copying them
   BT_K(L, kProfAllreduce, s, launch_barrier(x, nullptr, 0, L->err_d, s));
   return BT_OK;

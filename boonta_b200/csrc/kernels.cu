@@ -554,9 +554,14 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
     reinterpret_cast<float4*>(p.mu)[q] = m;
     reinterpret_cast<float4*>(p.nu)[q] = v;
     if (p.shadow) store_bf16x4(p.shadow, p.shadow_lo, 4 * q, prm);
-    for (int r = 0; r < p.npush; ++r) {
-      reinterpret_cast<float4*>(p.push_params[r])[q] = prm;
-      if (p.push_shadow[r]) store_bf16x4(p.push_shadow[r], p.push_shadow_lo[r], 4 * q, prm);
+    if (p.npush) {
+      bool fp32 = true;
+      for (int k = 0; k < p.nskip; ++k)
+        if (4 * q >= p.skip_lo[k] && 4 * q < p.skip_hi[k]) fp32 = false;
+      for (int r = 0; r < p.npush; ++r) {
+        if (fp32) reinterpret_cast<float4*>(p.push_params[r])[q] = prm;
+        if (p.push_shadow[r]) store_bf16x4(p.push_shadow[r], p.push_shadow_lo[r], 4 * q, prm);
+      }
     }
   };
   int64_t q = first;
@@ -585,8 +590,11 @@ __global__ void __launch_bounds__(256) adam_kernel(AdamParams p) {
     p.mu[i] = m;
     p.nu[i] = v;
     if (p.shadow) store_bf16(p.shadow, p.shadow_lo, i, prm);
+    bool fp32 = true;
+    for (int k = 0; k < p.nskip; ++k)
+      if (i >= p.skip_lo[k] && i < p.skip_hi[k]) fp32 = false;
     for (int r = 0; r < p.npush; ++r) {
-      p.push_params[r][i] = prm;
+      if (fp32) p.push_params[r][i] = prm;
       if (p.push_shadow[r]) store_bf16(p.push_shadow[r], p.push_shadow_lo[r], i, prm);
     }
   }

@@ -202,6 +202,11 @@ struct AdamParams {
   float* push_params[7];
   __nv_bfloat16* push_shadow[7];
   __nv_bfloat16* push_shadow_lo[7];
+  // Element ranges [skip_lo, skip_hi) (relative to params, multiples of 4) whose fp32 values
+  // are not pushed (only their bf16 shadow): parameters the peers read through the shadow alone
+  // while an update runs.
+  int nskip;
+  int64_t skip_lo[8], skip_hi[8];
 };
 int launch_adam(const AdamParams& p, cudaStream_t stream);
 
