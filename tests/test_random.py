@@ -66,3 +66,22 @@ def test_uniform_bit_trick_stays_in_range():
     u = orand.uniform(orand.key(7), 100_000, np.finfo(np.float32).tiny, 1.0)
     assert u.min() >= np.finfo(np.float32).tiny and u.max() < 1.0
     assert abs(float(u.mean()) - 0.5) < 0.01
+
+
+def test_python_keys_and_host_split():
+    import torch
+
+    from boonta_b200 import random as trandom
+
+    np.testing.assert_array_equal(trandom.key(0), [0, 0])
+    np.testing.assert_array_equal(trandom.key(2 ** 32 + 5), [1, 5])
+    np.testing.assert_array_equal(trandom.as_key(7), trandom.key(7))
+    np.testing.assert_array_equal(trandom.as_key(torch.tensor([7])), trandom.key(7))
+    np.testing.assert_array_equal(trandom.as_key([3, 4]), np.array([3, 4], np.uint32))
+    with pytest.raises(ValueError):
+        trandom.as_key([1, 2, 3])
+    with pytest.raises(ValueError):
+        trandom.key(-1)
+    # split on the host through the library, both layouts, against the oracle
+    for part in (True, False):
+        np.testing.assert_array_equal(trandom.split(7, 5, part), orand.split(orand.key(7), 5, part))
