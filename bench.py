@@ -9,7 +9,9 @@ forward/loss/backward/(all-reduce)/clip+Adam. Inputs are seeded synthetic rollou
 workload's shapes, resident in HBM when the timed region starts (`value`); `e2e` repeats
 the measurement through the public API with the rollout copied from pinned host memory
 and the statistics read back every step. Every timed rollout and its permutations are
-larger than L2 (126 MB), and each step uses a different permutation.
+larger than L2 (126 MB), and each step uses a different permutation. The line also carries
+`act`: the act step (PPO.step) through Learner.act over one rollout step's N envs, device-timed
+(not part of `value`).
 
 `--impl reference` times the reference's algorithm on the host cores. boonta's own JAX
 path cannot run here (no jax/flax/optax in the image), so it times the NumPy port of it
